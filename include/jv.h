@@ -1,0 +1,171 @@
+/*
+ * jv.h — C ABI of the B200 Jevstral forward pass.
+ *
+ * The .NET host keeps its public API (JevstralDecider, VerdictScorer, SystemPromptCache,
+ * the `jev` CLI) and replaces the body of MinistralModel and KvCache with P/Invoke calls
+ * into this library. Every entry point below names the reference member it replaces
+ * (paths inside theolivenbaum/llm-shield). Signatures hold plain pointers and sizes only.
+ *
+ * Threading: a jv_model (weights on one GPU) may be shared by several jv_ctx; a jv_ctx
+ * (one KV cache, one CUDA stream, activation buffers) is single-threaded, like a
+ * MinistralModel instance (src/Jevstral/Model/MinistralModel.cs:21-22).
+ *
+ * Errors: every int-returning call returns a JV_* status. jv_last_error() gives the
+ * calling thread's last message. The C# binding maps codes back to the exception types
+ * the reference throws (src/Jevstral/Model/MinistralModel.cs:202,207,306;
+ * src/Jevstral/Numerics/QuantMatMul.cs:300-302; src/Jevstral/Model/KvCache.cs:96-97,118-120;
+ * src/Jevstral/Gguf/GgufFile.cs:156-172).
+ */
+#ifndef JV_H
+#define JV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum jv_status {
+    JV_OK = 0,
+    JV_ERR_ARG = 1,            /* ArgumentException / ArgumentNullException          */
+    JV_ERR_RANGE = 2,          /* ArgumentOutOfRangeException                        */
+    JV_ERR_FORMAT = 3,         /* InvalidDataException / KeyNotFoundException         */
+    JV_ERR_IO = 4,             /* IOException / FileNotFoundException                 */
+    JV_ERR_UNSUPPORTED = 5,    /* NotSupportedException                              */
+    JV_ERR_CANCELLED = 6,      /* OperationCanceledException                         */
+    JV_ERR_DEVICE = 7,         /* a CUDA call failed                                 */
+    JV_ERR_DEVICE_TIMEOUT = 8, /* a bounded device-side wait gave up                 */
+    JV_ERR_OOM = 9             /* device memory exhausted                            */
+};
+
+typedef struct jv_model jv_model;       /* weights resident on one device            */
+typedef struct jv_ctx jv_ctx;           /* MinistralModel instance: KV cache + stream */
+typedef struct jv_snapshot jv_snapshot; /* refcounted KV pages of a prefix            */
+
+/* ModelConfig (src/Jevstral/Model/ModelConfig.cs:11-56), plus the resolved RoPE magnitude
+ * scale (Rope.MagnitudeScale, src/Jevstral/Model/Rope.cs:28) and the weight type. */
+typedef struct jv_config {
+    int32_t layers, hidden, heads, kv_heads, head_dim, ff, vocab, rope_dim;
+    int32_t context_length, rope_orig_ctx, yarn_active, weight_type;
+    float eps, rope_base, rope_scale, rope_mscale, temperature_scale;
+} jv_config;
+
+/* TokenLayout (src/Jevstral/Model/MinistralModel.cs:703-718): token t is written to KV slot
+ * slot[t], rotated as position[t], and sees slots [0, shared[t]) and [segment[t], slot[t]].
+ * outputs[] are the token indices whose logits are returned; end is one past the highest
+ * slot written; sparse is carried for fidelity (it only picks a CPU loop in the reference). */
+typedef struct jv_layout {
+    const int32_t* slot;
+    const int32_t* position;
+    const int32_t* shared;
+    const int32_t* segment;
+    const int32_t* outputs;
+    int32_t n_outputs;
+    int32_t end;
+    int32_t sparse;
+} jv_layout;
+
+/* IActivationSink.Observe (src/Jevstral/Model/MinistralModel.cs:787-790). Called
+ * synchronously with host fp32 data named as the reference names them: "embeddings",
+ * "blk.{l}.attn_norm|q_rope|k_rope|v|attn_weighted|attn_out|post_attn|ffn_norm|ffn_out|output",
+ * "final_norm", "logits". */
+typedef void (*jv_activation_sink)(void* user, const char* name, const float* values, int32_t rows,
+                                   int32_t cols);
+
+/* ---- library / device -------------------------------------------------------------- */
+
+const char* jv_last_error(void);
+int jv_device_count(int32_t* count);
+/* Counts this library's kernel launches on the calling process (all contexts). */
+int64_t jv_kernel_launches(void);
+
+/* ---- model (weights) ----------------------------------------------------------------- */
+
+/* new MinistralModel(ggufPath) weight binding (MinistralModel.cs:56-123), GgufFile parsing
+ * (src/Jevstral/Gguf/GgufFile.cs:76-172) and ModelConfig.FromGguf (ModelConfig.cs:62-112).
+ * Copies the quantized blocks of every matrix to `device` once, re-tiled but bit-identical.
+ * kv_pool_mb sizes the device KV page pool (0 = default). */
+int jv_model_open(const char* gguf_path, int32_t device, int32_t kv_pool_mb, jv_model** out);
+void jv_model_close(jv_model* model);
+/* MinistralModel.Config (MinistralModel.cs:48). */
+int jv_model_config(const jv_model* model, jv_config* out);
+
+/* ---- context (MinistralModel instance state) ---------------------------------------- */
+
+/* The KvCache + logits buffer a MinistralModel owns (MinistralModel.cs:100-101). */
+int jv_ctx_create(jv_model* model, int32_t initial_capacity, jv_ctx** out);
+void jv_ctx_destroy(jv_ctx* ctx);
+/* Activation capture (the IActivationSink argument of ForwardAsync, MinistralModel.cs:155). */
+int jv_ctx_set_sink(jv_ctx* ctx, jv_activation_sink sink, void* user);
+/* ParallelOptions.CancellationToken: when *flag becomes non-zero the forward stops between
+ * layers and returns JV_ERR_CANCELLED (KernelTests.cs:206-218). NULL clears it. */
+int jv_ctx_set_cancel(jv_ctx* ctx, const volatile int32_t* flag);
+/* The cudaStream_t every kernel of this context runs on (for event timing). */
+void* jv_ctx_stream(jv_ctx* ctx);
+
+/* ---- forward passes ------------------------------------------------------------------- */
+
+/* MinistralModel.ForwardAsync(tokens, options) (MinistralModel.cs:139) — appends tokens and
+ * writes the full-vocabulary logits of the last position to logits[vocab]. With logits ==
+ * NULL this is PrefillAsync (MinistralModel.cs:148): KV only, no LM head. */
+int jv_forward(jv_ctx* ctx, const int32_t* tokens, int32_t n, float* logits);
+
+/* MinistralModel.ForwardSelectedAsync (MinistralModel.cs:165-172): appends tokens; out[n_rows]
+ * = logits of vocab rows `rows` at the last position. */
+int jv_forward_selected(jv_ctx* ctx, const int32_t* tokens, int32_t n, const int32_t* rows,
+                        int32_t n_rows, float* out);
+
+/* MinistralModel.ForwardTreeAsync (MinistralModel.cs:198-219); ForwardBranchesAsync
+ * (MinistralModel.cs:187) when n_trunk == 0. branch_tokens holds the branches back to back
+ * (branch_lengths[b] tokens each). out[n_branches][n_rows] = logits of `rows` at each
+ * branch's last token. The branch tokens stay in the KV cache, as in the reference. */
+int jv_forward_tree(jv_ctx* ctx, const int32_t* trunk, int32_t n_trunk, const int32_t* branch_tokens,
+                    const int32_t* branch_lengths, int32_t n_branches, const int32_t* rows,
+                    int32_t n_rows, float* out);
+
+/* The private ForwardAsync(tokens, capture, options, computeLogits, layout, selectedRows,
+ * selectedOut) every public overload funnels into (MinistralModel.cs:301-435).
+ * layout == NULL means a causal append at the cache end. With rows != NULL, out receives
+ * [n_outputs][n_rows] selected logits; with rows == NULL and full_vocab != 0, out receives
+ * [n_outputs][vocab] (ForwardTreeLogitsAsync / ForwardRowsAsync, MinistralModel.cs:227-294);
+ * with compute_logits != 0, logits receives the last position's full vocabulary. */
+int jv_forward_layout(jv_ctx* ctx, const int32_t* tokens, int32_t n, const jv_layout* layout,
+                      const int32_t* rows, int32_t n_rows, int32_t full_vocab, float* out,
+                      int32_t compute_logits, float* logits);
+
+/* The benchmark's decode loop (src/Jevstral.Cli/Benchmark.cs:411-422): `steps` single-token
+ * forwards with the full LM head, each feeding back the argmax
+ * (Kernels.ArgMax, src/Jevstral/Numerics/Kernels.cs:146) of the previous one, starting from
+ * first_token. Writes the chosen tokens to out_tokens[steps]. */
+int jv_decode_greedy(jv_ctx* ctx, int32_t first_token, int32_t steps, int32_t* out_tokens);
+
+/* ---- KV cache (src/Jevstral/Model/KvCache.cs) ----------------------------------------- */
+
+int32_t jv_kv_length(jv_ctx* ctx);                             /* KvCache.Length   :23     */
+int32_t jv_kv_capacity(jv_ctx* ctx);                           /* KvCache.Capacity :21     */
+int jv_kv_reset(jv_ctx* ctx);                                  /* KvCache.Reset    :43     */
+int jv_kv_truncate(jv_ctx* ctx, int32_t length);               /* KvCache.Truncate :46     */
+int jv_kv_ensure_capacity(jv_ctx* ctx, int32_t required);      /* EnsureCapacity   :48-70  */
+int64_t jv_kv_bytes_per_position(jv_ctx* ctx);                 /* BytesPerPosition :139    */
+/* KvCache.Snapshot (:94-112): the reference's flat fp32 layout (keys for every layer and
+ * head, then values), so SystemPromptCache files (SystemPromptCache.cs:110-164) stay valid.
+ * n_floats must equal jv_kv_snapshot_floats(length). */
+int64_t jv_kv_snapshot_floats(jv_ctx* ctx, int32_t length);
+int jv_kv_snapshot(jv_ctx* ctx, int32_t length, float* out, int64_t n_floats);
+/* KvCache.Restore (:115-136). */
+int jv_kv_restore(jv_ctx* ctx, const float* snapshot, int64_t n_floats, int32_t length);
+
+/* Zero-copy prefix reuse (the question-snapshot LRU and system-prompt cache of
+ * JevstralDecider.cs:131-137,262-280 without the memcpy): jv_kv_share pins the pages that
+ * hold the first `length` positions; jv_kv_adopt makes a context's cache exactly that prefix
+ * (copy-on-write for the one partially filled page). Contexts must share the jv_model. */
+int jv_kv_share(jv_ctx* ctx, int32_t length, jv_snapshot** out);
+int jv_kv_adopt(jv_ctx* ctx, const jv_snapshot* snapshot);
+int32_t jv_snapshot_length(const jv_snapshot* snapshot);
+void jv_snapshot_release(jv_snapshot* snapshot);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JV_H */

@@ -1,0 +1,81 @@
+"""Build the B200 Jevstral libraries in-tree.
+
+libjv.so     CUDA kernels for sm_100a + the host runtime behind include/jv.h
+             (nvcc -gencode arch=compute_100a,code=sm_100a, static CUDA runtime).
+libjvsynth.so  the random-weight GGUF filler used by the tests and the benchmark.
+
+Usage: python llm-shield_b200/build.py [--verbose] [--ptxas]
+"""
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+OUT = PKG / "_build"
+LIB = PKG / "libjv.so"
+SYNTH = PKG / "libjvsynth.so"
+
+NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+                     "-Xcompiler", "-Wall,-Wno-unused-function", "-I", str(PKG.parent / "include")]
+
+SOURCES = ["gguf.cpp", "runtime.cu", "kernels_quant.cu", "kernels_elem.cu", "kernels_attn.cu", "gemm_tc.cu"]
+
+
+def _run(cmd: list[str], verbose: bool) -> str:
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"command failed ({r.returncode}): {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    return r.stdout + r.stderr
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build(verbose: bool = False, ptxas: bool = False, force: bool = False) -> Path:
+    OUT.mkdir(exist_ok=True)
+    headers = list(CSRC.glob("*.h")) + [PKG.parent / "include" / "jv.h"]
+    jobs = []
+    objs = []
+    for src in SOURCES:
+        s = CSRC / src
+        o = OUT / (src + ".o")
+        objs.append(o)
+        if force or _stale(o, [s] + headers):
+            flags = list(NVCC_FLAGS)
+            if ptxas and src.endswith(".cu"):
+                flags += ["-Xptxas", "-v"]
+            jobs.append([NVCC] + flags + (["-x", "cu"] if src.endswith(".cu") else []) + ["-c", str(s), "-o", str(o)])
+    logs = []
+    with cf.ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
+        for out in ex.map(lambda c: _run(c, verbose), jobs):
+            logs.append(out)
+    if ptxas:
+        for log in logs:
+            print(log)
+    if force or jobs or _stale(LIB, objs):
+        _run([NVCC] + ARCH + ["-shared", "-o", str(LIB)] + [str(o) for o in objs] +
+             ["-cudart", "static", "-lpthread", "-ldl", "-lrt"], verbose)
+    synth_src = CSRC / "synth" / "gguf_synth.cpp"
+    if force or _stale(SYNTH, [synth_src]):
+        _run(["g++", "-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math", "-shared", "-o", str(SYNTH),
+              str(synth_src), "-lpthread"], verbose)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(verbose="--verbose" in sys.argv, ptxas="--ptxas" in sys.argv, force="--force" in sys.argv)
+    print(LIB)

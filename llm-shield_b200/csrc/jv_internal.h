@@ -1,0 +1,175 @@
+// jv_internal.h — shared declarations of the B200 Jevstral runtime (host C++ and CUDA).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "../../include/jv.h"
+
+namespace jv {
+
+// ------------------------------------------------------------------ errors
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define JV_CUDA(call)                                                                          \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            throw ::jv::Error(e_ == cudaErrorMemoryAllocation ? JV_ERR_OOM : JV_ERR_DEVICE,    \
+                              std::string(#call) + ": " + cudaGetErrorString(e_));            \
+    } while (0)
+
+// ------------------------------------------------------------- GGML types
+
+// ggml_type numbering (reference src/Jevstral/Gguf/GgmlType.cs:9-44).
+enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_1 = 7, T_Q8_0 = 8, T_BF16 = 30 };
+
+// Tile geometry of a quantized matrix in HBM. The GGUF blocks of 128 consecutive rows ×
+// 64 consecutive columns are gathered into one contiguous "chunk", split into planes so
+// that every plane starts 16-byte aligned. The bits are the file's bits: re-tiled, never
+// re-quantized. Chunks are stored [row tile][k step], so one k step of one row tile is a
+// single bulk copy, and a GEMV CTA streams its row tile front to back.
+//   Q8_0: qs  int8 [128][64]   | d fp16 [128][2]                                  = 8704 B
+//   Q4_0: qs  u8   [128][2][16] | d fp16 [128][2]                                 = 4608 B
+//   Q5_1: qs  u8   [128][2][16] | qh u32 [128][2] | d fp16 [128][2] | m fp16 [128][2] = 6144 B
+constexpr int TILE_ROWS = 128;
+constexpr int TILE_K = 64;
+
+__host__ __device__ constexpr int chunk_bytes(int type) {
+    return type == T_Q8_0 ? 8704 : type == T_Q4_0 ? 4608 : type == T_Q5_1 ? 6144 : 0;
+}
+__host__ __device__ constexpr int qs_bytes(int type) { return type == T_Q8_0 ? 8192 : 4096; }
+
+struct QWeight {
+    int type = 0;
+    int rows = 0, cols = 0;      // output features (N), input features (K)
+    int tiles = 0, ksteps = 0;   // rows / 128, cols / 64
+    uint8_t* data = nullptr;     // [tiles][ksteps][chunk]
+    size_t bytes() const { return (size_t)tiles * ksteps * chunk_bytes(type); }
+};
+
+// ----------------------------------------------------------- activations
+
+// GEMM operands are fp16: the K-slab layout [K/64][Tpad][64] with the 128-byte swizzle
+// already applied (16-byte chunk c of row t is stored at chunk c ^ (t & 7)). A row tile of
+// BN tokens of one K slab is then one contiguous bulk copy that lands in shared memory in
+// exactly the UMMA K-major SWIZZLE_128B layout.
+__host__ __device__ inline size_t kslab_offset(int t, int k, int tpad) {
+    int kb = k >> 6, kk = k & 63;
+    int c = (kk >> 3) ^ (t & 7);
+    return ((size_t)kb * tpad + t) * 64 + c * 8 + (kk & 7);
+}
+
+// ------------------------------------------------------------ GEMM plans
+
+enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1 };
+
+struct GemmArgs {
+    const QWeight* w;
+    const __half* x;   // K-slab fp16 activations, tpad rows
+    int T, tpad, bn;   // tokens, padded tokens (multiple of bn), token tile
+    float* y;          // [T][ldy]
+    int ldy;
+    int epilogue;
+    int* err;          // device error word (JV_ERR_DEVICE_TIMEOUT on a bounded-wait timeout)
+};
+
+// Token tile for a GEMM over T tokens: balanced tiles of at most 256 (the MMA's N limit),
+// multiples of 16. Depends on T only, never on which tokens they are; the K order of the
+// MMA chain does not depend on it, so a token's result is independent of its batch.
+int gemm_bn_for(int T);
+int gemm_tpad_for(int T);
+
+// ------------------------------------------------------------ kernel API
+
+void launch_repack(const uint8_t* raw, int type, int rows, int cols, int64_t raw_row_bytes, uint8_t* dst,
+                   int dst_tiles, int ksteps, int row_in_tile_base, int tile_offset, int interleave,
+                   cudaStream_t s);
+void launch_embed(const QWeight& table, const int32_t* ids, int T, float* h, int hidden, int* err, cudaStream_t s);
+void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __half* xs, int tpad, float* out32,
+                    cudaStream_t s);
+void launch_rmsnorm_rows(const float* h, const int32_t* rows, int n_rows, const float* w, int n, float eps,
+                         float* out32, __half* xs, int tpad, cudaStream_t s);
+void launch_gemm(const GemmArgs& a, cudaStream_t s);
+void launch_gemm_reference(const GemmArgs& a, cudaStream_t s);
+void launch_gemv(const QWeight& w, const float* x, float* partial, int splits, cudaStream_t s);
+void launch_gemv_reduce(const float* partial, int splits, int n, float* y, int epilogue, cudaStream_t s);
+int gemv_splits_for(const QWeight& w, int sm_count);
+
+struct RopeArgs {
+    const float* qkv;       // [T][qdim + 2 kvdim]
+    const int32_t* pos;     // [T]
+    const int32_t* slot;    // [T]
+    const float2* table;    // [max_pos][half] (cos*mscale, sin*mscale)
+    int T, heads, kv_heads, head_dim, layer;
+    float temperature_scale;
+    int orig_ctx;
+    __half* q16;            // [T][qdim] (prefill) or null
+    float* q32;             // [T][qdim] (decode / capture) or null
+    __half* kv_pool;        // page pool
+    const int32_t* page_table;
+    int64_t page_bytes;     // bytes per page
+    int page_slots;         // slots per page
+    float* k32;             // optional capture of rotated keys [T][kvdim]
+};
+void launch_rope_kv(const RopeArgs& a, cudaStream_t s);
+void launch_rope_table(float2* table, const float* freqs, int half, int pos0, int npos, float mscale, cudaStream_t s);
+
+struct AttnItem {  // one query tile: up to 16 consecutive tokens of one segment, one KV head
+    int32_t t0, ntok, kv_head, slot0, shared, segment, nblocks, pad;
+};
+struct AttnArgs {
+    const __half* q16;          // [T][heads*hd]
+    const AttnItem* items;
+    int n_items;
+    const __half* kv_pool;
+    const int32_t* page_table;
+    int64_t page_bytes;
+    int page_slots;
+    int layer, heads, kv_heads;
+    float scale;
+    __half* ctx16;              // K-slab [qdim/64][tpad][64]
+    int tpad;
+    float* ctx32;               // optional [T][qdim]
+};
+void launch_attention(const AttnArgs& a, cudaStream_t s);
+
+struct DecodeAttnArgs {
+    const float* q32;           // [heads*hd]
+    const __half* kv_pool;
+    const int32_t* page_table;
+    int64_t page_bytes;
+    int page_slots;
+    int layer, heads, kv_heads, n_keys;  // n_keys = visible logical keys
+    int shared, segment;                 // logical key L < shared is slot L, else segment + L - shared
+    float scale;
+    float* partial;             // workspace
+    int splits;
+    float* ctx32;               // [heads*hd]
+};
+void launch_decode_attention(const DecodeAttnArgs& a, cudaStream_t s);
+
+void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, cudaStream_t s);
+void launch_add(float* h, const float* x, int64_t n, cudaStream_t s);
+void launch_head_rows(const QWeight& table, const float* normed, int n_out, const int32_t* rows, int n_rows,
+                      float* out, int* err, cudaStream_t s);
+void launch_argmax(const float* x, int n, int32_t* out, cudaStream_t s);
+void launch_kslab_to_f32(const __half* xs, int T, int K, int tpad, float* out, cudaStream_t s);
+// KV pages <-> the reference's flat fp32 snapshot layout (keys of every layer/head, then values).
+void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
+                      int kv_heads, int len, float* out, cudaStream_t s);
+void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
+                      int kv_heads, int len, const float* in, cudaStream_t s);
+int64_t launches_total();
+
+void note_launch(int n = 1);
+
+}  // namespace jv

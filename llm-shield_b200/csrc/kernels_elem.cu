@@ -1,0 +1,262 @@
+// kernels_elem.cu — the fused elementwise kernels: RMSNorm (writing the fp16 GEMM operand
+// straight into the K-slab layout), the RoPE table, RoPE + temperature + KV page write,
+// SwiGLU, residual add.
+#include "jv_internal.h"
+
+namespace jv {
+
+// --------------------------------------------------------------- RMSNorm
+
+// Kernels.RmsNorm (reference src/Jevstral/Numerics/Kernels.cs:25-60):
+//   scale = 1 / sqrt((float)(sum(x^2) / n) + eps);  y = (x * scale) * w
+// The sum of squares is accumulated in double (the reference widens its two float
+// accumulators to double) over a fixed thread/lane assignment and a fixed tree, so it is
+// deterministic. Output goes to the fp16 K-slab operand (xs, prefill) and/or fp32 (out32,
+// decode path and capture).
+constexpr int NORM_THREADS = 256;
+
+__device__ __forceinline__ double block_sum_double(double v, double* red) {
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    double s = 0;
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w];
+        red[32] = s;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+__device__ __forceinline__ void rmsnorm_row(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
+                                            int t, __half* __restrict__ xs, int tpad, float* __restrict__ out32) {
+    __shared__ double red[33];
+    double s = 0;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        float v = x[k];
+        s += (double)v * (double)v;
+    }
+    s = block_sum_double(s, red);
+    float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / n), eps)));
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        float y = __fmul_rn(__fmul_rn(x[k], scale), w[k]);
+        if (xs) xs[kslab_offset(t, k, tpad)] = __float2half_rn(y);
+        if (out32) out32[k] = y;
+    }
+}
+
+__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm(const float* __restrict__ h, const float* __restrict__ w,
+                                                           int n, float eps, __half* __restrict__ xs, int tpad,
+                                                           float* __restrict__ out32) {
+    int t = blockIdx.x;
+    rmsnorm_row(h + (int64_t)t * n, w, n, eps, t, xs, tpad, out32 ? out32 + (int64_t)t * n : nullptr);
+}
+
+void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __half* xs, int tpad, float* out32,
+                    cudaStream_t s) {
+    k_rmsnorm<<<T, NORM_THREADS, 0, s>>>(h, w, n, eps, xs, tpad, out32);
+    note_launch();
+}
+
+// RMSNorm of selected rows (the output rows of a tree/rows pass, MinistralModel.cs:371-373,396).
+__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_rows(const float* __restrict__ h, const int32_t* __restrict__ rows,
+                                                                const float* __restrict__ w, int n, float eps,
+                                                                float* __restrict__ out32, __half* __restrict__ xs, int tpad) {
+    int b = blockIdx.x;
+    rmsnorm_row(h + (int64_t)rows[b] * n, w, n, eps, b, xs, tpad, out32 ? out32 + (int64_t)b * n : nullptr);
+}
+
+void launch_rmsnorm_rows(const float* h, const int32_t* rows, int n_rows, const float* w, int n, float eps,
+                         float* out32, __half* xs, int tpad, cudaStream_t s) {
+    k_rmsnorm_rows<<<n_rows, NORM_THREADS, 0, s>>>(h, rows, w, n, eps, out32, xs, tpad);
+    note_launch();
+}
+
+// ------------------------------------------------------------------ RoPE
+
+// Rope.Apply's per-position table (reference src/Jevstral/Model/Rope.cs:112-135):
+// theta = (float)position * freq[i] in fp32, then cos/sin correctly rounded to fp32 (via
+// double precision), times the magnitude scale.
+__global__ void k_rope_table(float2* __restrict__ table, const float* __restrict__ freqs, int half, int pos0, int npos,
+                             float mscale) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)npos * half) return;
+    int p = pos0 + (int)(i / half), f = (int)(i % half);
+    float theta = __fmul_rn((float)p, freqs[f]);
+    double sd, cd;
+    sincos((double)theta, &sd, &cd);
+    table[(int64_t)p * half + f] = make_float2(__fmul_rn((float)cd, mscale), __fmul_rn((float)sd, mscale));
+}
+
+void launch_rope_table(float2* table, const float* freqs, int half, int pos0, int npos, float mscale, cudaStream_t s) {
+    int64_t n = (int64_t)npos * half;
+    if (n <= 0) return;
+    k_rope_table<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(table, freqs, half, pos0, npos, mscale);
+    note_launch();
+}
+
+__device__ __forceinline__ __half* kv_addr(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots,
+                                           int layer, int kv_heads, int head, int kv, int slot) {
+    int page = page_table[slot / page_slots];
+    int64_t off = (int64_t)page * page_bytes +
+                  ((int64_t)((layer * kv_heads + head) * 2 + kv) * page_slots + (slot % page_slots)) * 256;
+    return (__half*)((char*)pool + off);
+}
+
+// RotateQueries / StoreKeys / StoreValues / ApplyPositionScale (MinistralModel.cs:638-682):
+// adjacent-pair rotation at position[t] (x0*cos - x1*sin, x0*sin + x1*cos with separate
+// roundings), the llama-4 temperature on q, then q to the attention operand and k, v to
+// their KV page slots as fp16.
+__global__ void k_rope_kv(RopeArgs a) {
+    int t = blockIdx.x;
+    int hd = a.head_dim, half = hd / 2;
+    int qdim = a.heads * hd, kvdim = a.kv_heads * hd;
+    int pos = a.pos[t], slot = a.slot[t];
+    const float* row = a.qkv + (int64_t)t * (qdim + 2 * kvdim);
+    const float2* tab = a.table + (int64_t)pos * half;
+    float temp = 1.0f;
+    if (a.orig_ctx > 0 && a.temperature_scale != 0.f) {
+        float interval = floorf(__fdiv_rn((float)pos, (float)a.orig_ctx));
+        if (interval != 0.f) temp = __fadd_rn(1.0f, __fmul_rn(a.temperature_scale, logf(__fadd_rn(1.0f, interval))));
+    }
+    // q and k pairs
+    int npairs = (qdim + kvdim) / 2;
+    for (int p = threadIdx.x; p < npairs; p += blockDim.x) {
+        int e = 2 * p;
+        int i = (e % hd) / 2;
+        float2 cs = tab[i];
+        float x0 = row[e], x1 = row[e + 1];
+        float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+        float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+        if (e < qdim) {
+            if (temp != 1.0f) { r0 = __fmul_rn(r0, temp); r1 = __fmul_rn(r1, temp); }
+            if (a.q16) *(__half2*)(a.q16 + (int64_t)t * qdim + e) = __floats2half2_rn(r0, r1);
+            if (a.q32) { a.q32[(int64_t)t * qdim + e] = r0; a.q32[(int64_t)t * qdim + e + 1] = r1; }
+        } else {
+            int ke = e - qdim, head = ke / hd, d = ke % hd;
+            __half* dst = kv_addr(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, head, 0, slot);
+            *(__half2*)(dst + d) = __floats2half2_rn(r0, r1);
+            if (a.k32) { a.k32[(int64_t)t * kvdim + ke] = r0; a.k32[(int64_t)t * kvdim + ke + 1] = r1; }
+        }
+    }
+    // v: straight copy to its slot
+    for (int e = threadIdx.x * 2; e < kvdim; e += blockDim.x * 2) {
+        int head = e / hd, d = e % hd;
+        float v0 = row[qdim + kvdim + e], v1 = row[qdim + kvdim + e + 1];
+        __half* dst = kv_addr(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, head, 1, slot);
+        *(__half2*)(dst + d) = __floats2half2_rn(v0, v1);
+    }
+}
+
+void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
+    k_rope_kv<<<a.T, 256, 0, s>>>(a);
+    note_launch();
+}
+
+// ---------------------------------------------------------------- SwiGLU
+
+// Kernels.SwiGlu (Kernels.cs:82-89): up <- g*u; dst <- 1/(1+exp(-g)); dst <- dst*up.
+// gu holds the fused gate/up GEMM output: row tile i carries gate rows 64i..64i+63 in
+// columns 128i..128i+63 and the matching up rows in 128i+64..128i+127.
+__global__ void k_swiglu(const float* __restrict__ gu, int ff, __half* __restrict__ xs, int tpad, float* __restrict__ out32) {
+    int t = blockIdx.x;
+    const float* row = gu + (int64_t)t * 2 * ff;
+    for (int j = threadIdx.x; j < ff; j += blockDim.x) {
+        int col = (j >> 6) * 128 + (j & 63);
+        float g = row[col], u = row[col + 64];
+        float up = __fmul_rn(g, u);
+        float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+        float y = __fmul_rn(sg, up);
+        if (xs) xs[kslab_offset(t, j, tpad)] = __float2half_rn(y);
+        if (out32) out32[(int64_t)t * ff + j] = y;
+    }
+}
+
+void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, cudaStream_t s) {
+    k_swiglu<<<T, 256, 0, s>>>(gu, ff, xs, tpad, out32);
+    note_launch();
+}
+
+// ------------------------------------------------------------ residual add
+
+// Kernels.Add (Kernels.cs:63): h += x.
+__global__ void k_add(float* __restrict__ h, const float* __restrict__ x, int64_t n) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) h[i] = __fadd_rn(h[i], x[i]);
+}
+
+void launch_add(float* h, const float* x, int64_t n, cudaStream_t s) {
+    k_add<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(h, x, n);
+    note_launch();
+}
+
+// K-slab fp16 -> plain fp32 [T][K] (activation capture only).
+__global__ void k_kslab_to_f32(const __half* __restrict__ xs, int T, int K, int tpad, float* __restrict__ out) {
+    int t = blockIdx.x;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) out[(int64_t)t * K + k] = __half2float(xs[kslab_offset(t, k, tpad)]);
+}
+
+void launch_kslab_to_f32(const __half* xs, int T, int K, int tpad, float* out, cudaStream_t s) {
+    k_kslab_to_f32<<<T, 256, 0, s>>>(xs, T, K, tpad, out);
+    note_launch();
+}
+
+}  // namespace jv
+
+namespace jv {
+
+// KvCache.Snapshot / Restore layout (reference src/Jevstral/Model/KvCache.cs:94-136):
+// [pass: K then V][layer][kv head][position < len][128] fp32.
+__global__ void k_kv_export(const __half* __restrict__ pool, const int32_t* __restrict__ page_table, int64_t page_bytes,
+                            int page_slots, int layers, int kv_heads, int len, float* __restrict__ out) {
+    int64_t total = (int64_t)2 * layers * kv_heads * len * 128;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int d = (int)(i % 128);
+        int64_t r = i / 128;
+        int p = (int)(r % len);
+        r /= len;
+        int h = (int)(r % kv_heads);
+        r /= kv_heads;
+        int l = (int)(r % layers);
+        int kv = (int)(r / layers);
+        int page = page_table[p / page_slots];
+        const __half* src = (const __half*)((const char*)pool + (int64_t)page * page_bytes +
+                                             ((int64_t)((l * kv_heads + h) * 2 + kv) * page_slots + p % page_slots) * 256);
+        out[i] = __half2float(src[d]);
+    }
+}
+
+__global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict__ page_table, int64_t page_bytes,
+                            int page_slots, int layers, int kv_heads, int len, const float* __restrict__ in) {
+    int64_t total = (int64_t)2 * layers * kv_heads * len * 128;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int d = (int)(i % 128);
+        int64_t r = i / 128;
+        int p = (int)(r % len);
+        r /= len;
+        int h = (int)(r % kv_heads);
+        r /= kv_heads;
+        int l = (int)(r % layers);
+        int kv = (int)(r / layers);
+        int page = page_table[p / page_slots];
+        __half* dst = (__half*)((char*)pool + (int64_t)page * page_bytes +
+                                ((int64_t)((l * kv_heads + h) * 2 + kv) * page_slots + p % page_slots) * 256);
+        dst[d] = __float2half_rn(in[i]);
+    }
+}
+
+void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
+                      int kv_heads, int len, float* out, cudaStream_t s) {
+    if (len <= 0) return;
+    k_kv_export<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, out);
+    note_launch();
+}
+void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
+                      int kv_heads, int len, const float* in, cudaStream_t s) {
+    if (len <= 0) return;
+    k_kv_import<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, in);
+    note_launch();
+}
+
+}  // namespace jv
