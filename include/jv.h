@@ -103,6 +103,16 @@ int jv_ctx_set_cancel(jv_ctx* ctx, const volatile int32_t* flag);
 /* The cudaStream_t every kernel of this context runs on (for event timing). */
 void* jv_ctx_stream(jv_ctx* ctx);
 
+/* Per-kernel-class timing with CUDA events on the context's stream (no counterpart in the
+ * reference, which times with a Stopwatch around whole calls, src/Jevstral.Cli/Benchmark.cs:549-623).
+ * While enabled every launch of the class is bracketed by events; totals accumulate until
+ * reset. kind: 0 tensor-core GEMM, 1 GEMV, 2 attention, 3 everything else. flops/bytes are
+ * the algorithmic work of the timed launches. */
+enum jv_profile_kind { JV_PROF_GEMM = 0, JV_PROF_GEMV = 1, JV_PROF_ATTENTION = 2, JV_PROF_OTHER = 3 };
+int jv_ctx_profile(jv_ctx* ctx, int32_t enable);
+int jv_ctx_profile_read(jv_ctx* ctx, int32_t kind, double* total_ms, int64_t* launches, double* flops, double* bytes);
+int jv_ctx_profile_reset(jv_ctx* ctx);
+
 /* ---- forward passes ------------------------------------------------------------------- */
 
 /* MinistralModel.ForwardAsync(tokens, options) (MinistralModel.cs:139) — appends tokens and

@@ -183,7 +183,66 @@ struct jv_ctx {
     HostVec<float> h_out;
     HostVec<float> h_cap;
     HostVec<int32_t> h_err;
+    // jv_ctx_profile: events around GEMM / GEMV / attention launches
+    struct Pending {
+        cudaEvent_t a, b;
+        int kind;
+        double flops, bytes;
+    };
+    bool prof = false;
+    std::vector<Pending> pending;
+    std::vector<cudaEvent_t> spare_events;
+    double prof_ms[4] = {0, 0, 0, 0}, prof_flops[4] = {0, 0, 0, 0}, prof_bytes[4] = {0, 0, 0, 0};
+    int64_t prof_launches[4] = {0, 0, 0, 0};
+
+    cudaEvent_t take_event() {
+        if (!spare_events.empty()) {
+            cudaEvent_t e = spare_events.back();
+            spare_events.pop_back();
+            return e;
+        }
+        cudaEvent_t e;
+        JV_CUDA(cudaEventCreate(&e));
+        return e;
+    }
+    // Called after the stream is synchronized.
+    void resolve_profile() {
+        for (auto& p : pending) {
+            float ms = 0.f;
+            JV_CUDA(cudaEventElapsedTime(&ms, p.a, p.b));
+            prof_ms[p.kind] += ms;
+            prof_flops[p.kind] += p.flops;
+            prof_bytes[p.kind] += p.bytes;
+            prof_launches[p.kind] += 1;
+            spare_events.push_back(p.a);
+            spare_events.push_back(p.b);
+        }
+        pending.clear();
+    }
 };
+
+namespace {
+// Brackets the launches issued in its lifetime with events when profiling is on.
+struct ProfScope {
+    jv_ctx* x;
+    jv_ctx::Pending p;
+    ProfScope(jv_ctx* ctx, int kind, double flops, double bytes) : x(ctx) {
+        if (!x->prof) return;
+        p.a = x->take_event();
+        p.b = x->take_event();
+        p.kind = kind;
+        p.flops = flops;
+        p.bytes = bytes;
+        JV_CUDA(cudaEventRecord(p.a, x->stream));
+    }
+    ~ProfScope() {
+        if (!x->prof) return;
+        if (cudaEventRecord(p.b, x->stream) == cudaSuccess) x->pending.push_back(p);
+    }
+};
+
+double weight_bytes(const QWeight& w) { return (double)w.bytes(); }
+}  // namespace
 
 namespace {
 
@@ -552,6 +611,8 @@ void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float*
     a.epilogue = epi;
     a.err = x->d_err;
     static const bool use_ref = getenv("JV_GEMM_REFERENCE") != nullptr;
+    ProfScope ps(x, JV_PROF_GEMM, 2.0 * T * w.rows * w.cols,
+                 weight_bytes(w) + 2.0 * T * w.cols + (epi == EPI_ADD ? 8.0 : 4.0) * T * w.rows);
     if (use_ref)
         launch_gemm_reference(a, x->stream);
     else
@@ -561,6 +622,7 @@ void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float*
 void gemv(jv_ctx* x, const QWeight& w, const float* v, float* y, int epi) {
     int splits = gemv_splits_for(w, x->m->sm_count);
     float* part = x->partial.get((size_t)splits * w.rows);
+    ProfScope ps(x, JV_PROF_GEMV, 2.0 * w.rows * w.cols, weight_bytes(w) + 4.0 * w.cols + 4.0 * w.rows);
     launch_gemv(w, v, part, splits, x->stream);
     launch_gemv_reduce(part, splits, w.rows, y, epi, x->stream);
 }
@@ -652,6 +714,11 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         }
         std::stable_sort(items.begin(), items.end(), [](const AttnItem& a, const AttnItem& b) { return a.nblocks > b.nblocks; });
     }
+    // Algorithmic attention work: QK^T and PV over exactly the visible (query, key) pairs.
+    double attn_flops = 0, attn_bytes = 2.0 * 2 * T * qdim;
+    for (int t = 0; t < T; t++) attn_flops += 4.0 * c.heads * c.head_dim * (L->shared[t] + (L->slot[t] - L->seg[t] + 1));
+    for (const AttnItem& it : items)
+        attn_bytes += (double)(it.shared + (it.slot0 + it.ntok - 1 - it.segment + 1)) * c.head_dim * 2 * 2;
 
     // One H2D for every per-call input: tokens, slot, pos, outputs, rows, items.
     size_t n_items_words = items.size() * (sizeof(AttnItem) / 4);
@@ -730,7 +797,11 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
             da.splits = (da.n_keys + 63) / 64;
             da.partial = x->tmp32.get((size_t)c.heads * da.splits * (2 + c.head_dim));
             da.ctx32 = x->ctx32.get(qdim);
-            launch_decode_attention(da, s);
+            {
+                ProfScope ps(x, JV_PROF_ATTENTION, 4.0 * c.heads * c.head_dim * da.n_keys,
+                             (double)da.n_keys * c.kv_heads * c.head_dim * 2 * 2 + 8.0 * qdim);
+                launch_decode_attention(da, s);
+            }
             observe(x, p + "attn_weighted", da.ctx32, 1, qdim);
             if (capture) {
                 float* ao = x->out32.get(hidden);
@@ -785,7 +856,10 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         aa.ctx16 = x->ctx16.get((size_t)tpad * qdim);
         aa.tpad = tpad;
         aa.ctx32 = capture ? x->ctx32.get((size_t)T * qdim) : nullptr;
-        launch_attention(aa, s);
+        {
+            ProfScope ps(x, JV_PROF_ATTENTION, attn_flops, attn_bytes);
+            launch_attention(aa, s);
+        }
         if (capture) observe(x, p + "attn_weighted", aa.ctx32, T, qdim);
         if (capture) {
             float* ao = x->out32.get((size_t)T * hidden);
@@ -865,6 +939,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         }
     }
     sync_check(x);
+    x->resolve_profile();
 }
 
 HostLayout layout_from(const jv_layout* l, int T) {
@@ -1018,6 +1093,11 @@ void jv_ctx_destroy(jv_ctx* x) {
     x->h_cap.release();
     x->h_err.release();
     if (x->d_err) cudaFree(x->d_err);
+    for (auto& p : x->pending) {
+        cudaEventDestroy(p.a);
+        cudaEventDestroy(p.b);
+    }
+    for (auto e : x->spare_events) cudaEventDestroy(e);
     cudaStreamDestroy(x->stream);
     delete x;
 }
@@ -1036,6 +1116,30 @@ int jv_ctx_set_cancel(jv_ctx* x, const volatile int32_t* flag) {
 }
 
 void* jv_ctx_stream(jv_ctx* x) { return x ? (void*)x->stream : nullptr; }
+
+int jv_ctx_profile(jv_ctx* x, int32_t enable) {
+    if (!x) return set_error(JV_ERR_ARG, "NULL context");
+    x->prof = enable != 0;
+    return JV_OK;
+}
+
+int jv_ctx_profile_read(jv_ctx* x, int32_t kind, double* total_ms, int64_t* launches, double* flops, double* bytes) {
+    if (!x || kind < 0 || kind > 3) return set_error(JV_ERR_ARG, "bad profile query");
+    if (total_ms) *total_ms = x->prof_ms[kind];
+    if (launches) *launches = x->prof_launches[kind];
+    if (flops) *flops = x->prof_flops[kind];
+    if (bytes) *bytes = x->prof_bytes[kind];
+    return JV_OK;
+}
+
+int jv_ctx_profile_reset(jv_ctx* x) {
+    if (!x) return set_error(JV_ERR_ARG, "NULL context");
+    for (int k = 0; k < 4; k++) {
+        x->prof_ms[k] = x->prof_flops[k] = x->prof_bytes[k] = 0;
+        x->prof_launches[k] = 0;
+    }
+    return JV_OK;
+}
 
 int jv_forward(jv_ctx* x, const int32_t* tokens, int32_t n, float* logits) {
     if (!x || (!tokens && n > 0)) return set_error(JV_ERR_ARG, "NULL argument");

@@ -49,6 +49,10 @@ SIGNATURES = [
     ("jv_ctx_set_sink", C.c_int, [vp, SINK, vp]),
     ("jv_ctx_set_cancel", C.c_int, [vp, i32p]),
     ("jv_ctx_stream", vp, [vp]),
+    ("jv_ctx_profile", C.c_int, [vp, i32]),
+    ("jv_ctx_profile_read", C.c_int, [vp, i32, C.POINTER(C.c_double), C.POINTER(i64), C.POINTER(C.c_double),
+                                      C.POINTER(C.c_double)]),
+    ("jv_ctx_profile_reset", C.c_int, [vp]),
     ("jv_forward", C.c_int, [vp, i32p, i32, f32p]),
     ("jv_forward_selected", C.c_int, [vp, i32p, i32, i32p, i32, f32p]),
     ("jv_forward_tree", C.c_int, [vp, i32p, i32, i32p, i32p, i32, i32p, i32, f32p]),

@@ -198,6 +198,21 @@ class MinistralModel:
     def reset_kv_cache(self) -> None:
         self.kv_cache.reset()
 
+    PROFILE_KINDS = {"gemm": 0, "gemv": 1, "attention": 2, "other": 3}
+
+    def profile(self, enable: bool = True) -> None:
+        """Bracket GEMM / GEMV / attention launches with CUDA events on this context's stream."""
+        check(lib.jv_ctx_profile(self._h, int(enable)))
+
+    def profile_reset(self) -> None:
+        check(lib.jv_ctx_profile_reset(self._h))
+
+    def profile_read(self, kind: str) -> dict:
+        ms, n, fl, by = C.c_double(), C.c_int64(), C.c_double(), C.c_double()
+        check(lib.jv_ctx_profile_read(self._h, self.PROFILE_KINDS[kind], C.byref(ms), C.byref(n), C.byref(fl),
+                                      C.byref(by)))
+        return {"ms": ms.value, "launches": n.value, "flops": fl.value, "bytes": by.value}
+
     def set_activation_sink(self, sink: Optional[Callable[[str, np.ndarray], None]]) -> None:
         """IActivationSink: sink(name, array[rows, cols]) after every named sub-step."""
         if sink is None:

@@ -1,0 +1,86 @@
+"""The C ABI boundary without a GPU: the library loads, exports every declared symbol, and its
+error paths return statuses instead of crashing."""
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+HEADER = REPO / "include" / "jv.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(jv_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    import ctypes
+
+    from jevstral_b200._lib import LIB_PATH
+
+    lib = ctypes.CDLL(str(LIB_PATH))
+    names = declared_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"declared in jv.h but not exported: {missing}"
+
+
+def test_python_binding_covers_the_header():
+    from jevstral_b200 import SIGNATURES
+
+    bound = {s[0] for s in SIGNATURES}
+    assert set(declared_functions()) <= bound
+
+
+def test_build_targets_sm100a_only():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("jv_build", REPO / "llm-shield_b200" / "build.py")
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    assert b.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_error_paths_return_statuses():
+    import jevstral_b200 as jv
+
+    assert jv.device_count() >= 0
+    if jv.device_count() == 0:
+        with pytest.raises(jv.JvError):
+            jv.Model("/nonexistent.gguf")
+    else:
+        with pytest.raises(jv.GgufIOError):
+            jv.Model("/nonexistent.gguf")
+
+
+def test_token_layout_restatement_matches_the_reference_rules():
+    """TokenLayout.Tree / Rows (MinistralModel.cs:720-780) on a hand-checked case."""
+    from jevstral_b200 import TokenLayout
+
+    t = TokenLayout.tree(start_pos=10, trunk=3, offsets=[3, 5], tokens=8)
+    assert t.slot == list(range(10, 18))
+    assert t.position == [10, 11, 12, 13, 14, 13, 14, 15]
+    assert t.shared == [10, 10, 10, 13, 13, 13, 13, 13]
+    assert t.segment == [10, 10, 10, 13, 13, 15, 15, 15]
+    assert t.outputs == [4, 7] and t.end == 18
+    r = TokenLayout.rows(shared=4, row_base=[10, 20], row_length=[2, 0], row_tokens=[1, 2], sparse=True)
+    assert r.slot == [12, 20, 21] and r.position == [6, 4, 5] and r.segment == [10, 20, 20]
+    assert r.outputs == [0, 2] and r.end == 22
+
+
+def test_decider_tail_matches_the_reference_formulas():
+    """JevstralDecider.DecideAsync margins and softmax(z/T) (JevstralDecider.cs:306-313)."""
+    from jevstral_b200 import decision_probs, margins_from_verdicts
+
+    v = np.array([[1.0, 3.0, 0.5], [2.0, -1.0, -3.0]], np.float32)  # 2 yes rows, 1 no row
+    z = margins_from_verdicts(v, n_yes=2)
+    assert np.allclose(z, [2.5, 5.0])
+    p = decision_probs(z, 2.0)
+    e = np.exp(z / 2 - (z / 2).max())
+    assert np.allclose(p, e / e.sum(), rtol=1e-6)

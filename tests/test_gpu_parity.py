@@ -1,0 +1,278 @@
+"""Parity of the B200 path with the CPU oracle, through the C ABI (libjv.so).
+
+Gates: dequantization bit-exact; per-layer hidden states within
+1e-2 relative L2; per-option log-odds z_i within 2e-2 absolute with the same argmax.
+Self-consistency gates from the reference's own suites: a branch is bit-identical to the
+same continuation run alone (DeciderTests.cs:54-91) and a cached prefix is bit-identical
+to running the prompt whole (SystemPromptCacheTests.cs:41-68).
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import jevstral_b200 as jv
+from jevstral_b200 import margins_from_verdicts
+from oracle import binding as ob
+from small_model import SMALL_CFG, SMALL_PROMPT, VERDICT_ROWS, WIDE_CFG
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN_TOL = 1e-2   # relative L2 per layer (north star)
+Z_TOL = 2e-2        # absolute, per-option log-odds (north star)
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def toks(n, seed, vocab=16384):
+    return np.random.default_rng(seed).integers(1000, vocab, n).tolist()
+
+
+def capture_into(d):
+    return lambda name, arr: d.__setitem__(name, arr)
+
+
+@pytest.fixture(scope="module")
+def small(small_gguf):
+    m = jv.Model(small_gguf, kv_pool_mb=256)
+    yield m
+    m.close()
+
+
+def ctx(model, cap=512):
+    return jv.MinistralModel(model, cap)
+
+
+# ------------------------------------------------------------------ dequant
+
+
+@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
+def test_embedding_gather_is_bit_exact(model_factory, qtype):
+    """GatherRows decodes rows bit-exactly (d*q, d*(n-8), d*q5+m; no FMA)."""
+    path = model_factory(SMALL_CFG, qtype, seed=3)
+    prompt = [1] + toks(30, 5)
+    gpu, cpu = {}, {}
+    with jv.Model(path, kv_pool_mb=128) as m, ctx(m) as c:
+        c.set_activation_sink(capture_into(gpu))
+        c.forward(prompt)
+    with ob.OracleModel(path) as o:
+        o.forward(prompt, sink=capture_into(cpu))
+    assert gpu["embeddings"].view(np.uint32).tobytes() == cpu["embeddings"].view(np.uint32).tobytes()
+
+
+# ------------------------------------------------------------- forward parity
+
+
+def test_causal_forward_matches_the_reference_numpy_golden(small, golden_small):
+    """Per-layer outputs against the reference's own NumPy model (committed golden)."""
+    caps = {}
+    with ctx(small) as c:
+        c.set_activation_sink(capture_into(caps))
+        logits = c.forward(SMALL_PROMPT)
+    for l in range(SMALL_CFG.layers):
+        key = f"blk.{l}.output"
+        assert rel_l2(caps[key], golden_small["cap/" + key]) < HIDDEN_TOL, key
+    assert rel_l2(logits, golden_small["logits"]) < HIDDEN_TOL
+    assert int(np.argmax(logits)) == int(np.argmax(golden_small["logits"]))
+
+
+@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
+def test_tree_decision_matches_the_oracle(model_factory, qtype):
+    """A ForwardTreeAsync decision: per-layer hidden states and z_i against the oracle."""
+    path = model_factory(SMALL_CFG, qtype, seed=11)
+    trunk = [1] + toks(70, 21)
+    branches = [toks(n, 30 + i) for i, n in enumerate((12, 7, 20, 3, 16))]
+    gpu, cpu = {}, {}
+    with jv.Model(path, kv_pool_mb=128) as m, ctx(m) as c:
+        c.set_activation_sink(capture_into(gpu))
+        v_gpu = c.forward_tree(trunk, branches, VERDICT_ROWS)
+    with ob.OracleModel(path) as o:
+        v_cpu = o.forward_tree(trunk, branches, VERDICT_ROWS, sink=capture_into(cpu))
+    for l in range(SMALL_CFG.layers):
+        assert rel_l2(gpu[f"blk.{l}.output"], cpu[f"blk.{l}.output"]) < HIDDEN_TOL
+    z_gpu, z_cpu = margins_from_verdicts(v_gpu, 1), margins_from_verdicts(v_cpu, 1)
+    assert np.abs(z_gpu - z_cpu).max() < Z_TOL
+    assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
+
+
+@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
+def test_full_width_tree_matches_the_oracle(model_factory, qtype):
+    """Every real matrix shape of Ministral-3 3B (two layers): tree decision parity."""
+    path = model_factory(WIDE_CFG, qtype, seed=5)
+    trunk = [1] + toks(190, 7)
+    branches = [toks(n, 40 + i) for i, n in enumerate((32, 17, 48))]
+    gpu, cpu = {}, {}
+    with jv.Model(path, kv_pool_mb=512) as m, ctx(m) as c:
+        c.set_activation_sink(capture_into(gpu))
+        v_gpu = c.forward_tree(trunk, branches, VERDICT_ROWS)
+    with ob.OracleModel(path) as o:
+        v_cpu = o.forward_tree(trunk, branches, VERDICT_ROWS, sink=capture_into(cpu))
+    for key in [f"blk.{l}.{n}" for l in range(WIDE_CFG.layers) for n in ("attn_out", "ffn_out", "output")]:
+        assert rel_l2(gpu[key], cpu[key]) < HIDDEN_TOL, key
+    z_gpu, z_cpu = margins_from_verdicts(v_gpu, 1), margins_from_verdicts(v_cpu, 1)
+    assert np.abs(z_gpu - z_cpu).max() < Z_TOL
+    assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
+
+
+def test_decode_steps_match_the_oracle(small):
+    """Single-token forwards (the decode GEMV path) with the full LM head."""
+    prompt = [1] + toks(40, 9)
+    with ctx(small) as c, ob.OracleModel(small.path) as o:
+        lg = c.forward(prompt)
+        lo = o.forward(prompt)
+        assert rel_l2(lg, lo) < HIDDEN_TOL
+        nxt = int(np.argmax(lo))
+        for step in range(4):
+            lg = c.forward([nxt])
+            lo = o.forward([nxt])
+            assert rel_l2(lg, lo) < HIDDEN_TOL, step
+            nxt = int(np.argmax(lo))
+
+
+def test_decode_greedy_follows_its_own_argmax(small):
+    prompt = [1] + toks(20, 19)
+    with ctx(small) as a, ctx(small) as b:
+        a.prefill(prompt)
+        got = a.decode_greedy(1500, 5)
+        b.prefill(prompt)
+        want, tok = [], 1500
+        for _ in range(5):
+            tok = int(np.argmax(b.forward([tok])))
+            want.append(tok)
+        assert got.tolist() == want
+
+
+# -------------------------------------------------------- bit-identity gates
+
+
+def test_branches_match_running_each_continuation_alone(small):
+    trunk = [1] + toks(80, 1)
+    branches = [toks(n, 10 + i) for i, n in enumerate((5, 19, 33, 2))]
+    with ctx(small) as c:
+        tree = c.forward_tree(trunk, branches, VERDICT_ROWS)
+        for b, br in enumerate(branches):
+            c.kv_cache.reset()
+            c.prefill(trunk)
+            alone = c.forward_selected(br, VERDICT_ROWS)
+            assert alone.tobytes() == tree[b].tobytes(), f"branch {b}"
+
+
+def test_cached_and_uncached_produce_identical_logits(small):
+    prompt = [1] + toks(100, 3)
+    with ctx(small) as c:
+        whole = c.forward(prompt)
+        c.kv_cache.reset()
+        c.prefill(prompt[:61])
+        snap = c.kv_cache.snapshot(61)
+        c.kv_cache.reset()
+        c.kv_cache.restore(snap, 61)
+        cached = c.forward(prompt[61:])
+        assert whole.tobytes() == cached.tobytes()
+        # zero-copy pages shared with a second context
+        c.kv_cache.reset()
+        c.prefill(prompt[:61])
+        shared = c.kv_cache.share(61)
+        with ctx(small) as d:
+            d.kv_cache.adopt(shared)
+            again = d.forward(prompt[61:])
+        shared.release()
+        assert whole.tobytes() == again.tobytes()
+
+
+def test_reusing_the_trunk_for_a_second_decision_is_bit_identical(small):
+    """C3's second decision: the trunk stays in the cache; the decider re-runs its last token."""
+    from jevstral_b200 import TokenDecider
+
+    prefix = [1] + toks(150, 2)
+    b1 = [toks(n, 50 + i) for i, n in enumerate((6, 9, 4))]
+    b2 = [toks(n, 60 + i) for i, n in enumerate((8, 3, 12))]
+    with ctx(small) as c, ctx(small) as fresh:
+        d = TokenDecider(c, [13059], [2649])
+        d.decide(prefix, b1)
+        r2 = d.decide(prefix, b2)
+        assert r2.cached_tokens == len(prefix) - 1
+        ref = TokenDecider(fresh, [13059], [2649]).decide(prefix, b2)
+        assert r2.margins.tobytes() == ref.margins.tobytes()
+
+
+def test_snapshot_round_trip_and_errors(small):
+    with ctx(small) as c:
+        c.prefill([1] + toks(70, 4))
+        assert c.kv_cache.length == 71
+        snap = c.kv_cache.snapshot(70)
+        assert snap.size == 2 * SMALL_CFG.layers * SMALL_CFG.kv_heads * 70 * 128
+        with pytest.raises(jv.ArgumentOutOfRangeError):
+            c.kv_cache.snapshot(72)
+        with pytest.raises(jv.ArgumentError):
+            c.kv_cache.restore(snap, 71)
+        c.kv_cache.reset()
+        c.kv_cache.restore(snap, 70)
+        assert np.array_equal(c.kv_cache.snapshot(70), snap)
+
+
+def test_errors_map_to_the_reference_exceptions(small, tmp_path):
+    with ctx(small) as c:
+        with pytest.raises(jv.ArgumentOutOfRangeError):
+            c.forward([1, 16384])
+        with pytest.raises(jv.ArgumentError):
+            c.forward_tree([1, 2000], [], VERDICT_ROWS)
+        with pytest.raises(jv.ArgumentError):
+            c.forward_tree([1, 2000], [[1500], []], VERDICT_ROWS)
+        flag = np.ones(1, np.int32)
+        c.set_cancellation(flag)
+        with pytest.raises(jv.OperationCanceledError):
+            c.forward([1, 2000, 3000])
+        c.set_cancellation(None)
+        assert len(c.forward([1, 2000])) == SMALL_CFG.vocab
+    with open(small.path, "rb") as f:
+        data = f.read()
+    short = tmp_path / "short.gguf"
+    short.write_bytes(data[: len(data) // 3])
+    with pytest.raises(jv.GgufIOError):
+        jv.Model(short)
+
+
+def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
+    """The tcgen05 GEMM against a CUDA-core product over the same fp16 operands, at every real
+    matrix shape: only the accumulation order differs."""
+    path = model_factory(WIDE_CFG, "Q8_0", seed=5)
+    code = (
+        "import sys, numpy as np; sys.path[:0] = sys.argv[2:];"
+        "import jevstral_b200 as jv;"
+        "m = jv.Model(sys.argv[1], kv_pool_mb=512); c = jv.MinistralModel(m); caps = {};"
+        "c.set_activation_sink(lambda n, a: caps.__setitem__(n, a));"
+        "c.forward([1] + list(range(1000, 1300)));"
+        "np.savez(sys.stdout.buffer, **{k: v for k, v in caps.items() if k.endswith(('attn_out', 'ffn_out', 'output'))})"
+    )
+    import io
+
+    from conftest import REPO
+
+    paths = [str(REPO / "llm-shield_b200"), str(REPO)]
+    outs = []
+    for ref in (False, True):
+        env = dict(os.environ)
+        env.pop("JV_GEMM_REFERENCE", None)
+        if ref:
+            env["JV_GEMM_REFERENCE"] = "1"
+        r = subprocess.run([sys.executable, "-c", code, str(path)] + paths, env=env, capture_output=True, timeout=900)
+        assert r.returncode == 0, r.stderr.decode()[-2000:]
+        outs.append(np.load(io.BytesIO(r.stdout)))
+    tc, ref = outs
+    for k in ref.files:
+        assert rel_l2(tc[k], ref[k]) < 1e-4, k
+
+
+def test_kernel_launches_are_counted(small):
+    before = jv.kernel_launches()
+    with ctx(small) as c:
+        c.forward_tree([1, 1500, 2500], [[3000, 4000], [5000]], VERDICT_ROWS)
+    assert jv.kernel_launches() - before > 10 * SMALL_CFG.layers
