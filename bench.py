@@ -158,13 +158,13 @@ def cpu_baseline_c2(steps: int = 1, min_seconds: float = 10.0):
 # ------------------------------------------------------------------- b200 arm
 
 
-def ensure_model(qtype: str, rank: int, dist) -> Path:
-    from jevstral_b200.synth import MINISTRAL_3B, write_random_gguf
+def ensure_model(qtype: str, rank: int, dist, layers: int = 26) -> Path:
+    from jevstral_b200.synth import SynthConfig, write_random_gguf
 
     MODEL_DIR.mkdir(parents=True, exist_ok=True)
-    path = MODEL_DIR / f"ministral3b_{qtype.lower()}_seed0.gguf"
+    path = MODEL_DIR / f"ministral3b_{layers}l_{qtype.lower()}_seed0.gguf"
     if rank == 0 and not path.exists():
-        write_random_gguf(path, MINISTRAL_3B, qtype, seed=0, backend="fast")
+        write_random_gguf(path, SynthConfig(layers=layers), qtype, seed=0, backend="fast")
     if dist is not None:
         dist.barrier()
     return path
@@ -177,8 +177,8 @@ def run_b200(args, rank, world, local_rank, dist):
 
     torch.cuda.set_device(local_rank)
     qtype = {"c3": "Q5_1", "c4": "Q4_0"}.get(args.config, "Q8_0")
-    path = ensure_model(qtype, rank, dist)
-    model = jv.Model(path, device=local_rank, kv_pool_mb=16384)
+    path = ensure_model(qtype, rank, dist, args.layers)
+    model = jv.Model(path, device=local_rank, kv_pool_mb=args.kv_pool_mb)
     ctx = jv.MinistralModel(model, 512)
     stream = torch.cuda.ExternalStream(ctx.stream, device=local_rank)
     rng = np.random.default_rng(1000 + rank)
@@ -264,7 +264,7 @@ def run_b200(args, rank, world, local_rank, dist):
                        "parallelism": f"dp{world} (independent replicas, no collective)",
                        "l2": "weights (3.2+ GB) exceed the 126 MB L2 and stream from HBM every step"},
             "decisions_per_s": world * n_dec / dev_s,
-            "linear_tflops": world * tokens * LINEAR_FLOPS_PER_TOKEN / dev_s / 1e12,
+            "linear_tflops": world * tokens * LINEAR_FLOPS_PER_TOKEN * args.layers / 26 / dev_s / 1e12,
             "attention_pairs_per_step": pairs // n_dec,
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (all four projections)",
                          "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
@@ -360,6 +360,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=26, help="fewer layers of the same width (profiling only)")
+    ap.add_argument("--kv-pool-mb", type=int, default=4096)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

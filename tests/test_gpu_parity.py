@@ -250,7 +250,8 @@ def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
         "m = jv.Model(sys.argv[1], kv_pool_mb=512); c = jv.MinistralModel(m); caps = {};"
         "c.set_activation_sink(lambda n, a: caps.__setitem__(n, a));"
         "c.forward([1] + list(range(1000, 1300)));"
-        "np.savez(sys.stdout.buffer, **{k: v for k, v in caps.items() if k.endswith(('attn_out', 'ffn_out', 'output'))})"
+        "np.savez(sys.stdout.buffer, **{k: v for k, v in caps.items() "
+        "if k.endswith(('.v', 'k_rope', 'attn_out', 'ffn_out', 'output'))})"
     )
     import io
 
@@ -267,8 +268,14 @@ def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
         assert r.returncode == 0, r.stderr.decode()[-2000:]
         outs.append(np.load(io.BytesIO(r.stdout)))
     tc, ref = outs
-    for k in ref.files:
-        assert rel_l2(tc[k], ref[k]) < 1e-4, k
+    # Layer 0's QKV product sees identical operands in both runs: only the accumulation order
+    # differs. Later tensors also inherit fp16 re-rounding of slightly different activations
+    # (one fp16 ulp is 4.9e-4 relative), hence the looser bound there.
+    errs = {k: rel_l2(tc[k], ref[k]) for k in ref.files}
+    for k in ("blk.0.v", "blk.0.k_rope"):
+        assert errs[k] < 1e-5, (k, errs)
+    for k, e in errs.items():
+        assert e < 2e-3, (k, errs)
 
 
 def test_kernel_launches_are_counted(small):
