@@ -127,64 +127,64 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// int8 / small unsigned byte -> exact fp32 via the 2^23 magic number: byte b placed in the
-// mantissa of 2^23 gives 2^23 + b; subtracting the bias yields the integer exactly.
-__device__ __forceinline__ float byte_f(uint32_t x, uint32_t sel) { return __uint_as_float(__byte_perm(x, 0x4B000000u, sel)); }
-
-__device__ __forceinline__ uint32_t h2u(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *(uint32_t*)&h;
+// Bytes b0, b1 of x (picked by the byte_perm selector) as the fp16 pair (1024 + b0, 1024 + b1):
+// a byte placed under the exponent of 1024 (0x64) is 1024 + b exactly.
+__device__ __forceinline__ __half2 byte_pair(uint32_t x, uint32_t sel) {
+    uint32_t w = __byte_perm(x, 0x64646464u, sel);
+    return *reinterpret_cast<__half2*>(&w);
 }
+__device__ __forceinline__ uint32_t hu(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// Decode one (row, 16-byte chunk) item: 8 consecutive weights of row r, k = 8c..8c+7.
+// Decode one (row, 16-byte chunk) item: 8 consecutive weights of row r, k = 8c..8c+7, as
+// packed fp16 pairs. Q8_0 and Q4_0: the integer is exact in fp16 and d * q is one
+// correctly rounded fp16 multiply — the same value as the exact fp32 product rounded to
+// fp16. Q5_1: d * q5 + m with one fp16 rounding (an fp16 FMA).
 template <int TYPE>
 __device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r, int c) {
-    float f[8];
+    uint4 o;
     if (TYPE == T_Q8_0) {
         uint2 q = *(const uint2*)(raw + r * 64 + c * 8);
-        float d = __half2float(*(const __half*)(raw + 8192 + (r * 2 + (c >> 2)) * 2));
-        uint32_t x0 = q.x ^ 0x80808080u, x1 = q.y ^ 0x80808080u;
-        const float bias = 8388736.0f;  // 2^23 + 128
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            f[i] = __fmul_rn(d, __fsub_rn(byte_f(x0, 0x7540u + i), bias));
-            f[4 + i] = __fmul_rn(d, __fsub_rn(byte_f(x1, 0x7540u + i), bias));
-        }
-    } else {
-        int b = c >> 2, e0 = (c & 3) * 8;
-        uint2 q = *(const uint2*)(raw + r * 32 + b * 16 + (e0 & 15));
-        uint32_t x0, x1;
-        if (e0 < 16) {
-            x0 = q.x & 0x0F0F0F0Fu;
-            x1 = q.y & 0x0F0F0F0Fu;
-        } else {
-            x0 = (q.x >> 4) & 0x0F0F0F0Fu;
-            x1 = (q.y >> 4) & 0x0F0F0F0Fu;
-        }
-        if (TYPE == T_Q4_0) {
-            float d = __half2float(*(const __half*)(raw + 4096 + (r * 2 + b) * 2));
-            const float bias = 8388616.0f;  // 2^23 + 8
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                f[i] = __fmul_rn(d, __fsub_rn(byte_f(x0, 0x7540u + i), bias));
-                f[4 + i] = __fmul_rn(d, __fsub_rn(byte_f(x1, 0x7540u + i), bias));
-            }
-        } else {  // Q5_1
-            uint32_t qh = *(const uint32_t*)(raw + 4096 + (r * 2 + b) * 4);
-            float d = __half2float(*(const __half*)(raw + 5120 + (r * 2 + b) * 2));
-            float m = __half2float(*(const __half*)(raw + 5632 + (r * 2 + b) * 2));
-            uint32_t h0 = (qh >> e0) & 0xFu, h1 = (qh >> (e0 + 4)) & 0xFu;
-            x0 |= ((h0 & 1u) << 4) | ((h0 & 2u) << 11) | ((h0 & 4u) << 18) | ((h0 & 8u) << 25);
-            x1 |= ((h1 & 1u) << 4) | ((h1 & 2u) << 11) | ((h1 & 4u) << 18) | ((h1 & 8u) << 25);
-            const float bias = 8388608.0f;  // 2^23
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                f[i] = __fadd_rn(__fmul_rn(d, __fsub_rn(byte_f(x0, 0x7540u + i), bias)), m);
-                f[4 + i] = __fadd_rn(__fmul_rn(d, __fsub_rn(byte_f(x1, 0x7540u + i), bias)), m);
-            }
-        }
+        __half2 d2 = __half2half2(*(const __half*)(raw + 8192 + (r * 2 + (c >> 2)) * 2));
+        uint32_t x0 = q.x ^ 0x80808080u, x1 = q.y ^ 0x80808080u;  // int8 -> biased byte b = q + 128
+        const __half2 bias = __floats2half2_rn(1152.f, 1152.f);    // 1024 + 128
+        o.x = hu(__hmul2(__hsub2(byte_pair(x0, 0x4140u), bias), d2));
+        o.y = hu(__hmul2(__hsub2(byte_pair(x0, 0x4342u), bias), d2));
+        o.z = hu(__hmul2(__hsub2(byte_pair(x1, 0x4140u), bias), d2));
+        o.w = hu(__hmul2(__hsub2(byte_pair(x1, 0x4342u), bias), d2));
+        return o;
     }
-    return make_uint4(h2u(f[0], f[1]), h2u(f[2], f[3]), h2u(f[4], f[5]), h2u(f[6], f[7]));
+    int b = c >> 2, e0 = (c & 3) * 8;
+    uint2 q = *(const uint2*)(raw + r * 32 + b * 16 + (e0 & 15));
+    uint32_t x0, x1;
+    if (e0 < 16) {
+        x0 = q.x & 0x0F0F0F0Fu;
+        x1 = q.y & 0x0F0F0F0Fu;
+    } else {
+        x0 = (q.x >> 4) & 0x0F0F0F0Fu;
+        x1 = (q.y >> 4) & 0x0F0F0F0Fu;
+    }
+    if (TYPE == T_Q4_0) {
+        __half2 d2 = __half2half2(*(const __half*)(raw + 4096 + (r * 2 + b) * 2));
+        const __half2 bias = __floats2half2_rn(1032.f, 1032.f);  // 1024 + 8
+        o.x = hu(__hmul2(__hsub2(byte_pair(x0, 0x4140u), bias), d2));
+        o.y = hu(__hmul2(__hsub2(byte_pair(x0, 0x4342u), bias), d2));
+        o.z = hu(__hmul2(__hsub2(byte_pair(x1, 0x4140u), bias), d2));
+        o.w = hu(__hmul2(__hsub2(byte_pair(x1, 0x4342u), bias), d2));
+        return o;
+    }
+    // Q5_1: fifth bit of element e from qh bit e, spread into bit 4 of each byte.
+    uint32_t qh = *(const uint32_t*)(raw + 4096 + (r * 2 + b) * 4);
+    __half2 d2 = __half2half2(*(const __half*)(raw + 5120 + (r * 2 + b) * 2));
+    __half2 m2 = __half2half2(*(const __half*)(raw + 5632 + (r * 2 + b) * 2));
+    uint32_t h0 = (qh >> e0) & 0xFu, h1 = (qh >> (e0 + 4)) & 0xFu;
+    x0 |= ((h0 & 1u) << 4) | ((h0 & 2u) << 11) | ((h0 & 4u) << 18) | ((h0 & 8u) << 25);
+    x1 |= ((h1 & 1u) << 4) | ((h1 & 2u) << 11) | ((h1 & 4u) << 18) | ((h1 & 8u) << 25);
+    const __half2 bias = __floats2half2_rn(1024.f, 1024.f);
+    o.x = hu(__hfma2(__hsub2(byte_pair(x0, 0x4140u), bias), d2, m2));
+    o.y = hu(__hfma2(__hsub2(byte_pair(x0, 0x4342u), bias), d2, m2));
+    o.z = hu(__hfma2(__hsub2(byte_pair(x1, 0x4140u), bias), d2, m2));
+    o.w = hu(__hfma2(__hsub2(byte_pair(x1, 0x4342u), bias), d2, m2));
+    return o;
 }
 
 struct TcParams {
@@ -192,9 +192,14 @@ struct TcParams {
     const __half* x;
     float* y;
     int* err;
-    int ksteps, T, tpad, bn, ldy, epilogue, stages, ncols;
+    __half* xs_out;   // EPI_SWIGLU destination (K-slab, tpad rows)
+    float* ws;        // split-K partials [split][T][ldy] (splits > 1)
+    int* counters;    // one arrival counter per (row tile, token tile); zero between launches
+    int ksteps, T, tpad, bn, ldy, epilogue, stages, ncols, splits;
     int raw_off, b_off, bar_off;  // byte offsets inside the 1024-aligned dynamic smem
 };
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
 
 template <int TYPE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
@@ -207,10 +212,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     uint8_t* Rs = sm + p.raw_off;           // S x chunk
     uint64_t* bars = (uint64_t*)(sm + p.bar_off);
     uint32_t* tslot = (uint32_t*)(bars + 3 * S + 1);
+    volatile int* last_flag = (volatile int*)(tslot + 1);
     const uint32_t full0 = s_addr(bars), dec0 = s_addr(bars + S), empty0 = s_addr(bars + 2 * S), accf = s_addr(bars + 3 * S);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile = blockIdx.x, t0 = blockIdx.y * p.bn;
+    // Split-K: this CTA's contiguous share of the k steps. The split is fixed by the weight
+    // shape (host side), never by the token count, so it cannot break batch invariance.
+    const int nks = p.ksteps / p.splits, kbase = blockIdx.z * nks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -231,15 +240,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         if (lane == 0) {
             int issued = 0;
             bool ok = true;
-            const uint8_t* wsrc = p.w + (int64_t)tile * p.ksteps * cb;
+            const uint8_t* wsrc = p.w + ((int64_t)tile * p.ksteps + kbase) * cb;
             const uint32_t bbytes = (uint32_t)p.bn * 128u;
-            for (int ks = 0; ks < p.ksteps; ks++) {
+            for (int ks = 0; ks < nks; ks++) {
                 int s = ks % S;
                 uint32_t ph = (uint32_t)(ks / S) & 1u;
                 if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) { ok = false; break; }
                 mbar_expect_tx(full0 + 8 * s, (uint32_t)cb + bbytes);
                 bulk_g2s(s_addr(Rs + s * cb), wsrc + (int64_t)ks * cb, (uint32_t)cb, full0 + 8 * s);
-                bulk_g2s(s_addr(Bs + (size_t)s * bbytes), p.x + ((int64_t)ks * p.tpad + t0) * 64, bbytes, full0 + 8 * s);
+                bulk_g2s(s_addr(Bs + (size_t)s * bbytes), p.x + ((int64_t)(kbase + ks) * p.tpad + t0) * 64, bbytes,
+                         full0 + 8 * s);
                 issued++;
             }
             if (!ok) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
@@ -251,7 +261,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(p.bn, 128);
             const uint32_t bbytes = (uint32_t)p.bn * 128u;
-            for (int ks = 0; ks < p.ksteps; ks++) {
+            for (int ks = 0; ks < nks; ks++) {
                 int s = ks % S;
                 uint32_t ph = (uint32_t)(ks / S) & 1u;
                 if (!mbar_wait(full0 + 8 * s, ph) || !mbar_wait(dec0 + 8 * s, ph)) {
@@ -268,20 +278,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             umma_commit(accf);  // always: the epilogue and teardown wait for a quiescent accumulator
         }
     } else if (warp >= 4) {
+        // Thread dt decodes chunk c = dt % 8 of rows r0 + 32*it (it = 0..3); the swizzled
+        // position of that chunk is the same for all four rows.
         const int dt = threadIdx.x - 128;
+        const int c = dt & 7, r0 = dt >> 3;
+        const int a_off = r0 * 128 + ((c ^ (r0 & 7)) << 4);
         bool ok = true;
-        for (int ks = 0; ks < p.ksteps; ks++) {
+        for (int ks = 0; ks < nks; ks++) {
             int s = ks % S;
             uint32_t ph = (uint32_t)(ks / S) & 1u;
             if (!mbar_wait(full0 + 8 * s, ph)) { ok = false; break; }
             const uint8_t* raw = Rs + s * cb;
-            uint8_t* A = As + s * 16384;
+            uint8_t* A = As + s * 16384 + a_off;
+            uint4 v[4];
 #pragma unroll
-            for (int it = 0; it < 4; it++) {
-                int item = it * DEC_THREADS + dt;
-                int r = item >> 3, c = item & 7;
-                *(uint4*)(A + r * 128 + ((c ^ (r & 7)) << 4)) = decode8<TYPE>(raw, r, c);
-            }
+            for (int it = 0; it < 4; it++) v[it] = decode8<TYPE>(raw, r0 + 32 * it, c);
+#pragma unroll
+            for (int it = 0; it < 4; it++) *(uint4*)(A + it * 32 * 128) = v[it];
             fence_proxy_async();
             mbar_arrive(dec0 + 8 * s);
         }
@@ -291,26 +304,104 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             int q = warp & 3;
             bool ready = mbar_wait(accf, 0);
             tc_fence_after();
-            if (ready && ok) {
-                int n = tile * 128 + q * 32 + lane;
-                for (int col = 0; col < p.bn; col += 16) {
-                    float v[16];
-                    tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+            const int n = tile * 128 + q * 32 + lane;
+            const bool good = ready && ok;
+            if (p.epilogue == EPI_SWIGLU) {
+                // Kernels.SwiGlu (reference src/Jevstral/Numerics/Kernels.cs:82-89):
+                // up <- g*u; s <- 1/(1+exp(-g)); y <- s*up. Up rows (lanes 64-127) go through
+                // the stage memory, free now that every MMA has completed.
+                float* ubuf = (float*)sm;  // [bn][64]
+                if (good && q >= 2)
+                    for (int col = 0; col < p.bn; col += 16) {
+                        float v[16];
+                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        int t = t0 + col + j;
-                        if (t < p.T) {
-                            float* dst = p.y + (int64_t)t * p.ldy + n;
-                            if (p.epilogue == EPI_ADD)
-                                *dst = __fadd_rn(*dst, v[j]);
-                            else
-                                *dst = v[j];
+                        for (int j = 0; j < 16; j++) ubuf[(col + j) * 64 + (q - 2) * 32 + lane] = v[j];
+                    }
+                epi_bar();
+                if (good && q < 2) {
+                    const int jf = tile * 64 + q * 32 + lane;  // FFN feature
+                    for (int col = 0; col < p.bn; col += 16) {
+                        float g[16];
+                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, g);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            int t = t0 + col + j;
+                            float u = ubuf[(col + j) * 64 + q * 32 + lane];
+                            float up = __fmul_rn(g[j], u);
+                            float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[j])));
+                            if (t < p.T) p.xs_out[kslab_offset(t, jf, p.tpad)] = __float2half_rn(__fmul_rn(sg, up));
                         }
                     }
                 }
-            } else if (!ready) {
-                atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            } else if (p.splits == 1) {
+                if (good) {
+                    for (int col = 0; col < p.bn; col += 16) {
+                        float v[16];
+                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            int t = t0 + col + j;
+                            if (t < p.T) {
+                                float* dst = p.y + (int64_t)t * p.ldy + n;
+                                if (p.epilogue == EPI_ADD)
+                                    *dst = __fadd_rn(*dst, v[j]);
+                                else
+                                    *dst = v[j];
+                            }
+                        }
+                    }
+                }
+            } else {
+                // Both K halves publish their partial; the CTA that arrives last adds the other
+                // half to its own (still in TMEM): p0 + p1, which is the same value whichever
+                // CTA that is (IEEE addition commutes).
+                float* mine = p.ws + (int64_t)blockIdx.z * p.T * p.ldy;
+                const float* other = p.ws + (int64_t)(1 - blockIdx.z) * p.T * p.ldy;
+                if (good) {
+                    for (int col = 0; col < p.bn; col += 16) {
+                        float v[16];
+                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            int t = t0 + col + j;
+                            if (t < p.T) mine[(int64_t)t * p.ldy + n] = v[j];
+                        }
+                    }
+                }
+                __threadfence();
+                epi_bar();
+                if (warp == 4 && lane == 0) {
+                    int* ctr = p.counters + blockIdx.x * gridDim.y + blockIdx.y;
+                    int old = atomicAdd(ctr, 1);
+                    int last = old == p.splits - 1;
+                    if (last) atomicExch(ctr, 0);
+                    *last_flag = last;
+                }
+                epi_bar();
+                if (*last_flag && good) {
+                    __threadfence();
+                    for (int col = 0; col < p.bn; col += 16) {
+                        float v[16], o[16], yv[16];
+                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            int t = t0 + col + j;
+                            o[j] = t < p.T ? __ldcg(other + (int64_t)t * p.ldy + n) : 0.f;
+                            yv[j] = (t < p.T && p.epilogue == EPI_ADD) ? p.y[(int64_t)t * p.ldy + n] : 0.f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            int t = t0 + col + j;
+                            if (t < p.T) {
+                                float s = __fadd_rn(v[j], o[j]);
+                                p.y[(int64_t)t * p.ldy + n] = p.epilogue == EPI_ADD ? __fadd_rn(yv[j], s) : s;
+                            }
+                        }
+                    }
+                }
             }
+            if (!ready) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
         }
     }
     tc_fence_before();
@@ -346,9 +437,13 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.bn = a.bn;
     p.ldy = a.ldy;
     p.epilogue = a.epilogue;
+    p.splits = a.splits;
+    p.xs_out = a.xs_out;
+    p.ws = a.ws;
+    p.counters = a.counters;
     int cb = chunk_bytes(TYPE);
     size_t per_stage = 16384 + (size_t)a.bn * 128 + cb;
-    p.stages = (per_stage * 4 + 2048 <= 200 * 1024) ? 4 : 3;
+    p.stages = (per_stage * 4 + 3072 <= 225 * 1024) ? 4 : 3;
     int nc = 32;
     while (nc < a.bn) nc <<= 1;
     p.ncols = nc;
@@ -361,14 +456,24 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
         JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         configured = (int)smem;
     }
-    dim3 grid(w.tiles, a.tpad / a.bn);
+    dim3 grid(w.tiles, a.tpad / a.bn, a.splits);
     k_gemm_tc<TYPE><<<grid, GEMM_THREADS, smem, s>>>(p);
     note_launch();
+}
+
+int gemm_splits_for(const QWeight& w) {
+    // Few row tiles and a long K (the 3072-row O and down projections): two K halves, so
+    // the product fills the GPU. A property of the matrix, never of the token count.
+    return (w.tiles <= 32 && w.ksteps >= 64 && w.ksteps % 2 == 0) ? 2 : 1;
 }
 
 void launch_gemm(const GemmArgs& a, cudaStream_t s) {
     if (a.bn % 16 != 0 || a.bn < 16 || a.bn > 256 || a.tpad % a.bn != 0)
         throw Error(JV_ERR_ARG, "gemm: token tile must be a multiple of 16 in [16, 256] dividing the padded rows");
+    if (a.splits < 1 || a.splits > 2 || a.w->ksteps % a.splits != 0 || (a.splits > 1 && (!a.ws || !a.counters)))
+        throw Error(JV_ERR_ARG, "gemm: bad split-K arguments");
+    if (a.epilogue == EPI_SWIGLU && (a.splits != 1 || !a.xs_out))
+        throw Error(JV_ERR_ARG, "gemm: the SwiGLU epilogue needs an unsplit product and an output slab");
     switch (a.w->type) {
         case T_Q8_0: launch_tc_typed<T_Q8_0>(a, s); break;
         case T_Q4_0: launch_tc_typed<T_Q4_0>(a, s); break;

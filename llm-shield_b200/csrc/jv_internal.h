@@ -70,7 +70,9 @@ __host__ __device__ inline size_t kslab_offset(int t, int k, int tpad) {
 
 // ------------------------------------------------------------ GEMM plans
 
-enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1 };
+// EPI_SWIGLU: the fused gate/up matrix (each 128-row tile = 64 gate rows then the 64 matching
+// up rows) -> silu(gate) * up written as the fp16 K-slab operand of the down projection.
+enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
 
 struct GemmArgs {
     const QWeight* w;
@@ -80,7 +82,12 @@ struct GemmArgs {
     int ldy;
     int epilogue;
     int* err;          // device error word (JV_ERR_DEVICE_TIMEOUT on a bounded-wait timeout)
+    __half* xs_out = nullptr;  // EPI_SWIGLU: K-slab [ff/64][tpad][64] of the activation
+    int splits = 1;    // K splits (gemm_splits_for); > 1 needs ws and counters
+    float* ws = nullptr;       // [splits][T][ldy] fp32 partials
+    int* counters = nullptr;   // [tiles][tpad/bn], zero between launches
 };
+int gemm_splits_for(const QWeight& w);
 
 // Token tile for a GEMM over T tokens: balanced tiles of at most 256 (the MMA's N limit),
 // multiples of 16. Depends on T only, never on which tokens they are; the K order of the

@@ -177,6 +177,8 @@ struct jv_ctx {
     DevVec<float> h, qkv32, gu32, tmp32, q32, ctx32, x32, act32, k32, partial, out32, logits, cap32;
     DevVec<__half> xs, xs_ff, ctx16, q16;
     DevVec<int32_t> in_i32, out_i32;
+    DevVec<float> gemm_ws;   // split-K partials
+    DevVec<int> gemm_ctr;    // split-K arrival counters (the last CTA of a tile resets its own)
     DevVec<AttnItem> items;
     int* d_err = nullptr;
     HostVec<int32_t> h_in;
@@ -574,6 +576,7 @@ void sync_check(jv_ctx* x) {
     int e = *x->h_err.p;
     if (e != 0) {
         JV_CUDA(cudaMemsetAsync(x->d_err, 0, sizeof(int), x->stream));
+        if (x->gemm_ctr.p) JV_CUDA(cudaMemsetAsync(x->gemm_ctr.p, 0, x->gemm_ctr.cap * sizeof(int), x->stream));
         JV_CUDA(cudaStreamSynchronize(x->stream));
         if (e == JV_ERR_DEVICE_TIMEOUT)
             throw Error(JV_ERR_DEVICE_TIMEOUT, "a device-side wait timed out in a tensor-core GEMM");
@@ -599,8 +602,17 @@ void observe_kslab(jv_ctx* x, const std::string& name, const __half* xs, int T, 
     observe(x, name, tmp, T, K);
 }
 
-void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float* y, int ldy, int epi) {
+void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float* y, int ldy, int epi,
+          __half* xs_out = nullptr) {
+    static const bool use_ref = getenv("JV_GEMM_REFERENCE") != nullptr;
+    if (epi == EPI_SWIGLU && use_ref) {  // the CUDA-core check product has no fused epilogue
+        float* gu = x->gu32.get((size_t)T * w.rows);
+        gemm(x, w, xs, T, tpad, gu, w.rows, EPI_STORE);
+        launch_swiglu(gu, T, w.rows / 2, xs_out, tpad, nullptr, x->stream);
+        return;
+    }
     GemmArgs a;
+    a.xs_out = xs_out;
     a.w = &w;
     a.x = xs;
     a.T = T;
@@ -610,7 +622,11 @@ void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float*
     a.ldy = ldy;
     a.epilogue = epi;
     a.err = x->d_err;
-    static const bool use_ref = getenv("JV_GEMM_REFERENCE") != nullptr;
+    a.splits = epi == EPI_SWIGLU ? 1 : gemm_splits_for(w);
+    if (a.splits > 1) {
+        a.ws = x->gemm_ws.get((size_t)a.splits * T * ldy);
+        a.counters = x->gemm_ctr.get((size_t)w.tiles * (tpad / a.bn));
+    }
     ProfScope ps(x, JV_PROF_GEMM, 2.0 * T * w.rows * w.cols,
                  weight_bytes(w) + 2.0 * T * w.cols + (epi == EPI_ADD ? 8.0 : 4.0) * T * w.rows);
     if (use_ref)
@@ -872,10 +888,8 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         observe(x, p + "post_attn", h, T, hidden);
         launch_rmsnorm(h, W.ffn_norm, T, hidden, c.eps, xs, tpad, nullptr, s);
         observe_kslab(x, p + "ffn_norm", xs, T, hidden, tpad);
-        float* gu = x->gu32.get((size_t)T * 2 * ff);
-        gemm(x, W.gu, xs, T, tpad, gu, 2 * ff, EPI_STORE);
         __half* xf = x->xs_ff.get((size_t)tpad * ff);
-        launch_swiglu(gu, T, ff, xf, tpad, nullptr, s);
+        gemm(x, W.gu, xs, T, tpad, nullptr, 2 * ff, EPI_SWIGLU, xf);
         if (capture) {
             float* fo = x->out32.get((size_t)T * hidden);
             gemm(x, W.down, xf, T, tpad, fo, hidden, EPI_STORE);
@@ -1081,6 +1095,8 @@ void jv_ctx_destroy(jv_ctx* x) {
                     &x->out32, &x->logits, &x->cap32})
         v->release();
     x->xs.release();
+    x->gemm_ws.release();
+    x->gemm_ctr.release();
     x->xs_ff.release();
     x->ctx16.release();
     x->q16.release();
