@@ -282,4 +282,4 @@ def test_kernel_launches_are_counted(small):
     before = jv.kernel_launches()
     with ctx(small) as c:
         c.forward_tree([1, 1500, 2500], [[3000, 4000], [5000]], VERDICT_ROWS)
-    assert jv.kernel_launches() - before > 10 * SMALL_CFG.layers
+    assert jv.kernel_launches() - before >= 7 * SMALL_CFG.layers
