@@ -3,35 +3,42 @@
 // Y[t, n] (+)= sum_k X[t, k] * W[n, k]: the reference's PanelGemm (src/Jevstral/Numerics/
 // PanelGemm.cs:76-300), with W still in its GGUF quantization in HBM.
 //
-// Operands are swapped so the weights are the MMA's M side: a CTA owns 128 weight rows
-// (TMEM lanes) and a tile of BN tokens (TMEM columns, BN <= 256), and walks K in steps of
-// 64 in ascending order. Per k step:
-//   * warp 0 (one lane) bulk-copies the raw quant chunk of its 128 rows (one contiguous
-//     re-tiled chunk, see jv_internal.h) and the BN x 64 fp16 activation tile (one
-//     contiguous run of the pre-swizzled K-slab layout) into shared memory, completing
-//     on an mbarrier with a transaction count;
-//   * warps 4-11 decode the chunk to fp16 (d*q, d*(n-8), d*q5+m in fp32, rounded once to
-//     fp16) straight into the UMMA K-major SWIZZLE_128B layout;
-//   * warp 1 (one lane) issues four tcgen05.mma kind::f16 (K = 16 each) into the fp32
-//     TMEM accumulator and commits to the stage's "empty" mbarrier.
-// After the last k step warps 4-7 read the accumulator with tcgen05.ld and store (or add
-// into) Y; lanes are weight rows, so every store instruction writes 32 consecutive floats.
+// Operands are swapped so the weights are the MMA's M side: a work unit is 128 weight rows
+// (TMEM lanes) x a tile of BN tokens (TMEM columns, BN <= 256) x a contiguous range of k
+// steps of 64, walked in ascending order. The kernel is persistent: one CTA per SM takes
+// units round-robin, and its warps run decoupled pipelines across unit boundaries:
+//   * warp 0, lane 0 — bulk-copies each k step's raw quant chunk (one contiguous re-tiled
+//     chunk of 128 rows x 64 columns, see jv_internal.h) into a deep ring, and the BN x 64
+//     fp16 activation tile (one contiguous run of the pre-swizzled K-slab layout) into a
+//     second ring, each completing on an mbarrier with a transaction count;
+//   * warps 8-15 — decode a raw chunk to fp16 in registers, hand its ring slot back at
+//     once, and store the values into a decoded-weight slot in the UMMA K-major
+//     SWIZZLE_128B layout;
+//   * warp 1, lane 0 — issues four tcgen05.mma kind::f16 (K = 16) per k step into one of
+//     two fp32 TMEM accumulators and commits to free the activation and decoded slots;
+//   * warps 4-7 — drain the other accumulator with tcgen05.ld while the next unit
+//     accumulates: store, add into Y, fused SwiGLU, or the split-K combine.
+// Raw chunks are freed by the decoders, not by the tensor core, so the weight stream runs
+// many steps ahead; only the fp16 activation ring and the decoded slots follow the MMA.
 //
-// Batch invariance: each output is one accumulation chain over K in a fixed order, with
-// no split of K, and the tensor core computes an element from its own row and column
-// only. A token's result therefore does not depend on BN, on its column in the tile or on
-// the other tokens of the call (the property of PanelGemmTests.cs:61-74).
+// Batch invariance: each output is one accumulation chain over K in a fixed order; the
+// only K split is fixed per weight matrix (gemm_splits_for), never by the token count; the
+// tensor core computes an element from its own row and column only. A token's result
+// therefore does not depend on BN, its column in the tile, or the other tokens of the call
+// (the property of PanelGemmTests.cs:61-74).
 //
-// Every mbarrier wait is bounded (about two seconds of %globaltimer); on expiry the thread
-// sets the error word, the producer waits (bounded) for its copies in flight, the MMA lane
-// still commits so the accumulator is quiescent, and the CTA frees its TMEM and returns.
-// No cluster launch and no multicast: nothing here reads another GPU's memory.
+// Every mbarrier wait is bounded (about two seconds of %globaltimer). On expiry the thread
+// sets the error word and its role stops; the others then time out in turn; the producer
+// waits (bounded) for its copies in flight, the MMA lane drains its own MMAs, and the CTA
+// frees its TMEM and returns. No cluster launch and no multicast: nothing here reads another
+// GPU's memory.
 #include "jv_internal.h"
 
 namespace jv {
 
-constexpr int GEMM_THREADS = 384;
+constexpr int GEMM_THREADS = 512;
 constexpr int DEC_THREADS = 256;
+constexpr int DEC_WARP0 = 8;
 constexpr uint64_t WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t s_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -195,195 +202,231 @@ struct TcParams {
     __half* xs_out;   // EPI_SWIGLU destination (K-slab, tpad rows)
     float* ws;        // split-K partials [split][T][ldy] (splits > 1)
     int* counters;    // one arrival counter per (row tile, token tile); zero between launches
-    int ksteps, T, tpad, bn, ldy, epilogue, stages, ncols, splits;
-    int raw_off, b_off, bar_off;  // byte offsets inside the 1024-aligned dynamic smem
+    int ksteps, T, tpad, bn, ldy, epilogue, ncols, splits;
+    int tiles, ttiles, units;   // work units = tiles x ttiles x splits
+    int nr, nb, na;             // ring depths: raw chunks, activation tiles, decoded tiles
+    int raw_off, b_off, bar_off;  // byte offsets inside the 1024-aligned dynamic smem (A at 0)
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
+// Work unit u -> (row tile, token tile, K split), token tiles and splits of one row tile
+// adjacent so concurrently running CTAs share each weight chunk through L2.
+__device__ __forceinline__ void unit_coords(const TcParams& p, int u, int& tile, int& tt, int& sp) {
+    sp = u % p.splits;
+    int r = u / p.splits;
+    tt = r % p.ttiles;
+    tile = r / p.ttiles;
+}
 
 template <int TYPE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     extern __shared__ uint8_t gsm_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
-    const int S = p.stages;
     const int cb = chunk_bytes(TYPE);
-    uint8_t* As = sm;                       // S x 16 KB
-    uint8_t* Bs = sm + p.b_off;             // S x bn*128
-    uint8_t* Rs = sm + p.raw_off;           // S x chunk
+    const int NR = p.nr, NB = p.nb, NA = p.na;
+    uint8_t* As = sm;               // NA x 16 KB decoded weights
+    uint8_t* Bs = sm + p.b_off;     // NB x bn*128 activations
+    uint8_t* Rs = sm + p.raw_off;   // NR x chunk raw quant blocks
     uint64_t* bars = (uint64_t*)(sm + p.bar_off);
-    uint32_t* tslot = (uint32_t*)(bars + 3 * S + 1);
+    const uint32_t raw_full = s_addr(bars), raw_empty = raw_full + 8 * NR;
+    const uint32_t b_full = raw_empty + 8 * NR, b_empty = b_full + 8 * NB;
+    const uint32_t a_full = b_empty + 8 * NB, a_empty = a_full + 8 * NA;
+    const uint32_t acc_full = a_empty + 8 * NA, acc_empty = acc_full + 16, drained = acc_empty + 16;
+    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 2 * NB + 2 * NA + 5);
     volatile int* last_flag = (volatile int*)(tslot + 1);
-    const uint32_t full0 = s_addr(bars), dec0 = s_addr(bars + S), empty0 = s_addr(bars + 2 * S), accf = s_addr(bars + 3 * S);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile = blockIdx.x, t0 = blockIdx.y * p.bn;
-    // Split-K: this CTA's contiguous share of the k steps. The split is fixed by the weight
-    // shape (host side), never by the token count, so it cannot break batch invariance.
-    const int nks = p.ksteps / p.splits, kbase = blockIdx.z * nks;
+    const int nks = p.ksteps / p.splits;      // k steps per unit
+    const uint32_t bbytes = (uint32_t)p.bn * 128u;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) {
-            mbar_init(full0 + 8 * s, 1);
-            mbar_init(dec0 + 8 * s, DEC_THREADS);
-            mbar_init(empty0 + 8 * s, 1);
-        }
-        mbar_init(accf, 1);
+        for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_THREADS); }
+        for (int i = 0; i < NB; i++) { mbar_init(b_full + 8 * i, 1); mbar_init(b_empty + 8 * i, 1); }
+        for (int i = 0; i < NA; i++) { mbar_init(a_full + 8 * i, DEC_THREADS); mbar_init(a_empty + 8 * i, 1); }
+        for (int i = 0; i < 2; i++) { mbar_init(acc_full + 8 * i, 1); mbar_init(acc_empty + 8 * i, 128); }
+        mbar_init(drained, 1);
         fence_barrier_init();
     }
-    if (warp == 2) tmem_alloc(s_addr(tslot), p.ncols);
+    if (warp == 2) tmem_alloc(s_addr(tslot), 2 * p.ncols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
     if (warp == 0) {
-        if (lane == 0) {
-            int issued = 0;
+        if (lane == 0) {  // ---------------------------------------------- producer
+            int64_t g = 0;
             bool ok = true;
-            const uint8_t* wsrc = p.w + ((int64_t)tile * p.ksteps + kbase) * cb;
-            const uint32_t bbytes = (uint32_t)p.bn * 128u;
-            for (int ks = 0; ks < nks; ks++) {
-                int s = ks % S;
-                uint32_t ph = (uint32_t)(ks / S) & 1u;
-                if (!mbar_wait(empty0 + 8 * s, ph ^ 1u)) { ok = false; break; }
-                mbar_expect_tx(full0 + 8 * s, (uint32_t)cb + bbytes);
-                bulk_g2s(s_addr(Rs + s * cb), wsrc + (int64_t)ks * cb, (uint32_t)cb, full0 + 8 * s);
-                bulk_g2s(s_addr(Bs + (size_t)s * bbytes), p.x + ((int64_t)(kbase + ks) * p.tpad + t0) * 64, bbytes,
-                         full0 + 8 * s);
-                issued++;
+            int64_t issued_r = 0, issued_b = 0;
+            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+                int tile, tt, sp;
+                unit_coords(p, u, tile, tt, sp);
+                const int kb = sp * nks, t0 = tt * p.bn;
+                const uint8_t* wsrc = p.w + ((int64_t)tile * p.ksteps + kb) * cb;
+                for (int ks = 0; ks < nks; ks++, g++) {
+                    int ri = (int)(g % NR), bi = (int)(g % NB);
+                    if (!mbar_wait(raw_empty + 8 * ri, (uint32_t)((g / NR) & 1) ^ 1u)) { ok = false; break; }
+                    mbar_expect_tx(raw_full + 8 * ri, (uint32_t)cb);
+                    bulk_g2s(s_addr(Rs + ri * cb), wsrc + (int64_t)ks * cb, (uint32_t)cb, raw_full + 8 * ri);
+                    issued_r = g + 1;
+                    if (!mbar_wait(b_empty + 8 * bi, (uint32_t)((g / NB) & 1) ^ 1u)) { ok = false; break; }
+                    mbar_expect_tx(b_full + 8 * bi, bbytes);
+                    bulk_g2s(s_addr(Bs + (size_t)bi * bbytes), p.x + ((int64_t)(kb + ks) * p.tpad + t0) * 64, bbytes,
+                             b_full + 8 * bi);
+                    issued_b = g + 1;
+                }
             }
             if (!ok) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
             // Never leave with copies in flight into this CTA's shared memory.
-            for (int i = issued - 1; i >= 0 && i >= issued - S; i--)
-                if (!mbar_wait(full0 + 8 * (i % S), (uint32_t)(i / S) & 1u)) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            for (int64_t i = issued_r - 1; i >= 0 && i >= issued_r - NR; i--)
+                if (!mbar_wait(raw_full + 8 * (int)(i % NR), (uint32_t)((i / NR) & 1))) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            for (int64_t i = issued_b - 1; i >= 0 && i >= issued_b - NB; i--)
+                if (!mbar_wait(b_full + 8 * (int)(i % NB), (uint32_t)((i / NB) & 1))) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0) {  // --------------------------------------------- MMA issue
             const uint32_t idesc = idesc_f16(p.bn, 128);
-            const uint32_t bbytes = (uint32_t)p.bn * 128u;
-            for (int ks = 0; ks < nks; ks++) {
-                int s = ks % S;
-                uint32_t ph = (uint32_t)(ks / S) & 1u;
-                if (!mbar_wait(full0 + 8 * s, ph) || !mbar_wait(dec0 + 8 * s, ph)) {
-                    atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
-                    break;
-                }
+            int64_t g = 0;
+            bool ok = true;
+            int i = 0;
+            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, i++) {
+                const int ab = i & 1;
+                if (!mbar_wait(acc_empty + 8 * ab, (uint32_t)((i >> 1) & 1) ^ 1u)) { ok = false; break; }
                 tc_fence_after();
-                uint32_t a_base = s_addr(As + s * 16384), b_base = s_addr(Bs + (size_t)s * bbytes);
+                const uint32_t acc = tmem + (uint32_t)(ab * p.ncols);
+                for (int ks = 0; ks < nks; ks++, g++) {
+                    int ai = (int)(g % NA), bi = (int)(g % NB);
+                    if (!mbar_wait(a_full + 8 * ai, (uint32_t)((g / NA) & 1)) ||
+                        !mbar_wait(b_full + 8 * bi, (uint32_t)((g / NB) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t a_base = s_addr(As + ai * 16384), b_base = s_addr(Bs + (size_t)bi * bbytes);
 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    umma(tmem, sdesc(a_base + 32 * j), sdesc(b_base + 32 * j), idesc, (ks > 0 || j > 0) ? 1u : 0u);
-                umma_commit(empty0 + 8 * s);
+                    for (int j = 0; j < 4; j++)
+                        umma(acc, sdesc(a_base + 32 * j), sdesc(b_base + 32 * j), idesc, (ks > 0 || j > 0) ? 1u : 0u);
+                    umma_commit(a_empty + 8 * ai);
+                    umma_commit(b_empty + 8 * bi);
+                }
+                if (ok) umma_commit(acc_full + 8 * ab);
             }
-            umma_commit(accf);  // always: the epilogue and teardown wait for a quiescent accumulator
+            if (!ok) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            // Wait until every MMA this lane issued has completed before teardown.
+            umma_commit(drained);
+            if (!mbar_wait(drained, 0)) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
         }
-    } else if (warp >= 4) {
+    } else if (warp >= DEC_WARP0) {  // --------------------------------------- decode
         // Thread dt decodes chunk c = dt % 8 of rows r0 + 32*it (it = 0..3); the swizzled
         // position of that chunk is the same for all four rows.
-        const int dt = threadIdx.x - 128;
+        const int dt = threadIdx.x - DEC_WARP0 * 32;
         const int c = dt & 7, r0 = dt >> 3;
         const int a_off = r0 * 128 + ((c ^ (r0 & 7)) << 4);
+        int64_t g = 0;
         bool ok = true;
-        for (int ks = 0; ks < nks; ks++) {
-            int s = ks % S;
-            uint32_t ph = (uint32_t)(ks / S) & 1u;
-            if (!mbar_wait(full0 + 8 * s, ph)) { ok = false; break; }
-            const uint8_t* raw = Rs + s * cb;
-            uint8_t* A = As + s * 16384 + a_off;
-            uint4 v[4];
+        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+            for (int ks = 0; ks < nks; ks++, g++) {
+                int ri = (int)(g % NR), ai = (int)(g % NA);
+                if (!mbar_wait(raw_full + 8 * ri, (uint32_t)((g / NR) & 1))) { ok = false; break; }
+                const uint8_t* raw = Rs + ri * cb;
+                uint4 v[4];
 #pragma unroll
-            for (int it = 0; it < 4; it++) v[it] = decode8<TYPE>(raw, r0 + 32 * it, c);
+                for (int it = 0; it < 4; it++) v[it] = decode8<TYPE>(raw, r0 + 32 * it, c);
+                mbar_arrive(raw_empty + 8 * ri);
+                if (!mbar_wait(a_empty + 8 * ai, (uint32_t)((g / NA) & 1) ^ 1u)) { ok = false; break; }
+                uint8_t* A = As + ai * 16384 + a_off;
 #pragma unroll
-            for (int it = 0; it < 4; it++) *(uint4*)(A + it * 32 * 128) = v[it];
-            fence_proxy_async();
-            mbar_arrive(dec0 + 8 * s);
+                for (int it = 0; it < 4; it++) *(uint4*)(A + it * 32 * 128) = v[it];
+                fence_proxy_async();
+                mbar_arrive(a_full + 8 * ai);
+            }
         }
         if (!ok) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
-        if (warp < 8) {
-            // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows of this tile.
-            int q = warp & 3;
-            bool ready = mbar_wait(accf, 0);
+    } else if (warp >= 4) {  // ------------------------------------------------- epilogue
+        // Warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows of the unit's tile.
+        const int q = warp & 3;
+        int i = 0;
+        for (int u = blockIdx.x; u < p.units; u += gridDim.x, i++) {
+            int tile, tt, sp;
+            unit_coords(p, u, tile, tt, sp);
+            const int t0 = tt * p.bn, ab = i & 1;
+            const bool ready = mbar_wait(acc_full + 8 * ab, (uint32_t)((i >> 1) & 1));
             tc_fence_after();
+            if (!ready) {
+                atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+                break;
+            }
+            const uint32_t tacc = tmem + (uint32_t)(ab * p.ncols) + ((uint32_t)(q * 32) << 16);
             const int n = tile * 128 + q * 32 + lane;
-            const bool good = ready && ok;
             if (p.epilogue == EPI_SWIGLU) {
-                // Kernels.SwiGlu (reference src/Jevstral/Numerics/Kernels.cs:82-89):
-                // up <- g*u; s <- 1/(1+exp(-g)); y <- s*up. Up rows (lanes 64-127) go through
-                // the stage memory, free now that every MMA has completed.
-                float* ubuf = (float*)sm;  // [bn][64]
-                if (good && q >= 2)
-                    for (int col = 0; col < p.bn; col += 16) {
-                        float v[16];
-                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+                // Kernels.SwiGlu (reference src/Jevstral/Numerics/Kernels.cs:82-89): up <- g*u;
+                // s <- 1/(1+exp(-g)); y <- s*up. In each warp, lanes 0-15 hold gate rows and
+                // lanes 16-31 the matching up rows; one shuffle pairs them, and lane l < 16
+                // writes columns 0-7 of a chunk, lane l + 16 columns 8-15.
+                const int jf = tile * 64 + q * 16 + (lane & 15);
+                const bool hi = lane >= 16;
+                for (int col = 0; col < p.bn; col += 16) {
+                    float v[16], o[16];
+                    tmem_ld16(tacc + (uint32_t)col, v);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) ubuf[(col + j) * 64 + (q - 2) * 32 + lane] = v[j];
-                    }
-                epi_bar();
-                if (good && q < 2) {
-                    const int jf = tile * 64 + q * 32 + lane;  // FFN feature
-                    for (int col = 0; col < p.bn; col += 16) {
-                        float g[16];
-                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, g);
+                    for (int j = 0; j < 16; j++) o[j] = __shfl_xor_sync(0xffffffffu, v[j], 16);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            int t = t0 + col + j;
-                            float u = ubuf[(col + j) * 64 + q * 32 + lane];
-                            float up = __fmul_rn(g[j], u);
-                            float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g[j])));
-                            if (t < p.T) p.xs_out[kslab_offset(t, jf, p.tpad)] = __float2half_rn(__fmul_rn(sg, up));
-                        }
+                    for (int j = 0; j < 8; j++) {
+                        const int jj = hi ? j + 8 : j;
+                        const float gg = hi ? o[jj] : v[jj];
+                        const float uu = hi ? v[jj] : o[jj];
+                        const int t = t0 + col + jj;
+                        const float up = __fmul_rn(gg, uu);
+                        const float sg = __frcp_rn(__fadd_rn(1.0f, expf(-gg)));
+                        if (t < p.T) p.xs_out[kslab_offset(t, jf, p.tpad)] = __float2half_rn(__fmul_rn(sg, up));
                     }
                 }
             } else if (p.splits == 1) {
-                if (good) {
-                    for (int col = 0; col < p.bn; col += 16) {
-                        float v[16];
-                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+                for (int col = 0; col < p.bn; col += 16) {
+                    float v[16];
+                    tmem_ld16(tacc + (uint32_t)col, v);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            int t = t0 + col + j;
-                            if (t < p.T) {
-                                float* dst = p.y + (int64_t)t * p.ldy + n;
-                                if (p.epilogue == EPI_ADD)
-                                    *dst = __fadd_rn(*dst, v[j]);
-                                else
-                                    *dst = v[j];
-                            }
+                    for (int j = 0; j < 16; j++) {
+                        int t = t0 + col + j;
+                        if (t < p.T) {
+                            float* dst = p.y + (int64_t)t * p.ldy + n;
+                            *dst = p.epilogue == EPI_ADD ? __fadd_rn(*dst, v[j]) : v[j];
                         }
                     }
                 }
             } else {
-                // Both K halves publish their partial; the CTA that arrives last adds the other
-                // half to its own (still in TMEM): p0 + p1, which is the same value whichever
-                // CTA that is (IEEE addition commutes).
-                float* mine = p.ws + (int64_t)blockIdx.z * p.T * p.ldy;
-                const float* other = p.ws + (int64_t)(1 - blockIdx.z) * p.T * p.ldy;
-                if (good) {
-                    for (int col = 0; col < p.bn; col += 16) {
-                        float v[16];
-                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+                // Both K halves publish their partial; the unit that finishes last adds the
+                // other half to its own (still in TMEM): p0 + p1, the same value whichever
+                // unit that is (IEEE addition commutes).
+                float* mine = p.ws + (int64_t)sp * p.T * p.ldy;
+                const float* other = p.ws + (int64_t)(1 - sp) * p.T * p.ldy;
+                for (int col = 0; col < p.bn; col += 16) {
+                    float v[16];
+                    tmem_ld16(tacc + (uint32_t)col, v);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            int t = t0 + col + j;
-                            if (t < p.T) mine[(int64_t)t * p.ldy + n] = v[j];
-                        }
+                    for (int j = 0; j < 16; j++) {
+                        int t = t0 + col + j;
+                        if (t < p.T) mine[(int64_t)t * p.ldy + n] = v[j];
                     }
                 }
                 __threadfence();
                 epi_bar();
                 if (warp == 4 && lane == 0) {
-                    int* ctr = p.counters + blockIdx.x * gridDim.y + blockIdx.y;
+                    int* ctr = p.counters + tile * p.ttiles + tt;
                     int old = atomicAdd(ctr, 1);
                     int last = old == p.splits - 1;
                     if (last) atomicExch(ctr, 0);
                     *last_flag = last;
                 }
                 epi_bar();
-                if (*last_flag && good) {
+                const bool last = *last_flag != 0;
+                epi_bar();  // the flag is re-used by the next unit
+                if (last) {
                     __threadfence();
                     for (int col = 0; col < p.bn; col += 16) {
                         float v[16], o[16], yv[16];
-                        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+                        tmem_ld16(tacc + (uint32_t)col, v);
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
                             int t = t0 + col + j;
@@ -401,14 +444,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                     }
                 }
             }
-            if (!ready) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            tc_fence_before();
+            mbar_arrive(acc_empty + 8 * ab);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem, p.ncols);
+        tmem_dealloc(tmem, 2 * p.ncols);
     }
 }
 
@@ -423,6 +467,8 @@ int gemm_tpad_for(int T) {
     return (T + bn - 1) / bn * bn;
 }
 
+static int g_sm_count = 0;
+
 template <int TYPE>
 static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     const QWeight& w = *a.w;
@@ -431,6 +477,9 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.x = a.x;
     p.y = a.y;
     p.err = a.err;
+    p.xs_out = a.xs_out;
+    p.ws = a.ws;
+    p.counters = a.counters;
     p.ksteps = w.ksteps;
     p.T = a.T;
     p.tpad = a.tpad;
@@ -438,25 +487,33 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.ldy = a.ldy;
     p.epilogue = a.epilogue;
     p.splits = a.splits;
-    p.xs_out = a.xs_out;
-    p.ws = a.ws;
-    p.counters = a.counters;
-    int cb = chunk_bytes(TYPE);
-    size_t per_stage = 16384 + (size_t)a.bn * 128 + cb;
-    p.stages = (per_stage * 4 + 3072 <= 225 * 1024) ? 4 : 3;
+    p.tiles = w.tiles;
+    p.ttiles = a.tpad / a.bn;
+    p.units = p.tiles * p.ttiles * p.splits;
+    const int cb = chunk_bytes(TYPE);
     int nc = 32;
     while (nc < a.bn) nc <<= 1;
     p.ncols = nc;
-    p.b_off = 16384 * p.stages;
-    p.raw_off = p.b_off + a.bn * 128 * p.stages;
-    p.bar_off = (p.raw_off + cb * p.stages + 15) & ~15;
-    size_t smem = (size_t)p.bar_off + 8 * (3 * p.stages + 1) + 16 + 1024;
-    static int configured = 0;
-    if (configured < (int)smem) {
-        JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        configured = (int)smem;
+    // Ring depths within ~220 KB: 3 decoded slots, 4 activation tiles (3 if they do not fit),
+    // and as many raw chunks (up to 12) as the rest allows.
+    const size_t budget = 220 * 1024;
+    p.na = 3;
+    p.nb = 4;
+    if (16384 * 3 + (size_t)a.bn * 128 * 4 + 4 * cb > budget) p.nb = 3;
+    size_t used = 16384 * (size_t)p.na + (size_t)a.bn * 128 * p.nb;
+    p.nr = (int)std::min<size_t>(12, (budget - used) / cb);
+    if (p.nr < 2) throw Error(JV_ERR_ARG, "gemm: shared memory budget exceeded");
+    p.b_off = 16384 * p.na;
+    p.raw_off = p.b_off + a.bn * 128 * p.nb;
+    p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
+    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 2 * p.nb + 2 * p.na + 5) + 16 + 1024;
+    JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (g_sm_count == 0) {
+        int dev = 0;
+        JV_CUDA(cudaGetDevice(&dev));
+        JV_CUDA(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
     }
-    dim3 grid(w.tiles, a.tpad / a.bn, a.splits);
+    int grid = std::min(p.units, g_sm_count);
     k_gemm_tc<TYPE><<<grid, GEMM_THREADS, smem, s>>>(p);
     note_launch();
 }
@@ -485,8 +542,8 @@ void launch_gemm(const GemmArgs& a, cudaStream_t s) {
 // ------------------------------------------------------- reference GEMM
 
 // A plain CUDA-core product over the *same* fp16 operands (weights decoded and rounded to
-// fp16 exactly as the tensor-core producer does). Used only by the library's self-test
-// entry point to check the tcgen05 kernel at full shapes; never on the forward path.
+// fp16 exactly as the tensor-core producer does). Selected only by the JV_GEMM_REFERENCE
+// environment variable, to check the tcgen05 kernel at full shapes; never the default path.
 template <int TYPE>
 __global__ void k_gemm_ref(const uint8_t* __restrict__ w, int ksteps, const __half* __restrict__ x, int T, int tpad,
                            float* __restrict__ y, int ldy, int epilogue) {

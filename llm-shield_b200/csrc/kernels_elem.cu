@@ -157,14 +157,15 @@ void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
 // ---------------------------------------------------------------- SwiGLU
 
 // Kernels.SwiGlu (Kernels.cs:82-89): up <- g*u; dst <- 1/(1+exp(-g)); dst <- dst*up.
-// gu holds the fused gate/up GEMM output: row tile i carries gate rows 64i..64i+63 in
-// columns 128i..128i+63 and the matching up rows in 128i+64..128i+127.
+// gu holds the fused gate/up product: feature j = 64i + w sits in row tile i, gate at
+// column 128i + 32*(w/16) + w%16 and up 16 columns further.
 __global__ void k_swiglu(const float* __restrict__ gu, int ff, __half* __restrict__ xs, int tpad, float* __restrict__ out32) {
     int t = blockIdx.x;
     const float* row = gu + (int64_t)t * 2 * ff;
     for (int j = threadIdx.x; j < ff; j += blockDim.x) {
-        int col = (j >> 6) * 128 + (j & 63);
-        float g = row[col], u = row[col + 64];
+        int w = j & 63;
+        int col = (j >> 6) * 128 + (w >> 4) * 32 + (w & 15);
+        float g = row[col], u = row[col + 16];
         float up = __fmul_rn(g, u);
         float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
         float y = __fmul_rn(sg, up);

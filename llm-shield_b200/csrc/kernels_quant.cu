@@ -19,7 +19,10 @@ int64_t launches_total() { return g_launches.load(); }
 
 // raw: `rows` GGUF rows of `cols` elements (raw_row_bytes each). Row j goes to
 //   interleave == 0: tile tile_offset + j/128, row-in-tile j%128
-//   interleave != 0: tile j/64, row-in-tile row_in_tile_base + j%64 (gate/up pairing)
+//   interleave != 0: tile j/64; within the tile, 16-row groups alternate gate and up
+//                    (gate rows at 32*(w/16) + w%16, up rows 16 further, w = j%64), so a
+//                    warp's lanes l and l+16 hold the gate and up row of one FFN feature.
+//                    row_in_tile_base is 0 for the gate matrix and 16 for the up matrix.
 __global__ void k_repack(const uint8_t* __restrict__ raw, int type, int rows, int cols, int64_t raw_row_bytes,
                          uint8_t* __restrict__ dst, int ksteps, int row_in_tile_base, int tile_offset,
                          int interleave) {
@@ -30,7 +33,8 @@ __global__ void k_repack(const uint8_t* __restrict__ raw, int type, int rows, in
     int tile, rit;
     if (interleave) {
         tile = j / 64;
-        rit = row_in_tile_base + j % 64;
+        int w = j % 64;
+        rit = (w >> 4) * 32 + (w & 15) + row_in_tile_base;
     } else {
         tile = tile_offset + j / 128;
         rit = j % 128;

@@ -475,10 +475,10 @@ void load_model(jv_model* m, const std::string& path, int kv_pool_mb) {
         L.matrix_shape(to, orows, ocols);
         W.o = alloc_qweight(m, to.type, orows, ocols);
         L.upload(to, W.o, 0, 0, 0);
-        // gate and up interleaved in 64-row halves of each 128-row tile.
+        // gate and up interleaved in alternating 16-row groups of each 128-row tile.
         W.gu = alloc_qweight(m, tg.type, 2 * c.ff, c.hidden);
         L.upload(tg, W.gu, 0, 1, 0);
-        L.upload(tu, W.gu, 0, 1, 64);
+        L.upload(tu, W.gu, 0, 1, 16);
         int drows, dcols;
         L.matrix_shape(td, drows, dcols);
         W.down = alloc_qweight(m, td.type, drows, dcols);
