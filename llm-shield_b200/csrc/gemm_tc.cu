@@ -52,12 +52,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes (woken at
+// completion) or ~1 ms passes, instead of spinning.
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
@@ -122,16 +124,22 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+// tcgen05.ld of 16 consecutive accumulator columns (32 lanes x 32 bit) without waiting; the
+// registers are valid only after tmem_wait16 on the same array, which names them as in/out
+// operands so no use of them can be scheduled above the wait.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait16(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
 }
 
 // Bytes b0, b1 of x (picked by the byte_perm selector) as the fp16 pair (1024 + b0, 1024 + b1):
@@ -204,118 +212,151 @@ struct TcParams {
     int* counters;    // one arrival counter per (row tile, token tile); zero between launches
     int ksteps, T, tpad, bn, ldy, epilogue, ncols, splits;
     int tiles, ttiles, units;   // work units = tiles x ttiles x splits
-    int nr, nb, na;             // ring depths: raw chunks, activation tiles, decoded tiles
+    int nr, ns;                 // ring depths: raw chunks; stages (activation tile + decoded weights)
     int raw_off, b_off, bar_off;  // byte offsets inside the 1024-aligned dynamic smem (A at 0)
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
 
+// Position in a ring of n mbarrier-guarded slots: slot index and the parity of its current use.
+struct Ring {
+    int n, idx = 0;
+    uint32_t phase = 0;
+    __device__ explicit Ring(int slots) : n(slots) {}
+    __device__ __forceinline__ void next() {
+        if (++idx == n) { idx = 0; phase ^= 1u; }
+    }
+    __device__ __forceinline__ void prev() {
+        if (--idx < 0) { idx = n - 1; phase ^= 1u; }
+    }
+};
+
 // Work unit u -> (row tile, token tile, K split), token tiles and splits of one row tile
 // adjacent so concurrently running CTAs share each weight chunk through L2.
-__device__ __forceinline__ void unit_coords(const TcParams& p, int u, int& tile, int& tt, int& sp) {
-    sp = u % p.splits;
-    int r = u / p.splits;
-    tt = r % p.ttiles;
-    tile = r / p.ttiles;
+__device__ __forceinline__ void unit_coords(int u, int splits, int ttiles, int& tile, int& tt, int& sp) {
+    sp = u % splits;
+    int r = u / splits;
+    tt = r % ttiles;
+    tile = r / ttiles;
 }
 
 template <int TYPE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
+    // Every parameter in a register or a restrict pointer: nothing below takes the address of
+    // the parameter block, so no access is re-read after a store.
+    const uint8_t* __restrict__ g_w = p.w;
+    const __half* __restrict__ g_x = p.x;
+    float* __restrict__ g_y = p.y;
+    int* __restrict__ g_err = p.err;
+    __half* __restrict__ g_xs_out = p.xs_out;
+    float* g_ws = p.ws;
+    int* __restrict__ g_ctr = p.counters;
+    const int ksteps = p.ksteps, T = p.T, tpad = p.tpad, bn = p.bn, ldy = p.ldy, epi = p.epilogue, ncols = p.ncols;
+    const int splits = p.splits, ttiles = p.ttiles, units = p.units, nr_ = p.nr, ns_ = p.ns;
+    const int raw_off = p.raw_off, b_off = p.b_off, bar_off = p.bar_off;
     extern __shared__ uint8_t gsm_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
     const int cb = chunk_bytes(TYPE);
-    const int NR = p.nr, NB = p.nb, NA = p.na;
-    uint8_t* As = sm;               // NA x 16 KB decoded weights
-    uint8_t* Bs = sm + p.b_off;     // NB x bn*128 activations
-    uint8_t* Rs = sm + p.raw_off;   // NR x chunk raw quant blocks
-    uint64_t* bars = (uint64_t*)(sm + p.bar_off);
+    const int NR = nr_, NS = ns_;
+    uint8_t* As = sm;               // NS x 16 KB decoded weights
+    uint8_t* Bs = sm + b_off;     // NS x bn*128 activations
+    uint8_t* Rs = sm + raw_off;   // NR x chunk raw quant blocks
+    uint64_t* bars = (uint64_t*)(sm + bar_off);
+    // raw ring: raw_full (copy landed), raw_empty (8 decoder warps read it)
+    // stage ring: b_full (activation tile landed), a_full (8 decoder warps wrote the fp16
+    //             weights), st_empty (the MMA that read both completed)
     const uint32_t raw_full = s_addr(bars), raw_empty = raw_full + 8 * NR;
-    const uint32_t b_full = raw_empty + 8 * NR, b_empty = b_full + 8 * NB;
-    const uint32_t a_full = b_empty + 8 * NB, a_empty = a_full + 8 * NA;
-    const uint32_t acc_full = a_empty + 8 * NA, acc_empty = acc_full + 16, drained = acc_empty + 16;
-    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 2 * NB + 2 * NA + 5);
+    const uint32_t b_full = raw_empty + 8 * NR, a_full = b_full + 8 * NS, st_empty = a_full + 8 * NS;
+    const uint32_t acc_full = st_empty + 8 * NS, acc_empty = acc_full + 16, drained = acc_empty + 16;
+    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 3 * NS + 5);
     volatile int* last_flag = (volatile int*)(tslot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nks = p.ksteps / p.splits;      // k steps per unit
-    const uint32_t bbytes = (uint32_t)p.bn * 128u;
+    const int nks = ksteps / splits;      // k steps per unit
+    const uint32_t bbytes = (uint32_t)bn * 128u;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_THREADS); }
-        for (int i = 0; i < NB; i++) { mbar_init(b_full + 8 * i, 1); mbar_init(b_empty + 8 * i, 1); }
-        for (int i = 0; i < NA; i++) { mbar_init(a_full + 8 * i, DEC_THREADS); mbar_init(a_empty + 8 * i, 1); }
-        for (int i = 0; i < 2; i++) { mbar_init(acc_full + 8 * i, 1); mbar_init(acc_empty + 8 * i, 128); }
+        for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_THREADS / 32); }
+        for (int i = 0; i < NS; i++) {
+            mbar_init(b_full + 8 * i, 1);
+            mbar_init(a_full + 8 * i, DEC_THREADS / 32);
+            mbar_init(st_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < 2; i++) { mbar_init(acc_full + 8 * i, 1); mbar_init(acc_empty + 8 * i, 4); }
         mbar_init(drained, 1);
         fence_barrier_init();
     }
-    if (warp == 2) tmem_alloc(s_addr(tslot), 2 * p.ncols);
+    if (warp == 2) tmem_alloc(s_addr(tslot), 2 * ncols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    if (warp == 0) {
-        if (lane == 0) {  // ---------------------------------------------- producer
-            int64_t g = 0;
+    if (warp == 0 || warp == 3) {
+        if (lane == 0) {  // ----------------------------------------------- producers
+            // Warp 0 streams the raw weight chunks (ring freed by the decoders), warp 3 the
+            // activation tiles (stage ring, freed by the MMA): neither waits on the other.
+            const bool weights = warp == 0;
+            const int depth = weights ? NR : NS;
+            const uint32_t full = weights ? raw_full : b_full, empty = weights ? raw_empty : st_empty;
+            const uint32_t bytes = weights ? (uint32_t)cb : bbytes;
+            uint8_t* ring = weights ? Rs : Bs;
+            Ring r(depth);
             bool ok = true;
-            int64_t issued_r = 0, issued_b = 0;
-            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+            int issued = 0;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 int tile, tt, sp;
-                unit_coords(p, u, tile, tt, sp);
-                const int kb = sp * nks, t0 = tt * p.bn;
-                const uint8_t* wsrc = p.w + ((int64_t)tile * p.ksteps + kb) * cb;
-                for (int ks = 0; ks < nks; ks++, g++) {
-                    int ri = (int)(g % NR), bi = (int)(g % NB);
-                    if (!mbar_wait(raw_empty + 8 * ri, (uint32_t)((g / NR) & 1) ^ 1u)) { ok = false; break; }
-                    mbar_expect_tx(raw_full + 8 * ri, (uint32_t)cb);
-                    bulk_g2s(s_addr(Rs + ri * cb), wsrc + (int64_t)ks * cb, (uint32_t)cb, raw_full + 8 * ri);
-                    issued_r = g + 1;
-                    if (!mbar_wait(b_empty + 8 * bi, (uint32_t)((g / NB) & 1) ^ 1u)) { ok = false; break; }
-                    mbar_expect_tx(b_full + 8 * bi, bbytes);
-                    bulk_g2s(s_addr(Bs + (size_t)bi * bbytes), p.x + ((int64_t)(kb + ks) * p.tpad + t0) * 64, bbytes,
-                             b_full + 8 * bi);
-                    issued_b = g + 1;
+                unit_coords(u, splits, ttiles, tile, tt, sp);
+                const int kb = sp * nks, t0 = tt * bn;
+                const uint8_t* src = weights ? g_w + ((int64_t)tile * ksteps + kb) * cb
+                                             : (const uint8_t*)(g_x + ((int64_t)kb * tpad + t0) * 64);
+                const int64_t step = weights ? (int64_t)cb : (int64_t)tpad * 128;
+                for (int ks = 0; ks < nks; ks++) {
+                    if (!mbar_wait(empty + 8 * r.idx, r.phase ^ 1u)) { ok = false; break; }
+                    mbar_expect_tx(full + 8 * r.idx, bytes);
+                    bulk_g2s(s_addr(ring + (size_t)r.idx * bytes), src + ks * step, bytes, full + 8 * r.idx);
+                    r.next();
+                    issued++;
                 }
             }
-            if (!ok) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
-            // Never leave with copies in flight into this CTA's shared memory.
-            for (int64_t i = issued_r - 1; i >= 0 && i >= issued_r - NR; i--)
-                if (!mbar_wait(raw_full + 8 * (int)(i % NR), (uint32_t)((i / NR) & 1))) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
-            for (int64_t i = issued_b - 1; i >= 0 && i >= issued_b - NB; i--)
-                if (!mbar_wait(b_full + 8 * (int)(i % NB), (uint32_t)((i / NB) & 1))) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            if (!ok) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+            // Never leave with copies in flight into this CTA's shared memory: wait for the
+            // last min(issued, ring) copies.
+            for (int i = 0; i < issued && i < depth; i++) {
+                r.prev();
+                if (!mbar_wait(full + 8 * r.idx, r.phase)) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // --------------------------------------------- MMA issue
-            const uint32_t idesc = idesc_f16(p.bn, 128);
-            int64_t g = 0;
+            const uint32_t idesc = idesc_f16(bn, 128);
+            Ring rs(NS);
             bool ok = true;
             int i = 0;
-            for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, i++) {
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
                 const int ab = i & 1;
                 if (!mbar_wait(acc_empty + 8 * ab, (uint32_t)((i >> 1) & 1) ^ 1u)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t acc = tmem + (uint32_t)(ab * p.ncols);
-                for (int ks = 0; ks < nks; ks++, g++) {
-                    int ai = (int)(g % NA), bi = (int)(g % NB);
-                    if (!mbar_wait(a_full + 8 * ai, (uint32_t)((g / NA) & 1)) ||
-                        !mbar_wait(b_full + 8 * bi, (uint32_t)((g / NB) & 1))) {
+                const uint32_t acc = tmem + (uint32_t)(ab * ncols);
+                for (int ks = 0; ks < nks; ks++) {
+                    if (!mbar_wait(a_full + 8 * rs.idx, rs.phase) || !mbar_wait(b_full + 8 * rs.idx, rs.phase)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    uint32_t a_base = s_addr(As + ai * 16384), b_base = s_addr(Bs + (size_t)bi * bbytes);
+                    uint32_t a_base = s_addr(As + rs.idx * 16384), b_base = s_addr(Bs + (size_t)rs.idx * bbytes);
 #pragma unroll
                     for (int j = 0; j < 4; j++)
                         umma(acc, sdesc(a_base + 32 * j), sdesc(b_base + 32 * j), idesc, (ks > 0 || j > 0) ? 1u : 0u);
-                    umma_commit(a_empty + 8 * ai);
-                    umma_commit(b_empty + 8 * bi);
+                    umma_commit(st_empty + 8 * rs.idx);
+                    rs.next();
                 }
                 if (ok) umma_commit(acc_full + 8 * ab);
             }
-            if (!ok) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            if (!ok) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
             // Wait until every MMA this lane issued has completed before teardown.
             umma_commit(drained);
-            if (!mbar_wait(drained, 0)) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+            if (!mbar_wait(drained, 0)) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
         }
     } else if (warp >= DEC_WARP0) {  // --------------------------------------- decode
         // Thread dt decodes chunk c = dt % 8 of rows r0 + 32*it (it = 0..3); the swizzled
@@ -323,136 +364,148 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         const int dt = threadIdx.x - DEC_WARP0 * 32;
         const int c = dt & 7, r0 = dt >> 3;
         const int a_off = r0 * 128 + ((c ^ (r0 & 7)) << 4);
-        int64_t g = 0;
+        Ring rr(NR), rs(NS);
         bool ok = true;
-        for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-            for (int ks = 0; ks < nks; ks++, g++) {
-                int ri = (int)(g % NR), ai = (int)(g % NA);
-                if (!mbar_wait(raw_full + 8 * ri, (uint32_t)((g / NR) & 1))) { ok = false; break; }
-                const uint8_t* raw = Rs + ri * cb;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            for (int ks = 0; ks < nks; ks++) {
+                if (!mbar_wait(raw_full + 8 * rr.idx, rr.phase)) { ok = false; break; }
+                const uint8_t* raw = Rs + rr.idx * cb;
                 uint4 v[4];
 #pragma unroll
                 for (int it = 0; it < 4; it++) v[it] = decode8<TYPE>(raw, r0 + 32 * it, c);
-                mbar_arrive(raw_empty + 8 * ri);
-                if (!mbar_wait(a_empty + 8 * ai, (uint32_t)((g / NA) & 1) ^ 1u)) { ok = false; break; }
-                uint8_t* A = As + ai * 16384 + a_off;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(raw_empty + 8 * rr.idx);
+                rr.next();
+                if (!mbar_wait(st_empty + 8 * rs.idx, rs.phase ^ 1u)) { ok = false; break; }
+                uint8_t* A = As + rs.idx * 16384 + a_off;
 #pragma unroll
                 for (int it = 0; it < 4; it++) *(uint4*)(A + it * 32 * 128) = v[it];
-                fence_proxy_async();
-                mbar_arrive(a_full + 8 * ai);
+                fence_proxy_async();  // each writer's generic-proxy stores -> visible to the tensor core
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_full + 8 * rs.idx);
+                rs.next();
             }
         }
-        if (!ok) atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+        if (!ok) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
     } else if (warp >= 4) {  // ------------------------------------------------- epilogue
-        // Warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows of the unit's tile.
+        // Warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows of the unit's tile. Each 16
+        // column chunk's tcgen05.ld is issued before the previous chunk is processed.
         const int q = warp & 3;
         int i = 0;
-        for (int u = blockIdx.x; u < p.units; u += gridDim.x, i++) {
+        for (int u = blockIdx.x; u < units; u += gridDim.x, i++) {
             int tile, tt, sp;
-            unit_coords(p, u, tile, tt, sp);
-            const int t0 = tt * p.bn, ab = i & 1;
+            unit_coords(u, splits, ttiles, tile, tt, sp);
+            const int t0 = tt * bn, ab = i & 1;
             const bool ready = mbar_wait(acc_full + 8 * ab, (uint32_t)((i >> 1) & 1));
             tc_fence_after();
             if (!ready) {
-                atomicExch(p.err, JV_ERR_DEVICE_TIMEOUT);
+                atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
                 break;
             }
-            const uint32_t tacc = tmem + (uint32_t)(ab * p.ncols) + ((uint32_t)(q * 32) << 16);
+            const uint32_t tacc = tmem + (uint32_t)(ab * ncols) + ((uint32_t)(q * 32) << 16);
             const int n = tile * 128 + q * 32 + lane;
-            if (p.epilogue == EPI_SWIGLU) {
-                // Kernels.SwiGlu (reference src/Jevstral/Numerics/Kernels.cs:82-89): up <- g*u;
-                // s <- 1/(1+exp(-g)); y <- s*up. In each warp, lanes 0-15 hold gate rows and
-                // lanes 16-31 the matching up rows; one shuffle pairs them, and lane l < 16
-                // writes columns 0-7 of a chunk, lane l + 16 columns 8-15.
-                const int jf = tile * 64 + q * 16 + (lane & 15);
-                const bool hi = lane >= 16;
-                for (int col = 0; col < p.bn; col += 16) {
-                    float v[16], o[16];
-                    tmem_ld16(tacc + (uint32_t)col, v);
-#pragma unroll
-                    for (int j = 0; j < 16; j++) o[j] = __shfl_xor_sync(0xffffffffu, v[j], 16);
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const int jj = hi ? j + 8 : j;
-                        const float gg = hi ? o[jj] : v[jj];
-                        const float uu = hi ? v[jj] : o[jj];
-                        const int t = t0 + col + jj;
-                        const float up = __fmul_rn(gg, uu);
-                        const float sg = __frcp_rn(__fadd_rn(1.0f, expf(-gg)));
-                        if (t < p.T) p.xs_out[kslab_offset(t, jf, p.tpad)] = __float2half_rn(__fmul_rn(sg, up));
-                    }
-                }
-            } else if (p.splits == 1) {
-                for (int col = 0; col < p.bn; col += 16) {
-                    float v[16];
-                    tmem_ld16(tacc + (uint32_t)col, v);
-#pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        int t = t0 + col + j;
-                        if (t < p.T) {
-                            float* dst = p.y + (int64_t)t * p.ldy + n;
-                            *dst = p.epilogue == EPI_ADD ? __fadd_rn(*dst, v[j]) : v[j];
-                        }
-                    }
-                }
-            } else {
+            const int tn = min(bn, T - t0);  // valid columns of this token tile
+            bool last = true;
+            const float* other = nullptr;
+            if (splits > 1) {
                 // Both K halves publish their partial; the unit that finishes last adds the
                 // other half to its own (still in TMEM): p0 + p1, the same value whichever
                 // unit that is (IEEE addition commutes).
-                float* mine = p.ws + (int64_t)sp * p.T * p.ldy;
-                const float* other = p.ws + (int64_t)(1 - sp) * p.T * p.ldy;
-                for (int col = 0; col < p.bn; col += 16) {
-                    float v[16];
-                    tmem_ld16(tacc + (uint32_t)col, v);
+                float* mine = g_ws + (int64_t)sp * T * ldy;
+                other = g_ws + (int64_t)(1 - sp) * T * ldy;
+                uint32_t cur[16], nxt[16];
+                tmem_ld16_issue(tacc, cur);
+                tmem_wait16(cur);
+                for (int col = 0; col < bn; col += 16) {
+                    const bool more = col + 16 < bn;
+                    if (more) tmem_ld16_issue(tacc + (uint32_t)(col + 16), nxt);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        int t = t0 + col + j;
-                        if (t < p.T) mine[(int64_t)t * p.ldy + n] = v[j];
+                    for (int j = 0; j < 16; j++)
+                        if (col + j < tn) mine[(int64_t)(t0 + col + j) * ldy + n] = __uint_as_float(cur[j]);
+                    if (more) {
+                        tmem_wait16(nxt);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) cur[j] = nxt[j];
                     }
                 }
                 __threadfence();
                 epi_bar();
                 if (warp == 4 && lane == 0) {
-                    int* ctr = p.counters + tile * p.ttiles + tt;
+                    int* ctr = g_ctr + tile * ttiles + tt;
                     int old = atomicAdd(ctr, 1);
-                    int last = old == p.splits - 1;
-                    if (last) atomicExch(ctr, 0);
-                    *last_flag = last;
+                    int is_last = old == splits - 1;
+                    if (is_last) atomicExch(ctr, 0);
+                    *last_flag = is_last;
                 }
                 epi_bar();
-                const bool last = *last_flag != 0;
+                last = *last_flag != 0;
                 epi_bar();  // the flag is re-used by the next unit
-                if (last) {
-                    __threadfence();
-                    for (int col = 0; col < p.bn; col += 16) {
-                        float v[16], o[16], yv[16];
-                        tmem_ld16(tacc + (uint32_t)col, v);
+                if (last) __threadfence();
+            }
+            if (last) {
+                uint32_t cur[16], nxt[16];
+                tmem_ld16_issue(tacc, cur);
+                tmem_wait16(cur);
+                for (int col = 0; col < bn; col += 16) {
+                    const bool more = col + 16 < bn;
+                    if (more) tmem_ld16_issue(tacc + (uint32_t)(col + 16), nxt);
+                    if (epi == EPI_SWIGLU) {
+                        // Kernels.SwiGlu (reference src/Jevstral/Numerics/Kernels.cs:82-89):
+                        // up <- g*u; s <- 1/(1+exp(-g)); y <- s*up. Lanes 0-15 hold gate rows,
+                        // lanes 16-31 the matching up rows: one shuffle pairs them, lane l < 16
+                        // writes columns 0-7 of the chunk, lane l + 16 columns 8-15.
+                        const int jf = tile * 64 + q * 16 + (lane & 15);
+                        const bool hi = lane >= 16;
+                        float o[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j++) o[j] = __shfl_xor_sync(0xffffffffu, __uint_as_float(cur[j]), 16);
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const int jj = hi ? j + 8 : j;
+                            const float mv = hi ? __uint_as_float(cur[j + 8]) : __uint_as_float(cur[j]);
+                            const float ov = hi ? o[j + 8] : o[j];
+                            const float gg = hi ? ov : mv;
+                            const float uu = hi ? mv : ov;
+                            const float up = __fmul_rn(gg, uu);
+                            const float sg = __frcp_rn(__fadd_rn(1.0f, __expf(-gg)));
+                            if (col + jj < tn)
+                                g_xs_out[kslab_offset(t0 + col + jj, jf, tpad)] = __float2half_rn(__fmul_rn(sg, up));
+                        }
+                    } else {
+                        float o[16], yv[16];
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
-                            int t = t0 + col + j;
-                            o[j] = t < p.T ? __ldcg(other + (int64_t)t * p.ldy + n) : 0.f;
-                            yv[j] = (t < p.T && p.epilogue == EPI_ADD) ? p.y[(int64_t)t * p.ldy + n] : 0.f;
+                            const int64_t at = (int64_t)(t0 + col + j) * ldy + n;
+                            const bool in = col + j < tn;
+                            o[j] = (other && in) ? __ldcg(other + at) : 0.f;
+                            yv[j] = (epi == EPI_ADD && in) ? g_y[at] : 0.f;
                         }
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
-                            int t = t0 + col + j;
-                            if (t < p.T) {
-                                float s = __fadd_rn(v[j], o[j]);
-                                p.y[(int64_t)t * p.ldy + n] = p.epilogue == EPI_ADD ? __fadd_rn(yv[j], s) : s;
+                            if (col + j < tn) {
+                                float s = __uint_as_float(cur[j]);
+                                if (other) s = __fadd_rn(s, o[j]);
+                                g_y[(int64_t)(t0 + col + j) * ldy + n] = epi == EPI_ADD ? __fadd_rn(yv[j], s) : s;
                             }
                         }
+                    }
+                    if (more) {
+                        tmem_wait16(nxt);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) cur[j] = nxt[j];
                     }
                 }
             }
             tc_fence_before();
-            mbar_arrive(acc_empty + 8 * ab);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * p.ncols);
+        tmem_dealloc(tmem, 2 * ncols);
     }
 }
 
@@ -494,19 +547,16 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     int nc = 32;
     while (nc < a.bn) nc <<= 1;
     p.ncols = nc;
-    // Ring depths within ~220 KB: 3 decoded slots, 4 activation tiles (3 if they do not fit),
-    // and as many raw chunks (up to 12) as the rest allows.
-    const size_t budget = 220 * 1024;
-    p.na = 3;
-    p.nb = 4;
-    if (16384 * 3 + (size_t)a.bn * 128 * 4 + 4 * cb > budget) p.nb = 3;
-    size_t used = 16384 * (size_t)p.na + (size_t)a.bn * 128 * p.nb;
-    p.nr = (int)std::min<size_t>(12, (budget - used) / cb);
+    // Ring depths within ~222 KB: 4 stages (activation tile + decoded weights) if at least 4
+    // raw chunks still fit, else 3; the raw ring takes the rest (up to 12 chunks).
+    const size_t budget = 222 * 1024, stage = 16384 + (size_t)a.bn * 128;
+    p.ns = (stage * 4 + 4 * (size_t)cb <= budget) ? 4 : 3;
+    p.nr = (int)std::min<size_t>(12, (budget - stage * p.ns) / cb);
     if (p.nr < 2) throw Error(JV_ERR_ARG, "gemm: shared memory budget exceeded");
-    p.b_off = 16384 * p.na;
-    p.raw_off = p.b_off + a.bn * 128 * p.nb;
+    p.b_off = 16384 * p.ns;
+    p.raw_off = p.b_off + a.bn * 128 * p.ns;
     p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
-    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 2 * p.nb + 2 * p.na + 5) + 16 + 1024;
+    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
     JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (g_sm_count == 0) {
         int dev = 0;
