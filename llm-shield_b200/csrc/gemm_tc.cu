@@ -419,9 +419,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 for (int col = 0; col < bn; col += 16) {
                     const bool more = col + 16 < bn;
                     if (more) tmem_ld16_issue(tacc + (uint32_t)(col + 16), nxt);
+                    float* mp = mine + (int64_t)(t0 + col) * ldy + n;
+                    const int lim = min(16, tn - col);
 #pragma unroll
                     for (int j = 0; j < 16; j++)
-                        if (col + j < tn) mine[(int64_t)(t0 + col + j) * ldy + n] = __uint_as_float(cur[j]);
+                        if (j < lim) mp[(int64_t)j * ldy] = __uint_as_float(cur[j]);
                     if (more) {
                         tmem_wait16(nxt);
 #pragma unroll
@@ -472,21 +474,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                                 g_xs_out[kslab_offset(t0 + col + jj, jf, tpad)] = __float2half_rn(__fmul_rn(sg, up));
                         }
                     } else {
-                        float o[16], yv[16];
+                        // Row pointers step by ldy per token; the mode is uniform per launch.
+                        float* yp = g_y + (int64_t)(t0 + col) * ldy + n;
+                        const int lim = min(16, tn - col);
+                        if (other) {
+                            const float* op = other + (int64_t)(t0 + col) * ldy + n;
+                            float o[16], yv[16];
 #pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const int64_t at = (int64_t)(t0 + col + j) * ldy + n;
-                            const bool in = col + j < tn;
-                            o[j] = (other && in) ? __ldcg(other + at) : 0.f;
-                            yv[j] = (epi == EPI_ADD && in) ? g_y[at] : 0.f;
-                        }
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            if (col + j < tn) {
-                                float s = __uint_as_float(cur[j]);
-                                if (other) s = __fadd_rn(s, o[j]);
-                                g_y[(int64_t)(t0 + col + j) * ldy + n] = epi == EPI_ADD ? __fadd_rn(yv[j], s) : s;
+                            for (int j = 0; j < 16; j++) {
+                                o[j] = j < lim ? __ldcg(op + (int64_t)j * ldy) : 0.f;
+                                yv[j] = (epi == EPI_ADD && j < lim) ? yp[(int64_t)j * ldy] : 0.f;
                             }
+#pragma unroll
+                            for (int j = 0; j < 16; j++)
+                                if (j < lim) {
+                                    const float s = __fadd_rn(__uint_as_float(cur[j]), o[j]);
+                                    yp[(int64_t)j * ldy] = epi == EPI_ADD ? __fadd_rn(yv[j], s) : s;
+                                }
+                        } else if (epi == EPI_ADD) {
+                            float yv[16];
+#pragma unroll
+                            for (int j = 0; j < 16; j++) yv[j] = j < lim ? yp[(int64_t)j * ldy] : 0.f;
+#pragma unroll
+                            for (int j = 0; j < 16; j++)
+                                if (j < lim) yp[(int64_t)j * ldy] = __fadd_rn(yv[j], __uint_as_float(cur[j]));
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; j++)
+                                if (j < lim) yp[(int64_t)j * ldy] = __uint_as_float(cur[j]);
                         }
                     }
                     if (more) {
