@@ -149,6 +149,22 @@ int jv_forward_layout(jv_ctx* ctx, const int32_t* tokens, int32_t n, const jv_la
  * first_token. Writes the chosen tokens to out_tokens[steps]. */
 int jv_decode_greedy(jv_ctx* ctx, int32_t first_token, int32_t steps, int32_t* out_tokens);
 
+/* ---- QuantMatMul on device buffers (src/Jevstral/Numerics/QuantMatMul.cs) -------------
+ * A quantized matrix lives on the device in this library's re-tiled layout (the GGUF blocks
+ * of 128 rows x 64 columns gathered into one contiguous chunk; bits unchanged). All pointers
+ * below are device pointers; stream is a cudaStream_t (NULL = the legacy default stream).
+ * type is the GGML type id: 8 Q8_0, 7 Q5_1, 2 Q4_0. rows % 128 == 0, cols % 64 == 0. */
+
+/* Bytes of the re-tiled layout (WeightMatrix, src/Jevstral/Numerics/WeightMatrix.cs:16-66). */
+int64_t jv_qweight_bytes(int32_t type, int32_t rows, int32_t cols);
+/* Re-tile `rows` GGUF rows (GgmlTypeInfo.RowBytes(type, cols) bytes each, back to back) into
+ * `tiled` (jv_qweight_bytes bytes). */
+int jv_qweight_pack(int32_t type, const void* gguf_rows, int32_t rows, int32_t cols, void* tiled, void* stream);
+/* QuantMatMul.ForwardAsync for one token (QuantMatMul.cs:127-129 -> RunRowsFloat :140-176):
+ * y[rows] = W x[cols] with W decoded to fp32 exactly as Dequantizer does and fp32 FMA. Uses a
+ * split-K partial buffer that it allocates on the device on first use (and keeps). */
+int jv_qmatvec(int32_t type, const void* tiled, int32_t rows, int32_t cols, const float* x, float* y, void* stream);
+
 /* ---- KV cache (src/Jevstral/Model/KvCache.cs) ----------------------------------------- */
 
 int32_t jv_kv_length(jv_ctx* ctx);                             /* KvCache.Length   :23     */

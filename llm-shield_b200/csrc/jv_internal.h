@@ -180,4 +180,9 @@ int64_t launches_total();
 
 void note_launch(int n = 1);
 
+// The calling thread's jv_last_error() message; returns code.
+int api_error(int code, const std::string& msg);
+// A re-tiled quantized matrix described by the QuantMatMul C ABI; throws on bad arguments.
+QWeight qweight_view(int type, const void* tiled, int rows, int cols);
+
 }  // namespace jv

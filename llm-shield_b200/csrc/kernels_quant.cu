@@ -212,12 +212,20 @@ void launch_gemv(const QWeight& w, const float* x, float* partial, int splits, c
     dim3 grid(w.tiles, splits);
     int per = (w.ksteps + splits - 1) / splits;
     size_t smem = (size_t)per * 64 * sizeof(float);
-    if (w.type == T_Q8_0)
+    if (smem > 227 * 1024) throw Error(JV_ERR_UNSUPPORTED, "gemv: the activation slice does not fit in shared memory");
+    if (w.type == T_Q8_0) {
+        if (smem > 48 * 1024)
+            JV_CUDA(cudaFuncSetAttribute(k_gemv<T_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         k_gemv<T_Q8_0><<<grid, GEMV_THREADS, smem, s>>>(w.data, w.ksteps, w.rows, x, partial, splits);
-    else if (w.type == T_Q4_0)
+    } else if (w.type == T_Q4_0) {
+        if (smem > 48 * 1024)
+            JV_CUDA(cudaFuncSetAttribute(k_gemv<T_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         k_gemv<T_Q4_0><<<grid, GEMV_THREADS, smem, s>>>(w.data, w.ksteps, w.rows, x, partial, splits);
-    else
+    } else {
+        if (smem > 48 * 1024)
+            JV_CUDA(cudaFuncSetAttribute(k_gemv<T_Q5_1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         k_gemv<T_Q5_1><<<grid, GEMV_THREADS, smem, s>>>(w.data, w.ksteps, w.rows, x, partial, splits);
+    }
     note_launch();
 }
 

@@ -1002,6 +1002,26 @@ HostLayout layout_tree(int start, int trunk, const std::vector<int>& offsets, in
 
 }  // namespace
 
+namespace jv {
+int api_error(int code, const std::string& msg) { return set_error(code, msg); }
+
+QWeight qweight_view(int type, const void* tiled, int rows, int cols) {
+    if (type != T_Q8_0 && type != T_Q4_0 && type != T_Q5_1)
+        throw Error(JV_ERR_UNSUPPORTED, "weight type " + std::to_string(type) + " is not on the B200 path (Q8_0, Q5_1, Q4_0 are)");
+    if (rows <= 0 || cols <= 0 || rows % TILE_ROWS != 0 || cols % TILE_K != 0)
+        throw Error(JV_ERR_ARG, "a re-tiled matrix needs rows % 128 == 0 and cols % 64 == 0; got " + std::to_string(rows) +
+                                    "x" + std::to_string(cols));
+    QWeight w;
+    w.type = type;
+    w.rows = rows;
+    w.cols = cols;
+    w.tiles = rows / TILE_ROWS;
+    w.ksteps = cols / TILE_K;
+    w.data = (uint8_t*)tiled;
+    return w;
+}
+}  // namespace jv
+
 // =========================================================================== C ABI
 
 extern "C" {

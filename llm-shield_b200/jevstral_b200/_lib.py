@@ -58,6 +58,9 @@ SIGNATURES = [
     ("jv_forward_tree", C.c_int, [vp, i32p, i32, i32p, i32p, i32, i32p, i32, f32p]),
     ("jv_forward_layout", C.c_int, [vp, i32p, i32, C.POINTER(JvLayout), i32p, i32, i32, f32p, i32, f32p]),
     ("jv_decode_greedy", C.c_int, [vp, i32, i32, i32p]),
+    ("jv_qweight_bytes", i64, [i32, i32, i32]),
+    ("jv_qweight_pack", C.c_int, [i32, vp, i32, i32, vp, vp]),
+    ("jv_qmatvec", C.c_int, [i32, vp, i32, i32, vp, vp, vp]),
     ("jv_kv_length", i32, [vp]),
     ("jv_kv_capacity", i32, [vp]),
     ("jv_kv_reset", C.c_int, [vp]),

@@ -283,3 +283,30 @@ def test_kernel_launches_are_counted(small):
     with ctx(small) as c:
         c.forward_tree([1, 1500, 2500], [[3000, 4000], [5000]], VERDICT_ROWS)
     assert jv.kernel_launches() - before >= 7 * SMALL_CFG.layers
+
+
+@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
+@pytest.mark.parametrize("rows,cols", [(128, 256), (3072, 3072), (1024, 9216)])
+def test_quant_matvec_matches_the_oracle(qtype, rows, cols):
+    """jv_qmatvec (QuantMatMul.ForwardAsync, one token) against the oracle's RunRowsFloat."""
+    import torch
+
+    from jevstral_b200 import quant
+    from jevstral_b200.synth import synth_normal, synth_quantize
+
+    w = synth_normal(7, rows, rows * cols, 0.02)
+    raw = synth_quantize(w, qtype)
+    x = np.random.default_rng(rows + cols).uniform(-2, 2, cols).astype(np.float32)
+    dev = torch.device("cuda:0")
+    d_raw = torch.from_numpy(raw).to(dev)
+    d_tiled = torch.empty(quant.qweight_bytes(qtype, rows, cols), dtype=torch.uint8, device=dev)
+    d_x = torch.from_numpy(x).to(dev)
+    d_y = torch.empty(rows, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    quant.qweight_pack(qtype, d_raw.data_ptr(), rows, cols, d_tiled.data_ptr())
+    quant.qmatvec(qtype, d_tiled.data_ptr(), rows, cols, d_x.data_ptr(), d_y.data_ptr())
+    torch.cuda.synchronize()
+    want = ob.matmul(quant.TYPE_IDS[qtype], raw, rows, cols, x, 1)[0]
+    got = d_y.cpu().numpy()
+    err = np.abs(got - want) / np.maximum(1.0, np.abs(want))
+    assert err.max() < 1e-5, err.max()
