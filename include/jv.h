@@ -164,6 +164,18 @@ int jv_qweight_pack(int32_t type, const void* gguf_rows, int32_t rows, int32_t c
  * y[rows] = W x[cols] with W decoded to fp32 exactly as Dequantizer does and fp32 FMA. Uses a
  * split-K partial buffer that it allocates on the device on first use (and keeps). */
 int jv_qmatvec(int32_t type, const void* tiled, int32_t rows, int32_t cols, const float* x, float* y, void* stream);
+/* jv_qmatvec without any device allocation. No counterpart in the reference: it is for
+ * callers that must not allocate device memory on the call path (a host that has planned
+ * all of HBM up front, or one running under a memory cap owned by another component). The
+ * split-K partials live in a fixed 1 MiB device array (JV_QMATVEC_SCRATCH_FLOATS_MAX = 262144
+ * floats) built into the library; a call needs splits x rows floats (splits as jv_qmatvec
+ * picks them) and fails with JV_ERR_RANGE above that. All calls on a device share the array:
+ * nothing in it has to start at zero, but calls that overlap in time on one device race, so
+ * serialize them. The first call on each device does a one-time set-up (a symbol-address
+ * lookup with that device current); make it before any stream capture begins. */
+#define JV_QMATVEC_SCRATCH_FLOATS_MAX 262144
+int jv_qmatvec_noalloc(int32_t type, const void* tiled, int32_t rows, int32_t cols, const float* x, float* y,
+                       void* stream);
 
 /* ---- KV cache (src/Jevstral/Model/KvCache.cs) ----------------------------------------- */
 

@@ -61,6 +61,7 @@ SIGNATURES = [
     ("jv_qweight_bytes", i64, [i32, i32, i32]),
     ("jv_qweight_pack", C.c_int, [i32, vp, i32, i32, vp, vp]),
     ("jv_qmatvec", C.c_int, [i32, vp, i32, i32, vp, vp, vp]),
+    ("jv_qmatvec_noalloc", C.c_int, [i32, vp, i32, i32, vp, vp, vp]),
     ("jv_kv_length", i32, [vp]),
     ("jv_kv_capacity", i32, [vp]),
     ("jv_kv_reset", C.c_int, [vp]),
