@@ -27,7 +27,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-
                      "-Xcompiler", "-Wall,-Wno-unused-function", "-I", str(PKG.parent / "include")]
 
 SOURCES = ["gguf.cpp", "runtime.cu", "kernels_quant.cu", "kernels_elem.cu", "kernels_attn.cu", "gemm_tc.cu",
-           "quantmatmul.cu", "noalloc.cu"]
+           "quantmatmul.cu", "noalloc.cu", "kernels_decode.cu"]
 
 
 def _run(cmd: list[str], verbose: bool) -> str:

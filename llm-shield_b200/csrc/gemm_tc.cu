@@ -81,6 +81,10 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
 }
+// Bulk prefetch of [src, src + bytes) into L2 (no shared memory, no completion to wait for).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 __device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
@@ -202,6 +206,8 @@ __device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r,
     return o;
 }
 
+constexpr int RAW_PREFETCH = 24;  // raw chunks prefetched into L2 ahead of the shared-memory copies
+
 struct TcParams {
     const uint8_t* w;
     const __half* x;
@@ -311,7 +317,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 const uint8_t* src = weights ? g_w + ((int64_t)tile * ksteps + kb) * cb
                                              : (const uint8_t*)(g_x + ((int64_t)kb * tpad + t0) * 64);
                 const int64_t step = weights ? (int64_t)cb : (int64_t)tpad * 128;
+                // The raw ring holds only a few chunks, too few to cover HBM latency on its
+                // own: run an L2 prefetch RAW_PREFETCH chunks ahead of the copies.
+                if (weights)
+                    for (int ks = 0; ks < RAW_PREFETCH && ks < nks; ks++) bulk_prefetch_l2(src + ks * step, bytes);
                 for (int ks = 0; ks < nks; ks++) {
+                    if (weights && ks + RAW_PREFETCH < nks) bulk_prefetch_l2(src + (ks + RAW_PREFETCH) * step, bytes);
                     if (!mbar_wait(empty + 8 * r.idx, r.phase ^ 1u)) { ok = false; break; }
                     mbar_expect_tx(full + 8 * r.idx, bytes);
                     bulk_g2s(s_addr(ring + (size_t)r.idx * bytes), src + ks * step, bytes, full + 8 * r.idx);

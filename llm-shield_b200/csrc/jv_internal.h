@@ -165,6 +165,64 @@ struct DecodeAttnArgs {
 };
 void launch_decode_attention(const DecodeAttnArgs& a, cudaStream_t s);
 
+// ------------------------------------------------------- single-token step
+
+// The per-step values of a decode step, read by the decode kernels from device memory so
+// that a step's launches are the same for every token (and can be replayed as a graph).
+// Causal step: visible logical keys [0, n_keys) with key L at slot L below `shared`, else at
+// slot segment + L - shared.
+struct DecodeStep {
+    int32_t token, slot, pos, shared, segment, n_keys, index, pad;
+};
+
+enum DecMode : int { DEC_STORE = 0, DEC_ADD = 1, DEC_SWIGLU = 2, DEC_QKV = 3, DEC_HEAD = 4 };
+
+struct DecGemvArgs {
+    const uint8_t* w = nullptr;  // re-tiled matrix
+    int ksteps = 0, rows = 0;
+    const float* in = nullptr;   // x (fp32, n_in = 64 * ksteps)
+    int n_in = 0;
+    const float* norm_w = nullptr;  // RMSNorm gain (modes with a norm)
+    float eps = 0.f;
+    float* y = nullptr;          // STORE/ADD: [rows]; SWIGLU: [rows / 2]; HEAD: logits [rows]
+    float* partial = nullptr;    // [splits][rows]
+    int* counters = nullptr;     // [tiles + 1], zero between launches
+    // DEC_QKV
+    const DecodeStep* step = nullptr;
+    const float2* rope_table = nullptr;
+    int heads = 0, kv_heads = 0, layer = 0, orig_ctx = 0;
+    float temperature_scale = 0.f;
+    float* q32 = nullptr;
+    __half* kv_pool = nullptr;
+    const int32_t* page_table = nullptr;
+    int64_t page_bytes = 0;
+    int page_slots = 0;
+    // DEC_HEAD
+    float* cand_v = nullptr;     // [tiles]
+    int* cand_i = nullptr;       // [tiles]
+    int32_t* argmax_out = nullptr;
+    int advance = 0;             // advance *step to the next token after the argmax
+    int32_t* tokens_out = nullptr;  // [steps], written at step->index when advancing
+    DecodeStep* step_rw = nullptr;
+};
+void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int splits, cudaStream_t s);
+
+struct DecAttnArgs {
+    const float* q32;
+    const __half* kv_pool;
+    const int32_t* page_table;
+    int64_t page_bytes;
+    int page_slots;
+    int layer, heads, kv_heads;
+    float scale;
+    const DecodeStep* step;
+    float* partial;   // [heads][splits][2 + 128]
+    int* counters;    // [kv_heads], zero between launches
+    float* ctx32;     // [heads * 128]
+};
+constexpr int DEC_ATTN_KEYS = 64;  // logical keys per attention split
+void launch_dec_attn(const DecAttnArgs& a, int splits, cudaStream_t s);
+
 void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, cudaStream_t s);
 void launch_add(float* h, const float* x, int64_t n, cudaStream_t s);
 void launch_head_rows(const QWeight& table, const float* normed, int n_out, const int32_t* rows, int n_rows,

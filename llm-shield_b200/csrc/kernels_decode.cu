@@ -1,0 +1,565 @@
+// kernels_decode.cu — the single-token forward (a decode step), five fused kernels per layer:
+//
+//   1. attn_norm + QKV matvec + RoPE + temperature + K/V page write      (k_dec_gemv, DEC_QKV)
+//   2. attention over the visible keys, split over keys, combined by the last CTA (k_dec_attn)
+//   3. O matvec + residual add                                            (k_dec_gemv, DEC_ADD)
+//   4. ffn_norm + gate/up matvec + SwiGLU                                  (k_dec_gemv, DEC_SWIGLU)
+//   5. down matvec + residual add                                          (k_dec_gemv, DEC_ADD)
+//
+// and the LM head: final norm + full-vocabulary matvec + argmax (k_dec_gemv, DEC_HEAD).
+//
+// The matvec (reference QuantMatMul.RunRowsFloat, src/Jevstral/Numerics/QuantMatMul.cs:140-176)
+// is HBM-bound, so its cost per weight byte must stay below the memory rate. Decoding every
+// weight to fp32 and converting integers one by one does not: the conversions alone cap it
+// near a third of HBM bandwidth. Here the quantized integers go straight into fp16 tensor-core
+// fragments (mma.sync m16n8k16): q (Q8_0), q - 8 (Q4_0) and q5 (Q5_1) are small integers,
+// exact in fp16. One MMA sums 16 products of a row with x; x is split into hi = fp16(x) and
+// lo = fp16(x - hi) in the two B columns, so the products carry x to ~22 bits. Each 32-wide
+// block's sum is then scaled by its fp32 d (and Q5_1 adds m times the block's sum of x):
+//   y_r = sum_b d_rb * (sum_i q_rbi x_bi) [+ m_rb * sum_i x_bi],
+// which is the reference's sum_i (d q_i [+ m]) x_i with the products regrouped per block.
+//
+// The dynamic values of a step (token, slot, position, visible keys) are read from a
+// DecodeStep in device memory, so a step's launches do not change from one token to the
+// next and can be replayed as a CUDA graph; DEC_HEAD can advance the step on the device.
+#include "jv_internal.h"
+
+namespace jv {
+
+namespace {
+
+constexpr int DG_THREADS = 256;  // 8 warps x 16 rows = one 128-row tile
+constexpr int DG_UNROLL = 4;     // k steps whose raw words are loaded before any is used
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1, const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+// Bytes of x picked by the byte_perm selector as the fp16 pair (1024 + b0, 1024 + b1), minus
+// `bias` (exact: every operand is an integer below 2048).
+__device__ __forceinline__ uint32_t int_pair(uint32_t x, uint32_t sel, __half2 bias) {
+    uint32_t w = __byte_perm(x, 0x64646464u, sel);
+    __half2 h = __hsub2(*reinterpret_cast<__half2*>(&w), bias);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Fifth bits of four elements (bits 0-3 of h) into bit 4 of each byte.
+__device__ __forceinline__ uint32_t spread4(uint32_t h) {
+    return ((h & 1u) << 4) | ((h & 2u) << 11) | ((h & 4u) << 18) | ((h & 8u) << 25);
+}
+
+// The raw words one lane needs for one k step: rows r (g) and r + 8 (h), blocks 0 and 1.
+template <int TYPE>
+struct Raw {
+    uint32_t q[2][2][TYPE == T_Q8_0 ? 2 : 1];  // [row][block][word]
+    uint32_t d[2];                             // fp16 d of blocks 0,1 per row
+    uint32_t qh[2][2];                         // Q5_1: fifth bits per row and block
+    uint32_t m[2];                             // Q5_1: fp16 m of blocks 0,1 per row
+};
+
+template <int TYPE>
+__device__ __forceinline__ void load_raw(Raw<TYPE>& r, const uint8_t* __restrict__ chunk, int row, int kq) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int rr = row + 8 * h;
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+            if (TYPE == T_Q8_0) {
+                uint2 v = __ldg((const uint2*)(chunk + rr * 64 + 32 * b + 8 * kq));
+                r.q[h][b][0] = v.x;
+                r.q[h][b][TYPE == T_Q8_0 ? 1 : 0] = v.y;
+            } else {
+                r.q[h][b][0] = __ldg((const uint32_t*)(chunk + rr * 32 + 16 * b + 4 * kq));
+            }
+        }
+        r.d[h] = __ldg((const uint32_t*)(chunk + qs_bytes(TYPE) + (TYPE == T_Q5_1 ? 1024 : 0) + rr * 4));
+        if (TYPE == T_Q5_1) {
+            uint2 v = __ldg((const uint2*)(chunk + 4096 + rr * 8));
+            r.qh[h][0] = v.x;
+            r.qh[h][1] = v.y;
+            r.m[h] = __ldg((const uint32_t*)(chunk + 5632 + rr * 4));
+        }
+    }
+}
+
+// A fragments of the two MMAs (sub = 0, 1) of block b: regs {row g k lo, row h k lo, row g
+// k hi, row h k hi} as the m16n8k16 row-major A layout wants them.
+template <int TYPE>
+__device__ __forceinline__ void a_frags(const Raw<TYPE>& r, int b, int kq, uint32_t (&a)[2][4]) {
+    if (TYPE == T_Q8_0) {
+        const __half2 bias = __floats2half2_rn(1152.f, 1152.f);  // 1024 + 128: biased int8
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+#pragma unroll
+            for (int s = 0; s < 2; s++) {
+                uint32_t x = r.q[h][b][s & (TYPE == T_Q8_0 ? 1 : 0)] ^ 0x80808080u;
+                a[s][h] = int_pair(x, 0x4140u, bias);
+                a[s][2 + h] = int_pair(x, 0x4342u, bias);
+            }
+        }
+    } else {
+        const __half2 bias = TYPE == T_Q4_0 ? __floats2half2_rn(1032.f, 1032.f) : __floats2half2_rn(1024.f, 1024.f);
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            uint32_t q = r.q[h][b][0];
+            uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;
+            if (TYPE == T_Q5_1) {
+                lo |= spread4((r.qh[h][b] >> (4 * kq)) & 0xFu);
+                hi |= spread4((r.qh[h][b] >> (16 + 4 * kq)) & 0xFu);
+            }
+            a[0][h] = int_pair(lo, 0x4140u, bias);
+            a[0][2 + h] = int_pair(lo, 0x4342u, bias);
+            a[1][h] = int_pair(hi, 0x4140u, bias);
+            a[1][2 + h] = int_pair(hi, 0x4342u, bias);
+        }
+    }
+}
+
+// First element (within a k step) of the four consecutive x values lane kq feeds to MMA
+// (b, sub); the A side above holds the weights of exactly those elements.
+template <int TYPE>
+__device__ __forceinline__ int x_base(int b, int sub, int kq) {
+    return TYPE == T_Q8_0 ? 32 * b + 8 * kq + 4 * sub : 32 * b + 16 * sub + 4 * kq;
+}
+
+__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w];
+        red[32] = s;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// Kernels.ArgMax / IndexOfMax order: the larger value, the first index on ties, a NaN wins.
+__device__ __forceinline__ bool dec_better(float v, int i, float bv, int bi) {
+    bool vn = v != v, bn = bv != bv;
+    if (vn || bn) {
+        if (vn && bn) return i < bi;
+        return vn;
+    }
+    return v > bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ __half* kv_slot(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots,
+                                           int layer, int kv_heads, int head, int kv, int slot) {
+    int page = page_table[slot / page_slots];
+    int64_t off = (int64_t)page * page_bytes +
+                  ((int64_t)((layer * kv_heads + head) * 2 + kv) * page_slots + (slot % page_slots)) * 256;
+    return (__half*)((char*)pool + off);
+}
+
+template <int TYPE, int MODE, bool NORM>
+__global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
+    extern __shared__ __align__(16) uint8_t dg_smem[];
+    __shared__ double red[33];
+    __shared__ float s_out[128];
+    __shared__ int s_last;
+    const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+    const int ksteps = a.ksteps;
+    const int per = (ksteps + splits - 1) / splits;
+    const int ks0 = split * per, nk = max(0, min(ksteps, ks0 + per) - ks0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cb = chunk_bytes(TYPE);
+
+    float* xs = (float*)dg_smem;                        // [per*64] this CTA's slice of x
+    uint2* xf = (uint2*)(xs + per * 64);                // [per][2 blocks][2 subs][8 lanes]
+    float* sx = (float*)(xf + per * 32);                // [per][2] block sums of x (Q5_1)
+
+    // ---- x: the CTA's K slice, RMS-normalised first when NORM (Kernels.RmsNorm, Kernels.cs:25-60)
+    float scale = 1.f;
+    if (NORM) {
+        double s = 0;
+        for (int k = threadIdx.x; k < a.n_in; k += DG_THREADS) {
+            float v = a.in[k];
+            s += (double)v * (double)v;
+        }
+        s = block_sum_d(s, red);
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / a.n_in), a.eps)));
+    }
+    for (int i = threadIdx.x; i < nk * 64; i += DG_THREADS) {
+        const int k = ks0 * 64 + i;
+        const float v = a.in[k];
+        xs[i] = NORM ? __fmul_rn(__fmul_rn(v, scale), a.norm_w[k]) : v;
+    }
+    __syncthreads();
+    // B fragments: column 0 = fp16(x), column 1 = fp16(x - column 0); lanes 0-3 / 4-7.
+    for (int e = threadIdx.x; e < nk * 32; e += DG_THREADS) {
+        const int ks = e >> 5, rest = e & 31, b = rest >> 4, sub = (rest >> 3) & 1, l = rest & 7;
+        const int kq = l & 3, n = l >> 2;
+        const float* p = xs + ks * 64 + x_base<TYPE>(b, sub, kq);
+        uint32_t w[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            __half h0 = __float2half_rn(p[2 * j]), h1 = __float2half_rn(p[2 * j + 1]);
+            if (n == 1) {
+                h0 = __float2half_rn(__fsub_rn(p[2 * j], __half2float(h0)));
+                h1 = __float2half_rn(__fsub_rn(p[2 * j + 1], __half2float(h1)));
+            }
+            w[j] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        }
+        xf[e] = make_uint2(w[0], w[1]);
+    }
+    if (TYPE == T_Q5_1)
+        for (int e = threadIdx.x; e < nk * 2; e += DG_THREADS) {
+            const float* p = xs + e * 32;
+            float s = 0.f;
+            for (int i = 0; i < 32; i++) s = __fadd_rn(s, p[i]);
+            sx[e] = s;
+        }
+    __syncthreads();
+
+    // ---- main loop: warp w owns rows 16w + g and 16w + g + 8 of the tile
+    const int g = lane >> 2, kq = lane & 3;
+    const int row = 16 * warp + g;
+    const uint8_t* __restrict__ base = a.w + ((int64_t)tile * ksteps + ks0) * cb;
+    float acc[2] = {0.f, 0.f};
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < nk; k0 += DG_UNROLL) {
+        Raw<TYPE> r[DG_UNROLL];
+#pragma unroll
+        for (int u = 0; u < DG_UNROLL; u++)
+            if (k0 + u < nk) load_raw<TYPE>(r[u], base + (int64_t)(k0 + u) * cb, row, kq);
+#pragma unroll
+        for (int u = 0; u < DG_UNROLL; u++) {
+            if (k0 + u >= nk) break;
+            const int ks = k0 + u;
+#pragma unroll
+            for (int b = 0; b < 2; b++) {
+                uint32_t af[2][4];
+                a_frags<TYPE>(r[u], b, kq, af);
+                uint2 b0 = lane < 8 ? xf[(ks * 2 + b) * 16 + lane] : make_uint2(0u, 0u);
+                uint2 b1 = lane < 8 ? xf[(ks * 2 + b) * 16 + 8 + lane] : make_uint2(0u, 0u);
+                float c[4];
+                mma16816(c, af[0][0], af[0][1], af[0][2], af[0][3], b0.x, b0.y, zero);
+                mma16816(c, af[1][0], af[1][1], af[1][2], af[1][3], b1.x, b1.y, c);
+                // lanes with kq == 0 hold column 0 (x hi) and 1 (x lo) of rows g and g + 8
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const float s = __fadd_rn(c[2 * h], c[2 * h + 1]);
+                    const float d = b ? half_hi(r[u].d[h]) : half_lo(r[u].d[h]);
+                    acc[h] = fmaf(d, s, acc[h]);
+                    if (TYPE == T_Q5_1) {
+                        const float m = b ? half_hi(r[u].m[h]) : half_lo(r[u].m[h]);
+                        acc[h] = fmaf(m, sx[ks * 2 + b], acc[h]);
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- split-K: partials in order, summed by the last CTA of the tile
+    const int n0 = tile * 128;
+    if (splits == 1) {
+        if (kq == 0) {
+            s_out[row] = acc[0];
+            s_out[row + 8] = acc[1];
+        }
+        __syncthreads();
+    } else {
+        if (kq == 0) {
+            a.partial[(int64_t)split * a.rows + n0 + row] = acc[0];
+            a.partial[(int64_t)split * a.rows + n0 + row + 8] = acc[1];
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int prev = atomicAdd(a.counters + tile, 1);
+            s_last = prev == splits - 1;
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        if (threadIdx.x < 128) {
+            float s = 0.f;
+            for (int p = 0; p < splits; p++) s = __fadd_rn(s, __ldcg(a.partial + (int64_t)p * a.rows + n0 + threadIdx.x));
+            s_out[threadIdx.x] = s;
+        }
+        if (threadIdx.x == 0) a.counters[tile] = 0;  // ready for the next launch
+        __syncthreads();
+    }
+
+    // ---- epilogues
+    const int t = threadIdx.x;
+    if (MODE == DEC_STORE) {
+        if (t < 128) a.y[n0 + t] = s_out[t];
+    } else if (MODE == DEC_ADD) {
+        if (t < 128) a.y[n0 + t] = __fadd_rn(a.y[n0 + t], s_out[t]);
+    } else if (MODE == DEC_SWIGLU) {
+        // Kernels.SwiGlu (Kernels.cs:82-89) on the 16-row gate/up interleave of the tile.
+        if (t < 64) {
+            const int gr = 32 * (t >> 4) + (t & 15);
+            const float gg = s_out[gr], uu = s_out[gr + 16];
+            const float up = __fmul_rn(gg, uu);
+            const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg)));
+            a.y[tile * 64 + t] = __fmul_rn(sg, up);
+        }
+    } else if (MODE == DEC_QKV) {
+        // One tile = one head of 128 (q heads, then k heads, then v heads). RotateQueries /
+        // StoreKeys / StoreValues / ApplyPositionScale (MinistralModel.cs:638-682).
+        const DecodeStep st = *a.step;
+        const int hq = a.heads, hk = a.kv_heads;
+        if (t < 64) {
+            const float x0 = s_out[2 * t], x1 = s_out[2 * t + 1];
+            if (tile < hq + hk) {
+                const float2 cs = a.rope_table[(int64_t)st.pos * 64 + t];
+                float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+                float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+                if (tile < hq) {
+                    float temp = 1.0f;
+                    if (a.orig_ctx > 0 && a.temperature_scale != 0.f) {
+                        float interval = floorf(__fdiv_rn((float)st.pos, (float)a.orig_ctx));
+                        if (interval != 0.f)
+                            temp = __fadd_rn(1.0f, __fmul_rn(a.temperature_scale, logf(__fadd_rn(1.0f, interval))));
+                    }
+                    if (temp != 1.0f) { r0 = __fmul_rn(r0, temp); r1 = __fmul_rn(r1, temp); }
+                    a.q32[tile * 128 + 2 * t] = r0;
+                    a.q32[tile * 128 + 2 * t + 1] = r1;
+                } else {
+                    __half* dst = kv_slot(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq, 0, st.slot);
+                    *(__half2*)(dst + 2 * t) = __floats2half2_rn(r0, r1);
+                }
+            } else {
+                __half* dst = kv_slot(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq - hk, 1, st.slot);
+                *(__half2*)(dst + 2 * t) = __floats2half2_rn(x0, x1);
+            }
+        }
+    } else if (MODE == DEC_HEAD) {
+        // Logits of the tile's 128 vocabulary rows, then the first index of the maximum over
+        // the whole vocabulary (Kernels.ArgMax, Kernels.cs:146) by the last CTA to finish.
+        __shared__ float s_bv[128];
+        __shared__ int s_bi[128];
+        if (t < 128) {
+            a.y[n0 + t] = s_out[t];
+            s_bv[t] = s_out[t];
+            s_bi[t] = n0 + t;
+        }
+        __syncthreads();
+        for (int w = 64; w >= 1; w >>= 1) {
+            if (t < w && dec_better(s_bv[t + w], s_bi[t + w], s_bv[t], s_bi[t])) {
+                s_bv[t] = s_bv[t + w];
+                s_bi[t] = s_bi[t + w];
+            }
+            __syncthreads();
+        }
+        if (t == 0) {
+            a.cand_v[tile] = s_bv[0];
+            a.cand_i[tile] = s_bi[0];
+        }
+        __threadfence();
+        __syncthreads();
+        if (t == 0) s_last = atomicAdd(a.counters + gridDim.x, 1) == (int)gridDim.x - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int i = t; i < (int)gridDim.x; i += DG_THREADS) {
+            const float v = __ldcg(a.cand_v + i);
+            const int ix = __ldcg(a.cand_i + i);
+            if (dec_better(v, ix, bv, bi)) { bv = v; bi = ix; }
+        }
+        __shared__ float u_bv[DG_THREADS];
+        __shared__ int u_bi[DG_THREADS];
+        u_bv[t] = bv;
+        u_bi[t] = bi;
+        __syncthreads();
+        for (int w = DG_THREADS / 2; w >= 1; w >>= 1) {
+            if (t < w && dec_better(u_bv[t + w], u_bi[t + w], u_bv[t], u_bi[t])) {
+                u_bv[t] = u_bv[t + w];
+                u_bi[t] = u_bi[t + w];
+            }
+            __syncthreads();
+        }
+        if (t == 0) {
+            a.counters[gridDim.x] = 0;
+            const int best = u_bi[0] == 0x7fffffff ? 0 : u_bi[0];
+            if (a.argmax_out) *a.argmax_out = best;
+            if (a.advance) {
+                DecodeStep* st = a.step_rw;
+                if (a.tokens_out) a.tokens_out[st->index] = best;
+                st->token = best;
+                st->index += 1;
+                st->slot += 1;
+                st->pos += 1;
+                st->shared += 1;
+                st->segment += 1;
+                st->n_keys += 1;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ attention
+
+// One query token against its visible keys (MinistralModel.AttendHead, MinistralModel.cs:564-636):
+// CTA (kv head, split) takes logical keys [64 split, 64 split + 64) of the group's query heads
+// (one warp each): scores as an fp32 FMA chain over d times the scale, a max-shifted softmax,
+// the weighted value sum; the last CTA of the kv head merges the splits in split order.
+// Logical key L is slot L below `shared`, else slot segment + L - shared.
+constexpr int DA_KEYS = 64;
+constexpr int DA_STRIDE = 136;  // halves per staged key row (272 B: conflict-free 16-byte reads)
+
+__global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
+    __shared__ __align__(16) __half ks[DA_KEYS * DA_STRIDE];
+    __shared__ __align__(16) __half vs[DA_KEYS * 128];
+    __shared__ __align__(16) float qs[8 * 128];
+    __shared__ float ps[8 * DA_KEYS];
+    __shared__ int s_last;
+    const DecodeStep st = *a.step;
+    const int group = a.heads / a.kv_heads;
+    const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
+    const int k0 = split * DA_KEYS;
+    const int nk = max(0, min(st.n_keys, k0 + DA_KEYS) - k0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nthreads = 32 * group;
+    float* part = a.partial + ((int64_t)(kvh * group) * nsplit) * (2 + 128);
+
+    if (nk > 0) {
+        for (int i = threadIdx.x; i < group * 128; i += nthreads) qs[i] = a.q32[kvh * group * 128 + i];
+        for (int i = threadIdx.x; i < nk * 16; i += nthreads) {
+            const int key = i >> 4, c = i & 15;
+            const int L = k0 + key;
+            const int slot = L < st.shared ? L : st.segment + (L - st.shared);
+            const __half* kr = kv_slot(const_cast<__half*>(a.kv_pool), a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot);
+            const __half* vr = kv_slot(const_cast<__half*>(a.kv_pool), a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot);
+            *(int4*)(ks + key * DA_STRIDE + c * 8) = __ldg((const int4*)(kr + c * 8));
+            *(int4*)(vs + key * 128 + c * 8) = __ldg((const int4*)(vr + c * 8));
+        }
+        __syncthreads();
+        const int h = warp;
+        const float* q = qs + h * 128;
+        float mx = -INFINITY;
+        for (int i = lane; i < nk; i += 32) {
+            const __half* kr = ks + i * DA_STRIDE;
+            float acc = 0.f;
+#pragma unroll 4
+            for (int d = 0; d < 128; d += 8) {
+                int4 raw = *(const int4*)(kr + d);
+                const __half2* kh = (const __half2*)&raw;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    float2 kf = __half22float2(kh[e]);
+                    acc = fmaf(q[d + 2 * e], kf.x, acc);
+                    acc = fmaf(q[d + 2 * e + 1], kf.y, acc);
+                }
+            }
+            const float sc = acc * a.scale;
+            ps[h * DA_KEYS + i] = sc;
+            mx = fmaxf(mx, sc);
+        }
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        __syncwarp();
+        float l = 0.f;
+        for (int i = lane; i < nk; i += 32) {
+            const float p = __expf(ps[h * DA_KEYS + i] - mx);
+            ps[h * DA_KEYS + i] = p;
+            l += p;
+        }
+        for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        __syncwarp();
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int i = 0; i < nk; i++) {
+            const float p = ps[h * DA_KEYS + i];
+            uint2 raw = *(const uint2*)(vs + i * 128 + lane * 4);
+            const __half2* vh = (const __half2*)&raw;
+            float2 v01 = __half22float2(vh[0]), v23 = __half22float2(vh[1]);
+            acc[0] = fmaf(p, v01.x, acc[0]);
+            acc[1] = fmaf(p, v01.y, acc[1]);
+            acc[2] = fmaf(p, v23.x, acc[2]);
+            acc[3] = fmaf(p, v23.y, acc[3]);
+        }
+        float* dst = part + ((int64_t)h * nsplit + split) * (2 + 128);
+        if (lane == 0) { dst[0] = mx; dst[1] = l; }
+#pragma unroll
+        for (int e = 0; e < 4; e++) dst[2 + lane * 4 + e] = acc[e];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(a.counters + kvh, 1) == nsplit - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // merge the active splits in split order (k_decode_combine's arithmetic)
+    const int active = (st.n_keys + DA_KEYS - 1) / DA_KEYS;
+    for (int i = threadIdx.x; i < group * 128; i += nthreads) {
+        const int h = i >> 7, d = i & 127;
+        const float* b = part + (int64_t)h * nsplit * (2 + 128);
+        float m = -INFINITY;
+        for (int s = 0; s < active; s++) m = fmaxf(m, __ldcg(b + (int64_t)s * (2 + 128)));
+        float l = 0.f, acc = 0.f;
+        for (int s = 0; s < active; s++) {
+            const float* p = b + (int64_t)s * (2 + 128);
+            const float w = __expf(__ldcg(p) - m);
+            l += w * __ldcg(p + 1);
+            acc += w * __ldcg(p + 2 + d);
+        }
+        a.ctx32[(kvh * group + h) * 128 + d] = acc / l;
+    }
+    if (threadIdx.x == 0) a.counters[kvh] = 0;
+}
+
+template <int TYPE, int MODE, bool NORM>
+void launch_dec_typed(const DecGemvArgs& a, int splits, cudaStream_t s) {
+    const int per = (a.ksteps + splits - 1) / splits;
+    const size_t smem = (size_t)per * (64 * 4 + 32 * 8 + 2 * 4);
+    if (smem > 200 * 1024) throw Error(JV_ERR_UNSUPPORTED, "decode matvec: the K slice does not fit in shared memory");
+    static size_t configured = 48 * 1024;
+    if (smem > configured) {
+        JV_CUDA(cudaFuncSetAttribute(k_dec_gemv<TYPE, MODE, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = smem;
+    }
+    k_dec_gemv<TYPE, MODE, NORM><<<dim3(a.rows / 128, splits), DG_THREADS, smem, s>>>(a);
+}
+
+template <int MODE, bool NORM>
+void launch_dec_mode(int type, const DecGemvArgs& a, int splits, cudaStream_t s) {
+    if (type == T_Q8_0)
+        launch_dec_typed<T_Q8_0, MODE, NORM>(a, splits, s);
+    else if (type == T_Q4_0)
+        launch_dec_typed<T_Q4_0, MODE, NORM>(a, splits, s);
+    else if (type == T_Q5_1)
+        launch_dec_typed<T_Q5_1, MODE, NORM>(a, splits, s);
+    else
+        throw Error(JV_ERR_UNSUPPORTED, "decode matvec: unsupported weight type");
+}
+
+}  // namespace
+
+void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int splits, cudaStream_t s) {
+    if (a.rows % 128 != 0) throw Error(JV_ERR_UNSUPPORTED, "decode matvec: rows must be a multiple of 128");
+    switch (mode) {
+        case DEC_STORE: norm ? launch_dec_mode<DEC_STORE, true>(type, a, splits, s) : launch_dec_mode<DEC_STORE, false>(type, a, splits, s); break;
+        case DEC_ADD: launch_dec_mode<DEC_ADD, false>(type, a, splits, s); break;
+        case DEC_SWIGLU: launch_dec_mode<DEC_SWIGLU, true>(type, a, splits, s); break;
+        case DEC_QKV: launch_dec_mode<DEC_QKV, true>(type, a, splits, s); break;
+        case DEC_HEAD:
+            if (splits != 1) throw Error(JV_ERR_ARG, "decode head: one split");
+            launch_dec_mode<DEC_HEAD, true>(type, a, 1, s);
+            break;
+        default: throw Error(JV_ERR_ARG, "decode matvec: bad mode");
+    }
+    note_launch();
+}
+
+void launch_dec_attn(const DecAttnArgs& a, int splits, cudaStream_t s) {
+    const int group = a.heads / a.kv_heads;
+    if (group < 1 || group > 8 || a.heads % a.kv_heads) throw Error(JV_ERR_UNSUPPORTED, "decode attention: group size");
+    k_dec_attn<<<dim3(a.kv_heads, splits), 32 * group, 0, s>>>(a);
+    note_launch();
+}
+
+}  // namespace jv

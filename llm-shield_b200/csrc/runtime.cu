@@ -180,6 +180,12 @@ struct jv_ctx {
     DevVec<float> gemm_ws;   // split-K partials
     DevVec<int> gemm_ctr;    // split-K arrival counters (the last CTA of a tile resets its own)
     DevVec<AttnItem> items;
+    // single-token steps: arrival counters (zero between launches), head candidates, and the
+    // device-resident step of the greedy loop
+    DevVec<int> dec_ctr, dec_cand_i;
+    DevVec<float> dec_cand_v, dec_attn;
+    DevVec<DecodeStep> dec_step;
+    DevVec<int32_t> dec_tokens;
     int* d_err = nullptr;
     HostVec<int32_t> h_in;
     HostVec<float> h_out;
@@ -643,6 +649,126 @@ void gemv(jv_ctx* x, const QWeight& w, const float* v, float* y, int epi) {
     launch_gemv_reduce(part, splits, w.rows, y, epi, x->stream);
 }
 
+// One single-token step through every layer with the fused decode kernels: five launches per
+// layer (see kernels_decode.cu), then optionally the LM head with its argmax. Everything the
+// step varies by (token, slot, position, visible keys) is read from *d_step on the device.
+// attn_splits bounds the visible keys (64 per split) for every step this sequence serves.
+constexpr int DEC_ATTN_CTR = 4096;  // attention counters start here in dec_ctr
+void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool advance, int32_t* tokens_out) {
+    jv_model* m = x->m;
+    const jv_config& c = m->cfg;
+    cudaStream_t s = x->stream;
+    const int hidden = c.hidden, qdim = c.heads * c.head_dim, ff = c.ff;
+    if (c.head_dim != 128) throw Error(JV_ERR_UNSUPPORTED, "decode: head_dim must be 128");
+    const int sms = m->sm_count;
+    float* h = x->h.get(hidden);
+    float* q32 = x->q32.get(qdim);
+    float* ctx = x->ctx32.get(qdim);
+    float* act = x->act32.get(ff);
+    int* ctr = x->dec_ctr.get(DEC_ATTN_CTR + c.kv_heads);
+    size_t need = 0;
+    for (const LayerW& W : m->layers)
+        for (const QWeight* w : {&W.qkv, &W.o, &W.gu, &W.down})
+            need = std::max(need, (size_t)gemv_splits_for(*w, sms) * w->rows);
+    float* part = x->partial.get(std::max<size_t>(need, 1));
+    float* apart = x->dec_attn.get((size_t)c.heads * attn_splits * (2 + 128));
+    if (m->layers.size() && m->head.tiles + 1 > DEC_ATTN_CTR) throw Error(JV_ERR_UNSUPPORTED, "decode: vocabulary too large");
+
+    launch_embed(m->embd, &d_step->token, 1, h, hidden, x->d_err, s);
+    for (int l = 0; l < c.layers; l++) {
+        const LayerW& W = m->layers[l];
+        DecGemvArgs a;
+        a.partial = part;
+        a.counters = ctr;
+        a.eps = c.eps;
+        // 1. attn_norm + QKV + RoPE + K/V write
+        a.w = W.qkv.data;
+        a.ksteps = W.qkv.ksteps;
+        a.rows = W.qkv.rows;
+        a.in = h;
+        a.n_in = hidden;
+        a.norm_w = W.attn_norm;
+        a.step = d_step;
+        a.rope_table = m->rope_table;
+        a.heads = c.heads;
+        a.kv_heads = c.kv_heads;
+        a.layer = l;
+        a.orig_ctx = c.rope_orig_ctx;
+        a.temperature_scale = c.temperature_scale;
+        a.q32 = q32;
+        a.kv_pool = m->pool;
+        a.page_table = x->d_pages.p;
+        a.page_bytes = m->page_bytes;
+        a.page_slots = m->page_slots;
+        launch_dec_gemv(DEC_QKV, true, W.qkv.type, a, gemv_splits_for(W.qkv, sms), s);
+        // 2. attention
+        DecAttnArgs da;
+        da.q32 = q32;
+        da.kv_pool = m->pool;
+        da.page_table = x->d_pages.p;
+        da.page_bytes = m->page_bytes;
+        da.page_slots = m->page_slots;
+        da.layer = l;
+        da.heads = c.heads;
+        da.kv_heads = c.kv_heads;
+        da.scale = 1.f / std::sqrt((float)c.head_dim);
+        da.step = d_step;
+        da.partial = apart;
+        da.counters = ctr + DEC_ATTN_CTR;
+        da.ctx32 = ctx;
+        launch_dec_attn(da, attn_splits, s);
+        // 3. O + residual
+        DecGemvArgs o = a;
+        o.w = W.o.data;
+        o.ksteps = W.o.ksteps;
+        o.rows = W.o.rows;
+        o.in = ctx;
+        o.n_in = qdim;
+        o.norm_w = nullptr;
+        o.y = h;
+        launch_dec_gemv(DEC_ADD, false, W.o.type, o, gemv_splits_for(W.o, sms), s);
+        // 4. ffn_norm + gate/up + SwiGLU
+        DecGemvArgs g = a;
+        g.w = W.gu.data;
+        g.ksteps = W.gu.ksteps;
+        g.rows = W.gu.rows;
+        g.in = h;
+        g.n_in = hidden;
+        g.norm_w = W.ffn_norm;
+        g.y = act;
+        launch_dec_gemv(DEC_SWIGLU, true, W.gu.type, g, gemv_splits_for(W.gu, sms), s);
+        // 5. down + residual
+        DecGemvArgs d = a;
+        d.w = W.down.data;
+        d.ksteps = W.down.ksteps;
+        d.rows = W.down.rows;
+        d.in = act;
+        d.n_in = ff;
+        d.norm_w = nullptr;
+        d.y = h;
+        launch_dec_gemv(DEC_ADD, false, W.down.type, d, gemv_splits_for(W.down, sms), s);
+    }
+    if (head) {
+        DecGemvArgs a;
+        a.w = m->head.data;
+        a.ksteps = m->head.ksteps;
+        a.rows = m->head.rows;
+        a.in = h;
+        a.n_in = hidden;
+        a.norm_w = m->out_norm;
+        a.eps = c.eps;
+        a.y = x->logits.get(m->head.rows);
+        a.counters = ctr;
+        a.cand_v = x->dec_cand_v.get(m->head.tiles);
+        a.cand_i = x->dec_cand_i.get(m->head.tiles);
+        a.argmax_out = x->out_i32.get(1);
+        a.advance = advance ? 1 : 0;
+        a.tokens_out = tokens_out;
+        a.step_rw = d_step;
+        launch_dec_gemv(DEC_HEAD, true, m->head.type, a, 1, s);
+    }
+}
+
 // The private ForwardAsync (reference MinistralModel.cs:301-435).
 //   L == nullptr: a causal append at the cache end.
 //   rows != nullptr: selected vocab rows per output -> out[n_out][n_rows].
@@ -741,6 +867,11 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     size_t items_off = 3 * (size_t)T + n_out + (size_t)std::max(0, n_rows);
     items_off = (items_off + 7) & ~(size_t)7;  // 32-byte alignment for the item structs
     size_t total_words = items_off + n_items_words;
+    // A single token without an activation sink runs the fused decode kernels, which read
+    // the step from device memory (appended to the same upload).
+    const bool fused = decode && x->sink == nullptr;
+    const size_t step_off = (total_words + 7) & ~(size_t)7;
+    if (fused) total_words = step_off + sizeof(DecodeStep) / 4;
     int32_t* hin = x->h_in.get(total_words);
     int32_t* din = x->in_i32.get(total_words);
     std::memcpy(hin, tokens, sizeof(int32_t) * T);
@@ -749,6 +880,17 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     std::memcpy(hin + 3 * T, L->outputs.data(), sizeof(int32_t) * n_out);
     if (n_rows > 0 && rows) std::memcpy(hin + 3 * T + n_out, rows, sizeof(int32_t) * n_rows);
     if (!items.empty()) std::memcpy(hin + items_off, items.data(), items.size() * sizeof(AttnItem));
+    int dec_keys = 0;
+    if (fused) {
+        DecodeStep st{};
+        st.token = tokens[0];
+        st.slot = L->slot[0];
+        st.pos = L->pos[0];
+        st.shared = L->shared[0];
+        st.segment = L->seg[0];
+        st.n_keys = dec_keys = L->shared[0] + (L->slot[0] - L->seg[0] + 1);
+        std::memcpy(hin + step_off, &st, sizeof st);
+    }
     JV_CUDA(cudaMemcpyAsync(din, hin, sizeof(int32_t) * total_words, cudaMemcpyHostToDevice, x->stream));
     const int32_t* d_tokens = din;
     const int32_t* d_slot = din + T;
@@ -759,13 +901,19 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
 
     cudaStream_t s = x->stream;
     float* h = x->h.get((size_t)T * hidden);
-    launch_embed(m->embd, d_tokens, T, h, hidden, x->d_err, s);
-    observe(x, "embeddings", h, T, hidden);
+    if (fused) {
+        check_cancel(x);
+        decode_step(x, (DecodeStep*)(din + step_off), (dec_keys + DEC_ATTN_KEYS - 1) / DEC_ATTN_KEYS, compute_logits,
+                    false, nullptr);
+    } else {
+        launch_embed(m->embd, d_tokens, T, h, hidden, x->d_err, s);
+        observe(x, "embeddings", h, T, hidden);
+    }
 
     float* qkv32 = x->qkv32.get((size_t)T * qkvn);
     const bool capture = x->sink != nullptr;
 
-    for (int l = 0; l < c.layers; l++) {
+    for (int l = 0; l < (fused ? 0 : c.layers); l++) {
         check_cancel(x);
         const LayerW& W = m->layers[l];
         std::string p = "blk." + std::to_string(l) + ".";
@@ -939,11 +1087,13 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         int32_t last = T - 1;
         // the last row index lives in the output list for causal passes; for explicit
         // layouts use a one-word upload
-        int32_t* d_last = x->out_i32.get(1);
-        JV_CUDA(cudaMemcpyAsync(d_last, &last, sizeof(int32_t), cudaMemcpyHostToDevice, s));
-        launch_rmsnorm_rows(h, d_last, 1, m->out_norm, hidden, c.eps, normed, nullptr, 0, s);
-        observe(x, "final_norm", normed, 1, hidden);
-        gemv(x, m->head, normed, d_logits, EPI_STORE);
+        if (!fused) {  // the fused decode step already wrote the logits
+            int32_t* d_last = x->out_i32.get(1);
+            JV_CUDA(cudaMemcpyAsync(d_last, &last, sizeof(int32_t), cudaMemcpyHostToDevice, s));
+            launch_rmsnorm_rows(h, d_last, 1, m->out_norm, hidden, c.eps, normed, nullptr, 0, s);
+            observe(x, "final_norm", normed, 1, hidden);
+            gemv(x, m->head, normed, d_logits, EPI_STORE);
+        }
         observe(x, "logits", d_logits, 1, V);
         if (logits) {
             float* hres = x->h_out.get(V);

@@ -137,6 +137,23 @@ def test_decode_steps_match_the_oracle(small):
             nxt = int(np.argmax(lo))
 
 
+@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
+def test_full_width_decode_steps_match_the_oracle(model_factory, qtype):
+    """The fused single-token kernels on every real matrix shape: logits of decode steps."""
+    path = model_factory(WIDE_CFG, qtype, seed=8)
+    prompt = [1] + toks(90, 4)
+    with jv.Model(path, kv_pool_mb=512) as m, ctx(m) as c, ob.OracleModel(path) as o:
+        c.prefill(prompt)
+        o.forward(prompt, logits=False)
+        nxt = 2000
+        for step in range(3):
+            lg = c.forward([nxt])
+            lo = o.forward([nxt])
+            assert rel_l2(lg, lo) < HIDDEN_TOL, step
+            assert int(np.argmax(lg)) == int(np.argmax(lo)), step
+            nxt = int(np.argmax(lo))
+
+
 def test_decode_greedy_follows_its_own_argmax(small):
     prompt = [1] + toks(20, 19)
     with ctx(small) as a, ctx(small) as b:
