@@ -187,6 +187,7 @@ struct DecGemvArgs {
     float* y = nullptr;          // STORE/ADD: [rows]; SWIGLU: [rows / 2]; HEAD: logits [rows]
     float* partial = nullptr;    // [splits][rows]
     int* counters = nullptr;     // [tiles + 1], zero between launches
+    int* err = nullptr;          // device error word
     // DEC_QKV
     const DecodeStep* step = nullptr;
     const float2* rope_table = nullptr;
@@ -206,6 +207,7 @@ struct DecGemvArgs {
     DecodeStep* step_rw = nullptr;
 };
 void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int splits, cudaStream_t s);
+int dec_splits_for(const QWeight& w, int sm_count);
 
 struct DecAttnArgs {
     const float* q32;
@@ -216,11 +218,12 @@ struct DecAttnArgs {
     int layer, heads, kv_heads;
     float scale;
     const DecodeStep* step;
-    float* partial;   // [heads][splits][2 + 128]
+    float* partial;   // [heads][splits][DEC_ATTN_PSTRIDE]
     int* counters;    // [kv_heads], zero between launches
     float* ctx32;     // [heads * 128]
 };
-constexpr int DEC_ATTN_KEYS = 64;  // logical keys per attention split
+constexpr int DEC_ATTN_KEYS = 64;      // logical keys per attention split
+constexpr int DEC_ATTN_PSTRIDE = 132;  // floats per (head, split) partial, 16-byte multiple
 void launch_dec_attn(const DecAttnArgs& a, int splits, cudaStream_t s);
 
 void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, cudaStream_t s);

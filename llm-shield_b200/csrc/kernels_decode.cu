@@ -70,19 +70,19 @@ __device__ __forceinline__ void load_raw(Raw<TYPE>& r, const uint8_t* __restrict
 #pragma unroll
         for (int b = 0; b < 2; b++) {
             if (TYPE == T_Q8_0) {
-                uint2 v = __ldg((const uint2*)(chunk + rr * 64 + 32 * b + 8 * kq));
+                uint2 v = *(const uint2*)(chunk + rr * 64 + 32 * b + 8 * kq);
                 r.q[h][b][0] = v.x;
                 r.q[h][b][TYPE == T_Q8_0 ? 1 : 0] = v.y;
             } else {
-                r.q[h][b][0] = __ldg((const uint32_t*)(chunk + rr * 32 + 16 * b + 4 * kq));
+                r.q[h][b][0] = *(const uint32_t*)(chunk + rr * 32 + 16 * b + 4 * kq);
             }
         }
-        r.d[h] = __ldg((const uint32_t*)(chunk + qs_bytes(TYPE) + (TYPE == T_Q5_1 ? 1024 : 0) + rr * 4));
+        r.d[h] = *(const uint32_t*)(chunk + qs_bytes(TYPE) + (TYPE == T_Q5_1 ? 1024 : 0) + rr * 4);
         if (TYPE == T_Q5_1) {
-            uint2 v = __ldg((const uint2*)(chunk + 4096 + rr * 8));
+            uint2 v = *(const uint2*)(chunk + 4096 + rr * 8);
             r.qh[h][0] = v.x;
             r.qh[h][1] = v.y;
-            r.m[h] = __ldg((const uint32_t*)(chunk + 5632 + rr * 4));
+            r.m[h] = *(const uint32_t*)(chunk + 5632 + rr * 4);
         }
     }
 }
@@ -144,6 +144,50 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
     return red[32];
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start its independent
+// prologue (weight streaming) now / wait until the previous kernel's writes are visible.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void dg_mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void dg_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void dg_bulk(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ bool dg_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok)
+                 : "r"(bar), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t dg_timer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+// Bounded wait (2 s) for phase `parity` of an mbarrier; false if it never completed.
+__device__ __forceinline__ bool dg_wait(uint32_t bar, uint32_t parity) {
+    if (dg_try(bar, parity)) return true;
+    const uint64_t t0 = dg_timer();
+    while (!dg_try(bar, parity))
+        if (dg_timer() - t0 > 2000000000ull) return false;
+    return true;
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // Kernels.ArgMax / IndexOfMax order: the larger value, the first index on ties, a NaN wins.
 __device__ __forceinline__ bool dec_better(float v, int i, float bv, int bi) {
     bool vn = v != v, bn = bv != bv;
@@ -164,10 +208,11 @@ __device__ __forceinline__ __half* kv_slot(__half* pool, const int32_t* page_tab
 
 template <int TYPE, int MODE, bool NORM>
 __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
-    extern __shared__ __align__(16) uint8_t dg_smem[];
+    extern __shared__ __align__(128) uint8_t dg_smem[];
     __shared__ double red[33];
     __shared__ float s_out[128];
     __shared__ int s_last;
+    __shared__ __align__(8) uint64_t s_bar;
     const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
     const int ksteps = a.ksteps;
     const int per = (ksteps + splits - 1) / splits;
@@ -175,25 +220,59 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cb = chunk_bytes(TYPE);
 
-    float* xs = (float*)dg_smem;                        // [per*64] this CTA's slice of x
+    uint8_t* raw = dg_smem;                             // [per][chunk] this CTA's weights
+    float* xs = (float*)(dg_smem + (size_t)per * cb);   // [per*64] this CTA's slice of x
     uint2* xf = (uint2*)(xs + per * 64);                // [per][2 blocks][2 subs][8 lanes]
     float* sx = (float*)(xf + per * 32);                // [per][2] block sums of x (Q5_1)
 
+    // The weight slice is one contiguous run of chunks: stream it into shared memory first,
+    // before waiting for the previous kernel (the weights do not depend on it).
+    const uint32_t bar = smem_u32(&s_bar);
+    const uint8_t* __restrict__ src = a.w + ((int64_t)tile * ksteps + ks0) * cb;
+    if (threadIdx.x == 0) {
+        dg_mbar_init(bar, 1);
+        if (nk > 0) {
+            dg_expect_tx(bar, (uint32_t)(nk * cb));
+            for (int i = 0; i < nk; i++) dg_bulk(smem_u32(raw + (size_t)i * cb), src + (size_t)i * cb, (uint32_t)cb, bar);
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+
     // ---- x: the CTA's K slice, RMS-normalised first when NORM (Kernels.RmsNorm, Kernels.cs:25-60)
+    // Every load of a pass is issued before any is used (16-byte loads, fixed batches), so a
+    // pass costs one memory round trip.
     float scale = 1.f;
     if (NORM) {
+        const float4* in4 = (const float4*)a.in;
+        const int n4 = a.n_in >> 2;
         double s = 0;
-        for (int k = threadIdx.x; k < a.n_in; k += DG_THREADS) {
-            float v = a.in[k];
-            s += (double)v * (double)v;
+        for (int b0 = threadIdx.x; b0 < n4; b0 += 4 * DG_THREADS) {
+            float4 v[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) v[j] = b0 + j * DG_THREADS < n4 ? in4[b0 + j * DG_THREADS] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                s += (double)v[j].x * v[j].x + (double)v[j].y * v[j].y + (double)v[j].z * v[j].z + (double)v[j].w * v[j].w;
         }
         s = block_sum_d(s, red);
         scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / a.n_in), a.eps)));
     }
-    for (int i = threadIdx.x; i < nk * 64; i += DG_THREADS) {
-        const int k = ks0 * 64 + i;
-        const float v = a.in[k];
-        xs[i] = NORM ? __fmul_rn(__fmul_rn(v, scale), a.norm_w[k]) : v;
+    {
+        const float4* in4 = (const float4*)(a.in + ks0 * 64);
+        const float4* w4 = NORM ? (const float4*)(a.norm_w + ks0 * 64) : nullptr;
+        float4* xs4 = (float4*)xs;
+        for (int i = threadIdx.x; i < nk * 16; i += DG_THREADS) {
+            float4 v = in4[i];
+            if (NORM) {
+                const float4 w = w4[i];
+                v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
+                v.y = __fmul_rn(__fmul_rn(v.y, scale), w.y);
+                v.z = __fmul_rn(__fmul_rn(v.z, scale), w.z);
+                v.w = __fmul_rn(__fmul_rn(v.w, scale), w.w);
+            }
+            xs4[i] = v;
+        }
     }
     __syncthreads();
     // B fragments: column 0 = fp16(x), column 1 = fp16(x - column 0); lanes 0-3 / 4-7.
@@ -222,10 +301,17 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
         }
     __syncthreads();
 
+    if (nk > 0 && !dg_wait(bar, 0)) {
+        // the copy never landed: report, and do not leave while it may still be writing
+        if (threadIdx.x == 0) atomicExch(a.err, JV_ERR_DEVICE_TIMEOUT);
+        dg_wait(bar, 0);
+        return;
+    }
+
     // ---- main loop: warp w owns rows 16w + g and 16w + g + 8 of the tile
     const int g = lane >> 2, kq = lane & 3;
     const int row = 16 * warp + g;
-    const uint8_t* __restrict__ base = a.w + ((int64_t)tile * ksteps + ks0) * cb;
+    const uint8_t* base = raw;
     float acc[2] = {0.f, 0.f};
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k0 = 0; k0 < nk; k0 += DG_UNROLL) {
@@ -284,8 +370,17 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
         if (!s_last) return;
         __threadfence();
         if (threadIdx.x < 128) {
+            // in split order, eight loads in flight at a time
             float s = 0.f;
-            for (int p = 0; p < splits; p++) s = __fadd_rn(s, __ldcg(a.partial + (int64_t)p * a.rows + n0 + threadIdx.x));
+            for (int p0 = 0; p0 < splits; p0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    v[j] = p0 + j < splits ? __ldcg(a.partial + (int64_t)(p0 + j) * a.rows + n0 + threadIdx.x) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (p0 + j < splits) s = __fadd_rn(s, v[j]);
+            }
             s_out[threadIdx.x] = s;
         }
         if (threadIdx.x == 0) a.counters[tile] = 0;  // ready for the next launch
@@ -412,6 +507,7 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
 // Logical key L is slot L below `shared`, else slot segment + L - shared.
 constexpr int DA_KEYS = 64;
 constexpr int DA_STRIDE = 136;  // halves per staged key row (272 B: conflict-free 16-byte reads)
+constexpr int DA_PSTRIDE = DEC_ATTN_PSTRIDE;  // floats per split partial: m, l, pad, pad, acc[128]
 
 __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
     __shared__ __align__(16) __half ks[DA_KEYS * DA_STRIDE];
@@ -419,6 +515,10 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
     __shared__ __align__(16) float qs[8 * 128];
     __shared__ float ps[8 * DA_KEYS];
     __shared__ int s_last;
+    __shared__ const __half* krow[DA_KEYS];
+    __shared__ const __half* vrow[DA_KEYS];
+    pdl_launch_dependents();
+    pdl_wait();
     const DecodeStep st = *a.step;
     const int group = a.heads / a.kv_heads;
     const int kvh = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
@@ -426,19 +526,26 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
     const int nk = max(0, min(st.n_keys, k0 + DA_KEYS) - k0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nthreads = 32 * group;
-    float* part = a.partial + ((int64_t)(kvh * group) * nsplit) * (2 + 128);
+    float* part = a.partial + ((int64_t)(kvh * group) * nsplit) * DA_PSTRIDE;
 
     if (nk > 0) {
+        // rows of the split's keys first (one page-table lookup per key), then every 16-byte
+        // piece of them in flight at once
+        if ((int)threadIdx.x < nk) {
+            const int L = k0 + threadIdx.x;
+            const int slot = L < st.shared ? L : st.segment + (L - st.shared);
+            __half* pool = const_cast<__half*>(a.kv_pool);
+            krow[threadIdx.x] = kv_slot(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot);
+            vrow[threadIdx.x] = kv_slot(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot);
+        }
         for (int i = threadIdx.x; i < group * 128; i += nthreads) qs[i] = a.q32[kvh * group * 128 + i];
+        __syncthreads();
         for (int i = threadIdx.x; i < nk * 16; i += nthreads) {
             const int key = i >> 4, c = i & 15;
-            const int L = k0 + key;
-            const int slot = L < st.shared ? L : st.segment + (L - st.shared);
-            const __half* kr = kv_slot(const_cast<__half*>(a.kv_pool), a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot);
-            const __half* vr = kv_slot(const_cast<__half*>(a.kv_pool), a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot);
-            *(int4*)(ks + key * DA_STRIDE + c * 8) = __ldg((const int4*)(kr + c * 8));
-            *(int4*)(vs + key * 128 + c * 8) = __ldg((const int4*)(vr + c * 8));
+            cp_async16(ks + key * DA_STRIDE + c * 8, krow[key] + c * 8);
+            cp_async16(vs + key * 128 + c * 8, vrow[key] + c * 8);
         }
+        cp_async_wait_all();
         __syncthreads();
         const int h = warp;
         const float* q = qs + h * 128;
@@ -482,10 +589,9 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
             acc[2] = fmaf(p, v23.x, acc[2]);
             acc[3] = fmaf(p, v23.y, acc[3]);
         }
-        float* dst = part + ((int64_t)h * nsplit + split) * (2 + 128);
+        float* dst = part + ((int64_t)h * nsplit + split) * DA_PSTRIDE;
         if (lane == 0) { dst[0] = mx; dst[1] = l; }
-#pragma unroll
-        for (int e = 0; e < 4; e++) dst[2 + lane * 4 + e] = acc[e];
+        *(float4*)(dst + 4 + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     }
     __threadfence();
     __syncthreads();
@@ -493,36 +599,79 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // merge the active splits in split order (k_decode_combine's arithmetic)
+    // Merge the active splits in split order (k_decode_combine's arithmetic). Warp h merges
+    // query head h: the maximum over splits with the lanes striding the splits, then each
+    // lane's four dimensions with eight splits' loads in flight at a time.
     const int active = (st.n_keys + DA_KEYS - 1) / DA_KEYS;
-    for (int i = threadIdx.x; i < group * 128; i += nthreads) {
-        const int h = i >> 7, d = i & 127;
-        const float* b = part + (int64_t)h * nsplit * (2 + 128);
+    {
+        const int h = warp;
+        const float* hb = part + (int64_t)h * nsplit * DA_PSTRIDE;
         float m = -INFINITY;
-        for (int s = 0; s < active; s++) m = fmaxf(m, __ldcg(b + (int64_t)s * (2 + 128)));
-        float l = 0.f, acc = 0.f;
-        for (int s = 0; s < active; s++) {
-            const float* p = b + (int64_t)s * (2 + 128);
-            const float w = __expf(__ldcg(p) - m);
-            l += w * __ldcg(p + 1);
-            acc += w * __ldcg(p + 2 + d);
+        for (int sp = lane; sp < active; sp += 32) m = fmaxf(m, __ldcg(hb + (int64_t)sp * DA_PSTRIDE));
+        for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s0 = 0; s0 < active; s0 += 8) {
+            float mv[8], lv[8];
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float* p = hb + (int64_t)(s0 + j) * DA_PSTRIDE;
+                const bool ok = s0 + j < active;
+                mv[j] = ok ? __ldcg(p) : 0.f;
+                lv[j] = ok ? __ldcg(p + 1) : 0.f;
+                v[j] = ok ? __ldcg((const float4*)(p + 4 + lane * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (s0 + j >= active) break;
+                const float w = __expf(mv[j] - m);
+                l += w * lv[j];
+                acc[0] += w * v[j].x;
+                acc[1] += w * v[j].y;
+                acc[2] += w * v[j].z;
+                acc[3] += w * v[j].w;
+            }
         }
-        a.ctx32[(kvh * group + h) * 128 + d] = acc / l;
+        float* out = a.ctx32 + (kvh * group + h) * 128 + lane * 4;
+#pragma unroll
+        for (int e = 0; e < 4; e++) out[e] = acc[e] / l;
     }
     if (threadIdx.x == 0) a.counters[kvh] = 0;
 }
 
+// Launch with programmatic stream serialization: the kernel's CTAs may start while the
+// previous kernel finishes; each one streams its weights, then waits for that kernel.
+template <class K, class A>
+void launch_pdl(K kernel, dim3 grid, int threads, size_t smem, cudaStream_t s, const A& args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    JV_CUDA(cudaLaunchKernelEx(&cfg, kernel, args));
+}
+
+template <int TYPE>
+size_t dec_smem(int ksteps, int splits) {
+    const int per = (ksteps + splits - 1) / splits;
+    return (size_t)per * (chunk_bytes(TYPE) + 64 * 4 + 32 * 8 + 2 * 4);
+}
+
 template <int TYPE, int MODE, bool NORM>
 void launch_dec_typed(const DecGemvArgs& a, int splits, cudaStream_t s) {
-    const int per = (a.ksteps + splits - 1) / splits;
-    const size_t smem = (size_t)per * (64 * 4 + 32 * 8 + 2 * 4);
+    const size_t smem = dec_smem<TYPE>(a.ksteps, splits);
     if (smem > 200 * 1024) throw Error(JV_ERR_UNSUPPORTED, "decode matvec: the K slice does not fit in shared memory");
     static size_t configured = 48 * 1024;
     if (smem > configured) {
         JV_CUDA(cudaFuncSetAttribute(k_dec_gemv<TYPE, MODE, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured = smem;
     }
-    k_dec_gemv<TYPE, MODE, NORM><<<dim3(a.rows / 128, splits), DG_THREADS, smem, s>>>(a);
+    launch_pdl(k_dec_gemv<TYPE, MODE, NORM>, dim3(a.rows / 128, splits), DG_THREADS, smem, s, a);
 }
 
 template <int MODE, bool NORM>
@@ -539,6 +688,15 @@ void launch_dec_mode(int type, const DecGemvArgs& a, int splits, cudaStream_t s)
 
 }  // namespace
 
+int dec_splits_for(const QWeight& w, int sm_count) {
+    // about three CTAs per SM, and a weight slice of at most 64 KB so that three fit
+    int splits = gemv_splits_for(w, sm_count);
+    const int cb = chunk_bytes(w.type);
+    const int max_per = std::max(1, (64 * 1024) / cb);
+    splits = std::max(splits, (w.ksteps + max_per - 1) / max_per);
+    return std::min(splits, w.ksteps);
+}
+
 void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int splits, cudaStream_t s) {
     if (a.rows % 128 != 0) throw Error(JV_ERR_UNSUPPORTED, "decode matvec: rows must be a multiple of 128");
     switch (mode) {
@@ -546,10 +704,7 @@ void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int sp
         case DEC_ADD: launch_dec_mode<DEC_ADD, false>(type, a, splits, s); break;
         case DEC_SWIGLU: launch_dec_mode<DEC_SWIGLU, true>(type, a, splits, s); break;
         case DEC_QKV: launch_dec_mode<DEC_QKV, true>(type, a, splits, s); break;
-        case DEC_HEAD:
-            if (splits != 1) throw Error(JV_ERR_ARG, "decode head: one split");
-            launch_dec_mode<DEC_HEAD, true>(type, a, 1, s);
-            break;
+        case DEC_HEAD: launch_dec_mode<DEC_HEAD, true>(type, a, splits, s); break;
         default: throw Error(JV_ERR_ARG, "decode matvec: bad mode");
     }
     note_launch();
@@ -558,7 +713,7 @@ void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int sp
 void launch_dec_attn(const DecAttnArgs& a, int splits, cudaStream_t s) {
     const int group = a.heads / a.kv_heads;
     if (group < 1 || group > 8 || a.heads % a.kv_heads) throw Error(JV_ERR_UNSUPPORTED, "decode attention: group size");
-    k_dec_attn<<<dim3(a.kv_heads, splits), 32 * group, 0, s>>>(a);
+    launch_pdl(k_dec_attn, dim3(a.kv_heads, splits), 32 * group, 0, s, a);
     note_launch();
 }
 

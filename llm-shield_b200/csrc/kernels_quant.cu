@@ -105,14 +105,17 @@ __global__ void k_embed(const uint8_t* __restrict__ data, int type, int ksteps, 
     int t = blockIdx.x;
     int id = ids[t];
     if ((unsigned)id >= (unsigned)vocab) {
-        if (threadIdx.x == 0) atomicExch(err, JV_ERR_RANGE);
+        if (threadIdx.x == 0 && blockIdx.y == 0) atomicExch(err, JV_ERR_RANGE);
         return;
     }
-    for (int k = threadIdx.x; k < hidden; k += blockDim.x) h[(int64_t)t * hidden + k] = dq_element(data, type, ksteps, id, k);
+    for (int k = blockIdx.y * blockDim.x + threadIdx.x; k < hidden; k += gridDim.y * blockDim.x)
+        h[(int64_t)t * hidden + k] = dq_element(data, type, ksteps, id, k);
 }
 
 void launch_embed(const QWeight& table, const int32_t* ids, int T, float* h, int hidden, int* err, cudaStream_t s) {
-    k_embed<<<T, 256, 0, s>>>(table.data, table.type, table.ksteps, table.rows, ids, h, hidden, err);
+    // a single row gets one CTA per 256 elements; many rows, one CTA each
+    dim3 grid(T, T < 16 ? (hidden + 255) / 256 : 1);
+    k_embed<<<grid, 256, 0, s>>>(table.data, table.type, table.ksteps, table.rows, ids, h, hidden, err);
     note_launch();
 }
 

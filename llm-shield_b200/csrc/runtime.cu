@@ -186,6 +186,10 @@ struct jv_ctx {
     DevVec<float> dec_cand_v, dec_attn;
     DevVec<DecodeStep> dec_step;
     DevVec<int32_t> dec_tokens;
+    // jv_decode_greedy replays one captured step; the capture is valid while every buffer it
+    // names (and the attention split count) is unchanged
+    cudaGraphExec_t dec_graph = nullptr;
+    std::vector<const void*> dec_graph_sig;
     int* d_err = nullptr;
     HostVec<int32_t> h_in;
     HostVec<float> h_out;
@@ -669,9 +673,10 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
     size_t need = 0;
     for (const LayerW& W : m->layers)
         for (const QWeight* w : {&W.qkv, &W.o, &W.gu, &W.down})
-            need = std::max(need, (size_t)gemv_splits_for(*w, sms) * w->rows);
+            need = std::max(need, (size_t)dec_splits_for(*w, sms) * w->rows);
+    if (head) need = std::max(need, (size_t)dec_splits_for(m->head, sms) * m->head.rows);
     float* part = x->partial.get(std::max<size_t>(need, 1));
-    float* apart = x->dec_attn.get((size_t)c.heads * attn_splits * (2 + 128));
+    float* apart = x->dec_attn.get((size_t)c.heads * attn_splits * DEC_ATTN_PSTRIDE);
     if (m->layers.size() && m->head.tiles + 1 > DEC_ATTN_CTR) throw Error(JV_ERR_UNSUPPORTED, "decode: vocabulary too large");
 
     launch_embed(m->embd, &d_step->token, 1, h, hidden, x->d_err, s);
@@ -680,6 +685,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         DecGemvArgs a;
         a.partial = part;
         a.counters = ctr;
+        a.err = x->d_err;
         a.eps = c.eps;
         // 1. attn_norm + QKV + RoPE + K/V write
         a.w = W.qkv.data;
@@ -700,7 +706,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         a.page_table = x->d_pages.p;
         a.page_bytes = m->page_bytes;
         a.page_slots = m->page_slots;
-        launch_dec_gemv(DEC_QKV, true, W.qkv.type, a, gemv_splits_for(W.qkv, sms), s);
+        launch_dec_gemv(DEC_QKV, true, W.qkv.type, a, dec_splits_for(W.qkv, sms), s);
         // 2. attention
         DecAttnArgs da;
         da.q32 = q32;
@@ -726,7 +732,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         o.n_in = qdim;
         o.norm_w = nullptr;
         o.y = h;
-        launch_dec_gemv(DEC_ADD, false, W.o.type, o, gemv_splits_for(W.o, sms), s);
+        launch_dec_gemv(DEC_ADD, false, W.o.type, o, dec_splits_for(W.o, sms), s);
         // 4. ffn_norm + gate/up + SwiGLU
         DecGemvArgs g = a;
         g.w = W.gu.data;
@@ -736,7 +742,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         g.n_in = hidden;
         g.norm_w = W.ffn_norm;
         g.y = act;
-        launch_dec_gemv(DEC_SWIGLU, true, W.gu.type, g, gemv_splits_for(W.gu, sms), s);
+        launch_dec_gemv(DEC_SWIGLU, true, W.gu.type, g, dec_splits_for(W.gu, sms), s);
         // 5. down + residual
         DecGemvArgs d = a;
         d.w = W.down.data;
@@ -746,10 +752,12 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         d.n_in = ff;
         d.norm_w = nullptr;
         d.y = h;
-        launch_dec_gemv(DEC_ADD, false, W.down.type, d, gemv_splits_for(W.down, sms), s);
+        launch_dec_gemv(DEC_ADD, false, W.down.type, d, dec_splits_for(W.down, sms), s);
     }
     if (head) {
         DecGemvArgs a;
+        a.err = x->d_err;
+        a.partial = part;
         a.w = m->head.data;
         a.ksteps = m->head.ksteps;
         a.rows = m->head.rows;
@@ -765,7 +773,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         a.advance = advance ? 1 : 0;
         a.tokens_out = tokens_out;
         a.step_rw = d_step;
-        launch_dec_gemv(DEC_HEAD, true, m->head.type, a, 1, s);
+        launch_dec_gemv(DEC_HEAD, true, m->head.type, a, dec_splits_for(m->head, sms), s);
     }
 }
 
@@ -1264,6 +1272,11 @@ void jv_ctx_destroy(jv_ctx* x) {
     for (auto* v : {&x->h, &x->qkv32, &x->gu32, &x->tmp32, &x->q32, &x->ctx32, &x->x32, &x->act32, &x->k32, &x->partial,
                     &x->out32, &x->logits, &x->cap32})
         v->release();
+    if (x->dec_graph) cudaGraphExecDestroy(x->dec_graph);
+    for (auto* v : {&x->dec_ctr, &x->dec_cand_i, &x->dec_tokens}) v->release();
+    x->dec_cand_v.release();
+    x->dec_attn.release();
+    x->dec_step.release();
     x->xs.release();
     x->gemm_ws.release();
     x->gemm_ctr.release();
@@ -1374,15 +1387,88 @@ int jv_forward_layout(jv_ctx* x, const int32_t* tokens, int32_t n, const jv_layo
 int jv_decode_greedy(jv_ctx* x, int32_t first_token, int32_t steps, int32_t* out_tokens) {
     if (!x || !out_tokens) return set_error(JV_ERR_ARG, "NULL argument");
     return guarded([&] {
-        int32_t tok = first_token;
-        for (int i = 0; i < steps; i++) {
-            forward(x, &tok, 1, nullptr, nullptr, 0, false, nullptr, true, nullptr);
-            int32_t* d_next = x->out_i32.get(1);
-            launch_argmax(x->logits.p, x->m->head.rows, d_next, x->stream);
-            JV_CUDA(cudaMemcpyAsync(&out_tokens[i], d_next, sizeof(int32_t), cudaMemcpyDeviceToHost, x->stream));
-            JV_CUDA(cudaStreamSynchronize(x->stream));
-            tok = out_tokens[i];
+        if (steps <= 0) return;
+        jv_model* m = x->m;
+        set_device(m);
+        if (x->sink) {  // activation capture: the step-by-step path, every activation observed
+            int32_t tok = first_token;
+            for (int i = 0; i < steps; i++) {
+                forward(x, &tok, 1, nullptr, nullptr, 0, false, nullptr, true, nullptr);
+                int32_t* d_next = x->out_i32.get(1);
+                launch_argmax(x->logits.p, m->head.rows, d_next, x->stream);
+                JV_CUDA(cudaMemcpyAsync(&out_tokens[i], d_next, sizeof(int32_t), cudaMemcpyDeviceToHost, x->stream));
+                JV_CUDA(cudaStreamSynchronize(x->stream));
+                tok = out_tokens[i];
+            }
+            return;
         }
+        // Device-resident loop: the head kernel writes each argmax into the step record, which
+        // the next step's embedding reads; the host only launches.
+        if ((unsigned)first_token >= (unsigned)m->embd.rows)
+            throw Error(JV_ERR_RANGE, "Token id " + std::to_string(first_token) + " is outside the " +
+                                          std::to_string(m->embd.rows) + "-entry embedding table.");
+        const int start = x->length, end = start + steps;
+        if (end > m->rope_positions) throw Error(JV_ERR_RANGE, "position " + std::to_string(end - 1) + " is beyond the model's context window");
+        ctx_ensure_capacity(x, end);
+        std::vector<int> wp;
+        for (int p = start / m->page_slots; p <= (end - 1) / m->page_slots; p++) wp.push_back(p);
+        ctx_make_writable(x, wp);
+        ctx_upload_pages(x);
+        cudaStream_t s = x->stream;
+        DecodeStep* d_step = x->dec_step.get(1);
+        int32_t* d_toks = x->dec_tokens.get((size_t)steps);
+        DecodeStep st{};
+        st.token = first_token;
+        st.slot = st.pos = st.shared = st.segment = start;
+        st.n_keys = start + 1;
+        int32_t* hst = x->h_in.get(sizeof(DecodeStep) / 4);
+        std::memcpy(hst, &st, sizeof st);
+        JV_CUDA(cudaMemcpyAsync(d_step, hst, sizeof st, cudaMemcpyHostToDevice, s));
+        const int splits = (end + DEC_ATTN_KEYS - 1) / DEC_ATTN_KEYS;
+        const int64_t l0 = launches_total();
+        decode_step(x, d_step, splits, true, true, d_toks);
+        const int64_t per_step = launches_total() - l0;
+        if (steps > 1) {
+            std::vector<const void*> sig = {x->h.p, x->q32.p, x->ctx32.p, x->act32.p, x->partial.p, x->dec_attn.p,
+                                            x->dec_ctr.p, x->logits.p, x->dec_cand_v.p, x->dec_cand_i.p, x->out_i32.p,
+                                            x->d_pages.p, d_step, d_toks, (const void*)(intptr_t)splits};
+            if (!x->dec_graph || sig != x->dec_graph_sig) {
+                if (x->dec_graph) cudaGraphExecDestroy(x->dec_graph);
+                x->dec_graph = nullptr;
+                cudaGraph_t g = nullptr;
+                JV_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+                try {
+                    decode_step(x, d_step, splits, true, true, d_toks);
+                } catch (...) {
+                    cudaStreamEndCapture(s, &g);
+                    if (g) cudaGraphDestroy(g);
+                    throw;
+                }
+                JV_CUDA(cudaStreamEndCapture(s, &g));
+                note_launch(-(int)per_step);  // captured, not run
+                cudaError_t e = cudaGraphInstantiate(&x->dec_graph, g, 0);
+                cudaGraphDestroy(g);
+                if (e != cudaSuccess) {
+                    x->dec_graph = nullptr;
+                    JV_CUDA(e);
+                }
+                x->dec_graph_sig = sig;
+            }
+            for (int i = 1; i < steps; i++) {
+                if (x->cancel && *x->cancel) {
+                    sync_check(x);
+                    x->length = start + i;
+                    throw Error(JV_ERR_CANCELLED, "The operation was canceled.");
+                }
+                JV_CUDA(cudaGraphLaunch(x->dec_graph, s));
+                note_launch((int)per_step);
+            }
+        }
+        float* hres = x->h_out.get((size_t)steps);
+        JV_CUDA(cudaMemcpyAsync(hres, d_toks, sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, s));
+        sync_check(x);
+        std::memcpy(out_tokens, hres, sizeof(int32_t) * steps);
+        x->length = end;
     });
 }
 
