@@ -441,19 +441,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                         for (int j = 0; j < 16; j++) cur[j] = nxt[j];
                     }
                 }
-                __threadfence();
-                epi_bar();
-                if (warp == 4 && lane == 0) {
-                    int* ctr = g_ctr + tile * ttiles + tt;
-                    int old = atomicAdd(ctr, 1);
-                    int is_last = old == splits - 1;
-                    if (is_last) atomicExch(ctr, 0);
-                    *last_flag = is_last;
+                if (epi == EPI_PARTIAL) {  // the consumer adds both halves
+                    last = false;
+                } else {
+                    __threadfence();
+                    epi_bar();
+                    if (warp == 4 && lane == 0) {
+                        int* ctr = g_ctr + tile * ttiles + tt;
+                        int old = atomicAdd(ctr, 1);
+                        int is_last = old == splits - 1;
+                        if (is_last) atomicExch(ctr, 0);
+                        *last_flag = is_last;
+                    }
+                    epi_bar();
+                    last = *last_flag != 0;
+                    epi_bar();  // the flag is re-used by the next unit
+                    if (last) __threadfence();
                 }
-                epi_bar();
-                last = *last_flag != 0;
-                epi_bar();  // the flag is re-used by the next unit
-                if (last) __threadfence();
             }
             if (last) {
                 uint32_t cur[16], nxt[16];

@@ -73,7 +73,9 @@ __host__ __device__ inline size_t kslab_offset(int t, int k, int tpad) {
 
 // EPI_SWIGLU: the fused gate/up matrix (each 128-row tile = 64 gate rows then the 64 matching
 // up rows) -> silu(gate) * up written as the fp16 K-slab operand of the down projection.
-enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+// EPI_PARTIAL (K split in two): each half writes its fp32 partial to ws[split] and nothing
+// else; the consumer (the next RMSNorm) adds h += ws[0] + ws[1] as it reads h.
+enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3 };
 
 struct GemmArgs {
     const QWeight* w;
@@ -104,6 +106,12 @@ void launch_repack(const uint8_t* raw, int type, int rows, int cols, int64_t raw
 void launch_embed(const QWeight& table, const int32_t* ids, int T, float* h, int hidden, int* err, cudaStream_t s);
 void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __half* xs, int tpad, float* out32,
                     cudaStream_t s);
+// Prefill RMSNorm into the fp16 K-slab, first folding a pending split-K residual into h
+// (h += resid[0] + resid[1] when resid != nullptr, resid = [2][T][n]).
+void launch_rmsnorm_resid(float* h, const float* resid, const float* w, int T, int n, float eps, __half* xs, int tpad,
+                          cudaStream_t s);
+// h += resid[0] + resid[1] (resid = [2][T][n]).
+void launch_resid_add(float* h, const float* resid, int64_t count, cudaStream_t s);
 void launch_rmsnorm_rows(const float* h, const int32_t* rows, int n_rows, const float* w, int n, float eps,
                          float* out32, __half* xs, int tpad, cudaStream_t s);
 void launch_gemm(const GemmArgs& a, cudaStream_t s);

@@ -59,6 +59,73 @@ void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __h
     note_launch();
 }
 
+// The prefill RMSNorm: one row per CTA, each thread holding up to RN_VEC float4 of the row
+// in registers (one load pass, one store pass). With `resid`, the row is first completed
+// with the split-K partials of the projection that produced it: h = h + (p0 + p1), the same
+// value the one-pass epilogue computes. Sum of squares in double, per thread then a fixed
+// tree, as in rmsnorm_row.
+constexpr int RN_VEC = 4;
+__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_resid(float* __restrict__ h, const float* __restrict__ resid,
+                                                                 const float* __restrict__ w, int n, float eps,
+                                                                 __half* __restrict__ xs, int tpad, int64_t plane) {
+    __shared__ double red[33];
+    const int t = blockIdx.x, n4 = n >> 2;
+    float4* hr = (float4*)(h + (int64_t)t * n);
+    const float4* p0 = resid ? (const float4*)(resid + (int64_t)t * n) : nullptr;
+    const float4* p1 = resid ? (const float4*)(resid + plane + (int64_t)t * n) : nullptr;
+    float4 v[RN_VEC];
+    double s = 0;
+#pragma unroll
+    for (int j = 0; j < RN_VEC; j++) {
+        const int i = threadIdx.x + j * NORM_THREADS;
+        if (i < n4) {
+            v[j] = hr[i];
+            if (resid) {
+                const float4 a = p0[i], b = p1[i];
+                v[j].x = __fadd_rn(v[j].x, __fadd_rn(a.x, b.x));
+                v[j].y = __fadd_rn(v[j].y, __fadd_rn(a.y, b.y));
+                v[j].z = __fadd_rn(v[j].z, __fadd_rn(a.z, b.z));
+                v[j].w = __fadd_rn(v[j].w, __fadd_rn(a.w, b.w));
+                hr[i] = v[j];
+            }
+            s += (double)v[j].x * v[j].x + (double)v[j].y * v[j].y + (double)v[j].z * v[j].z + (double)v[j].w * v[j].w;
+        }
+    }
+    s = block_sum_double(s, red);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / n), eps)));
+    const float4* w4 = (const float4*)w;
+#pragma unroll
+    for (int j = 0; j < RN_VEC; j++) {
+        const int i = threadIdx.x + j * NORM_THREADS;
+        if (i < n4) {
+            const float4 g = w4[i];
+            __half2 lo = __floats2half2_rn(__fmul_rn(__fmul_rn(v[j].x, scale), g.x), __fmul_rn(__fmul_rn(v[j].y, scale), g.y));
+            __half2 hi = __floats2half2_rn(__fmul_rn(__fmul_rn(v[j].z, scale), g.z), __fmul_rn(__fmul_rn(v[j].w, scale), g.w));
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&lo);
+            pk.y = *reinterpret_cast<uint32_t*>(&hi);
+            *(uint2*)(xs + kslab_offset(t, 4 * i, tpad)) = pk;
+        }
+    }
+}
+
+void launch_rmsnorm_resid(float* h, const float* resid, const float* w, int T, int n, float eps, __half* xs, int tpad,
+                          cudaStream_t s) {
+    if (n % 4 != 0 || n > 4 * RN_VEC * NORM_THREADS) throw Error(JV_ERR_UNSUPPORTED, "rmsnorm: row width");
+    k_rmsnorm_resid<<<T, NORM_THREADS, 0, s>>>(h, resid, w, n, eps, xs, tpad, (int64_t)T * n);
+    note_launch();
+}
+
+__global__ void k_resid_add(float* __restrict__ h, const float* __restrict__ resid, int64_t count) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) h[i] = __fadd_rn(h[i], __fadd_rn(resid[i], resid[count + i]));
+}
+
+void launch_resid_add(float* h, const float* resid, int64_t count, cudaStream_t s) {
+    k_resid_add<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(h, resid, count);
+    note_launch();
+}
+
 // RMSNorm of selected rows (the output rows of a tree/rows pass, MinistralModel.cs:371-373,396).
 __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_rows(const float* __restrict__ h, const int32_t* __restrict__ rows,
                                                                 const float* __restrict__ w, int n, float eps,

@@ -645,6 +645,34 @@ void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float*
         launch_gemm(a, x->stream);
 }
 
+// h += W xs for the residual projections (O, down). With a two-way K split the halves are not
+// combined here: each writes its partial and the returned buffer ([2][T][ldy]) is added into
+// h by the next RMSNorm (launch_rmsnorm_resid), which reads h anyway. Returns nullptr when h
+// was updated in place (no split, or the CUDA-core check product).
+const float* gemm_resid(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float* h, int ldy) {
+    static const bool use_ref = getenv("JV_GEMM_REFERENCE") != nullptr;
+    if (use_ref || gemm_splits_for(w) != 2) {
+        gemm(x, w, xs, T, tpad, h, ldy, EPI_ADD);
+        return nullptr;
+    }
+    GemmArgs a;
+    a.w = &w;
+    a.x = xs;
+    a.T = T;
+    a.tpad = tpad;
+    a.bn = gemm_bn_for(T);
+    a.y = h;
+    a.ldy = ldy;
+    a.epilogue = EPI_PARTIAL;
+    a.err = x->d_err;
+    a.splits = 2;
+    a.ws = x->gemm_ws.get((size_t)2 * T * ldy);
+    a.counters = x->gemm_ctr.get((size_t)w.tiles * (tpad / a.bn));
+    ProfScope ps(x, JV_PROF_GEMM, 2.0 * T * w.rows * w.cols, weight_bytes(w) + 2.0 * T * w.cols + 8.0 * T * w.rows);
+    launch_gemm(a, x->stream);
+    return a.ws;
+}
+
 void gemv(jv_ctx* x, const QWeight& w, const float* v, float* y, int epi) {
     int splits = gemv_splits_for(w, x->m->sm_count);
     float* part = x->partial.get((size_t)splits * w.rows);
@@ -920,6 +948,8 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
 
     float* qkv32 = x->qkv32.get((size_t)T * qkvn);
     const bool capture = x->sink != nullptr;
+    // split-K partials of the last O / down projection not yet added into h (see gemm_resid)
+    const float* resid = nullptr;
 
     for (int l = 0; l < (fused ? 0 : c.layers); l++) {
         check_cancel(x);
@@ -1002,7 +1032,10 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
             continue;
         }
         __half* xs = x->xs.get((size_t)tpad * hidden);
-        launch_rmsnorm(h, W.attn_norm, T, hidden, c.eps, xs, tpad, nullptr, s);
+        if (capture)
+            launch_rmsnorm(h, W.attn_norm, T, hidden, c.eps, xs, tpad, nullptr, s);
+        else
+            launch_rmsnorm_resid(h, resid, W.attn_norm, T, hidden, c.eps, xs, tpad, s);
         observe_kslab(x, p + "attn_norm", xs, T, hidden, tpad);
         gemm(x, W.qkv, xs, T, tpad, qkv32, qkvn, EPI_STORE);
         ra.q16 = x->q16.get((size_t)T * qdim);
@@ -1039,10 +1072,14 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
             observe(x, p + "attn_out", ao, T, hidden);
             launch_add(h, ao, (int64_t)T * hidden, s);
         } else {
-            gemm(x, W.o, aa.ctx16, T, tpad, h, hidden, EPI_ADD);
+            resid = gemm_resid(x, W.o, aa.ctx16, T, tpad, h, hidden);
         }
         observe(x, p + "post_attn", h, T, hidden);
-        launch_rmsnorm(h, W.ffn_norm, T, hidden, c.eps, xs, tpad, nullptr, s);
+        if (capture)
+            launch_rmsnorm(h, W.ffn_norm, T, hidden, c.eps, xs, tpad, nullptr, s);
+        else
+            launch_rmsnorm_resid(h, resid, W.ffn_norm, T, hidden, c.eps, xs, tpad, s);
+        resid = nullptr;
         observe_kslab(x, p + "ffn_norm", xs, T, hidden, tpad);
         __half* xf = x->xs_ff.get((size_t)tpad * ff);
         gemm(x, W.gu, xs, T, tpad, nullptr, 2 * ff, EPI_SWIGLU, xf);
@@ -1052,10 +1089,11 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
             observe(x, p + "ffn_out", fo, T, hidden);
             launch_add(h, fo, (int64_t)T * hidden, s);
         } else {
-            gemm(x, W.down, xf, T, tpad, h, hidden, EPI_ADD);
+            resid = gemm_resid(x, W.down, xf, T, tpad, h, hidden);
         }
         observe(x, p + "output", h, T, hidden);
     }
+    if (resid) launch_resid_add(h, resid, (int64_t)T * hidden, s);  // the last layer's pending half sums
     check_cancel(x);
     // KvCache.Advance(max(0, end - Length)).
     x->length += std::max(0, end - x->length);
