@@ -39,6 +39,7 @@ namespace jv {
 constexpr int GEMM_THREADS = 512;
 constexpr int DEC_THREADS = 256;
 constexpr int DEC_WARP0 = 8;
+constexpr int DEC_WARPS_PER_GROUP = 4;  // two decoder groups, alternate k steps
 constexpr uint64_t WAIT_NS = 2000000000ull;
 
 __device__ __forceinline__ uint32_t s_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -282,10 +283,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     const uint32_t bbytes = (uint32_t)bn * 128u;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_THREADS / 32); }
+        for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_WARPS_PER_GROUP); }
         for (int i = 0; i < NS; i++) {
             mbar_init(b_full + 8 * i, 1);
-            mbar_init(a_full + 8 * i, DEC_THREADS / 32);
+            mbar_init(a_full + 8 * i, DEC_WARPS_PER_GROUP);
             mbar_init(st_empty + 8 * i, 1);
         }
         for (int i = 0; i < 2; i++) { mbar_init(acc_full + 8 * i, 1); mbar_init(acc_empty + 8 * i, 4); }
@@ -370,30 +371,38 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             if (!mbar_wait(drained, 0)) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
         }
     } else if (warp >= DEC_WARP0) {  // --------------------------------------- decode
-        // Thread dt decodes chunk c = dt % 8 of rows r0 + 32*it (it = 0..3); the swizzled
-        // position of that chunk is the same for all four rows.
-        const int dt = threadIdx.x - DEC_WARP0 * 32;
+        // Two groups of four warps take alternate k steps (group g the steps k = g mod 2 of
+        // the CTA's sequence), so two chunks are decoded at once and each wait/arrive covers
+        // twice the work. Thread dt of a group decodes chunk c = dt % 8 of rows r0 + 16*it
+        // (it = 0..7); the swizzled position of that chunk is the same for all eight rows.
+        const int grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
+        const int dt = threadIdx.x - (DEC_WARP0 + grp * DEC_WARPS_PER_GROUP) * 32;
         const int c = dt & 7, r0 = dt >> 3;
         const int a_off = r0 * 128 + ((c ^ (r0 & 7)) << 4);
         Ring rr(NR), rs(NS);
+        if (grp) { rr.next(); rs.next(); }
         bool ok = true;
+        int k = 0;  // position in the CTA's sequence of k steps
         for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-            for (int ks = 0; ks < nks; ks++) {
+            for (int ks = 0; ks < nks; ks++, k++) {
+                if ((k & 1) != grp) continue;
                 if (!mbar_wait(raw_full + 8 * rr.idx, rr.phase)) { ok = false; break; }
                 const uint8_t* raw = Rs + rr.idx * cb;
-                uint4 v[4];
+                uint4 v[8];
 #pragma unroll
-                for (int it = 0; it < 4; it++) v[it] = decode8<TYPE>(raw, r0 + 32 * it, c);
+                for (int it = 0; it < 8; it++) v[it] = decode8<TYPE>(raw, r0 + 16 * it, c);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(raw_empty + 8 * rr.idx);
+                rr.next();
                 rr.next();
                 if (!mbar_wait(st_empty + 8 * rs.idx, rs.phase ^ 1u)) { ok = false; break; }
                 uint8_t* A = As + rs.idx * 16384 + a_off;
 #pragma unroll
-                for (int it = 0; it < 4; it++) *(uint4*)(A + it * 32 * 128) = v[it];
+                for (int it = 0; it < 8; it++) *(uint4*)(A + it * 16 * 128) = v[it];
                 fence_proxy_async();  // each writer's generic-proxy stores -> visible to the tensor core
                 __syncwarp();
                 if (lane == 0) mbar_arrive(a_full + 8 * rs.idx);
+                rs.next();
                 rs.next();
             }
         }

@@ -77,6 +77,7 @@ __host__ __device__ inline size_t kslab_offset(int t, int k, int tpad) {
 // else; the consumer (the next RMSNorm) adds h += ws[0] + ws[1] as it reads h.
 enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3 };
 
+
 struct GemmArgs {
     const QWeight* w;
     const __half* x;   // K-slab fp16 activations, tpad rows
@@ -155,6 +156,7 @@ struct AttnArgs {
     __half* ctx16;              // K-slab [qdim/64][tpad][64]
     int tpad;
     float* ctx32;               // optional [T][qdim]
+    int max_keys = 0;           // largest visible-key count of any item (sizes the key table)
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 

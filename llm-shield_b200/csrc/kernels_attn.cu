@@ -80,6 +80,27 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
     const int qdim = a.heads * ATT_HD;
     const int max_limit = it.shared + (it.slot0 + it.ntok - 1 - it.segment + 1);
 
+    // Where every visible key lives, looked up once: (physical page << 8) | slot in page, so
+    // that the block loads below issue their copies without a dependent page-table read.
+    uint32_t* tab = (uint32_t*)(Vs + 2 * ATT_KEYS * ATT_HD);
+    for (int L0 = tid; L0 < max_limit; L0 += 4 * ATT_THREADS) {
+        int slot[4], page[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int L = L0 + j * ATT_THREADS;
+            slot[j] = L < it.shared ? L : it.segment + (L - it.shared);
+            page[j] = L < max_limit ? a.page_table[slot[j] / a.page_slots] : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int L = L0 + j * ATT_THREADS;
+            if (L < max_limit) tab[L] = ((uint32_t)page[j] << 8) | (uint32_t)(slot[j] % a.page_slots);
+        }
+    }
+    const int64_t head_off = (int64_t)((a.layer * a.kv_heads + it.kv_head) * 2) * a.page_slots * 256;
+    const int64_t v_off = (int64_t)a.page_slots * 256;
+    __syncthreads();
+
     // Q tile: row r = token (r / group) × head (r % group) of this KV head.
     for (int id = tid; id < ATT_ROWS * 16; id += ATT_THREADS) {
         int r = id >> 4, c = id & 15;
@@ -102,9 +123,10 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
             const __half* vs = a.kv_pool;
             int bytes = 0;
             if (L < max_limit) {
-                int slot = L < it.shared ? L : it.segment + (L - it.shared);
-                ks = kv_row(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, it.kv_head, 0, slot) + c * 8;
-                vs = kv_row(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, it.kv_head, 1, slot) + c * 8;
+                const uint32_t e = tab[L];
+                const char* row = (const char*)a.kv_pool + (int64_t)(e >> 8) * a.page_bytes + (int64_t)(e & 255u) * 256 + head_off;
+                ks = (const __half*)row + c * 8;
+                vs = (const __half*)(row + v_off) + c * 8;
                 bytes = 16;
             }
             cp_async16(kd + swz(r, c), ks, bytes);
@@ -258,11 +280,13 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
 
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.n_items <= 0) return;
-    size_t smem = (size_t)(ATT_ROWS + 4 * ATT_KEYS) * ATT_HD * sizeof(__half);
-    static bool configured = false;
-    if (!configured) {
+    if (a.page_slots > 256) throw Error(JV_ERR_UNSUPPORTED, "attention: pages of more than 256 slots");
+    size_t smem = (size_t)(ATT_ROWS + 4 * ATT_KEYS) * ATT_HD * sizeof(__half) + (size_t)a.max_keys * 4;
+    if (smem > 227 * 1024) throw Error(JV_ERR_UNSUPPORTED, "attention: too many visible keys for one pass");
+    static size_t configured = 0;
+    if (smem > configured) {
         JV_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        configured = true;
+        configured = smem;
     }
     k_attention<<<a.n_items, ATT_THREADS, smem, s>>>(a);
     note_launch();

@@ -892,6 +892,8 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         }
         std::stable_sort(items.begin(), items.end(), [](const AttnItem& a, const AttnItem& b) { return a.nblocks > b.nblocks; });
     }
+    int max_item_keys = 0;
+    for (const AttnItem& it : items) max_item_keys = std::max(max_item_keys, it.nblocks * 64);
     // Algorithmic attention work: QK^T and PV over exactly the visible (query, key) pairs.
     double attn_flops = 0, attn_bytes = 2.0 * 2 * T * qdim;
     for (int t = 0; t < T; t++) attn_flops += 4.0 * c.heads * c.head_dim * (L->shared[t] + (L->slot[t] - L->seg[t] + 1));
@@ -1037,9 +1039,9 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         else
             launch_rmsnorm_resid(h, resid, W.attn_norm, T, hidden, c.eps, xs, tpad, s);
         observe_kslab(x, p + "attn_norm", xs, T, hidden, tpad);
-        gemm(x, W.qkv, xs, T, tpad, qkv32, qkvn, EPI_STORE);
         ra.q16 = x->q16.get((size_t)T * qdim);
         ra.q32 = capture ? x->q32.get((size_t)T * qdim) : nullptr;
+        gemm(x, W.qkv, xs, T, tpad, qkv32, qkvn, EPI_STORE);
         launch_rope_kv(ra, s);
         if (capture) {
             observe(x, p + "q_rope", ra.q32, T, qdim);
@@ -1061,6 +1063,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         aa.ctx16 = x->ctx16.get((size_t)tpad * qdim);
         aa.tpad = tpad;
         aa.ctx32 = capture ? x->ctx32.get((size_t)T * qdim) : nullptr;
+        aa.max_keys = max_item_keys;
         {
             ProfScope ps(x, JV_PROF_ATTENTION, attn_flops, attn_bytes);
             launch_attention(aa, s);
