@@ -247,6 +247,92 @@ __device__ __forceinline__ void unit_coords(int u, int splits, int ttiles, int& 
     tile = r / ttiles;
 }
 
+// What drain_cols does with accumulator values: write them as they are (a K-split partial),
+// store / add them into Y (after adding the other K half when `other` is given), or the
+// SwiGLU of each gate/up pair into the fp16 K-slab of the down projection's input.
+enum DrainKind : int { DR_RAW = 0, DR_STORE = 1, DR_ADD = 2, DR_SWIGLU = 3 };
+
+// Start column of share s when the last unit's columns are split in thirds, in whole
+// 16-column chunks: share 0 = [drain_share(0), drain_share(1)) for the epilogue warps, shares
+// 1 and 2 for the two decoder groups; drain_share(3) = bn.
+__device__ __forceinline__ int drain_share(int bn, int s) {
+    const int nch = bn / 16;
+    return s <= 0 ? 0 : s >= 3 ? bn : 16 * ((s * nch + 2) / 3);
+}
+
+// Drain accumulator columns [c0, c1) (multiples of 16) of TMEM lane quarter q: one 16-column
+// tcgen05.ld in flight while the previous chunk is processed. Row n of the output, tokens
+// t0 + column for columns below tn.
+__device__ __forceinline__ void drain_cols(uint32_t tacc, int c0, int c1, int kind, int lane, int q, int n, int tile,
+                                           int t0, int tn, int tpad, int ldy, float* __restrict__ y,
+                                           const float* __restrict__ other, __half* __restrict__ xs_out) {
+    if (c0 >= c1) return;
+    uint32_t cur[16], nxt[16];
+    tmem_ld16_issue(tacc + (uint32_t)c0, cur);
+    tmem_wait16(cur);
+    for (int col = c0; col < c1; col += 16) {
+        const bool more = col + 16 < c1;
+        if (more) tmem_ld16_issue(tacc + (uint32_t)(col + 16), nxt);
+        const int lim = min(16, tn - col);
+        if (kind == DR_SWIGLU) {
+            // Kernels.SwiGlu (reference src/Jevstral/Numerics/Kernels.cs:82-89):
+            // up <- g*u; s <- 1/(1+exp(-g)); y <- s*up. Lanes 0-15 hold gate rows, lanes 16-31
+            // the matching up rows: one shuffle pairs them, lane l < 16 writes columns 0-7 of
+            // the chunk, lane l + 16 columns 8-15.
+            const int jf = tile * 64 + q * 16 + (lane & 15);
+            const bool hi = lane >= 16;
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) o[j] = __shfl_xor_sync(0xffffffffu, __uint_as_float(cur[j]), 16);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int jj = hi ? j + 8 : j;
+                const float mv = hi ? __uint_as_float(cur[j + 8]) : __uint_as_float(cur[j]);
+                const float ov = hi ? o[j + 8] : o[j];
+                const float gg = hi ? ov : mv;
+                const float uu = hi ? mv : ov;
+                const float up = __fmul_rn(gg, uu);
+                const float sg = __frcp_rn(__fadd_rn(1.0f, __expf(-gg)));
+                if (jj < lim) xs_out[kslab_offset(t0 + col + jj, jf, tpad)] = __float2half_rn(__fmul_rn(sg, up));
+            }
+        } else {
+            // Row pointers step by ldy per token.
+            float* yp = y + (int64_t)(t0 + col) * ldy + n;
+            if (other) {
+                const float* op = other + (int64_t)(t0 + col) * ldy + n;
+                float o[16], yv[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    o[j] = j < lim ? __ldcg(op + (int64_t)j * ldy) : 0.f;
+                    yv[j] = (kind == DR_ADD && j < lim) ? yp[(int64_t)j * ldy] : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (j < lim) {
+                        const float s = __fadd_rn(__uint_as_float(cur[j]), o[j]);
+                        yp[(int64_t)j * ldy] = kind == DR_ADD ? __fadd_rn(yv[j], s) : s;
+                    }
+            } else if (kind == DR_ADD) {
+                float yv[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) yv[j] = j < lim ? yp[(int64_t)j * ldy] : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (j < lim) yp[(int64_t)j * ldy] = __fadd_rn(yv[j], __uint_as_float(cur[j]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (j < lim) yp[(int64_t)j * ldy] = __uint_as_float(cur[j]);
+            }
+        }
+        if (more) {
+            tmem_wait16(nxt);
+#pragma unroll
+            for (int j = 0; j < 16; j++) cur[j] = nxt[j];
+        }
+    }
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     // Every parameter in a register or a restrict pointer: nothing below takes the address of
@@ -408,9 +494,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         }
         if (!ok) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
     } else if (warp >= 4) {  // ------------------------------------------------- epilogue
-        // Warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows of the unit's tile. Each 16
-        // column chunk's tcgen05.ld is issued before the previous chunk is processed.
+        // Warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows of the unit's tile. The CTA's
+        // last unit is drained by these warps and the (then idle) decoder warps together,
+        // a third of the columns each (see drain_share).
         const int q = warp & 3;
+        const bool counter_split = splits > 1 && epi != EPI_PARTIAL;
         int i = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, i++) {
             int tile, tt, sp;
@@ -425,119 +513,59 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             const uint32_t tacc = tmem + (uint32_t)(ab * ncols) + ((uint32_t)(q * 32) << 16);
             const int n = tile * 128 + q * 32 + lane;
             const int tn = min(bn, T - t0);  // valid columns of this token tile
-            bool last = true;
-            const float* other = nullptr;
-            if (splits > 1) {
+            float* mine = splits > 1 ? g_ws + (int64_t)sp * T * ldy : nullptr;
+            if (counter_split) {
                 // Both K halves publish their partial; the unit that finishes last adds the
                 // other half to its own (still in TMEM): p0 + p1, the same value whichever
                 // unit that is (IEEE addition commutes).
-                float* mine = g_ws + (int64_t)sp * T * ldy;
-                other = g_ws + (int64_t)(1 - sp) * T * ldy;
-                uint32_t cur[16], nxt[16];
-                tmem_ld16_issue(tacc, cur);
-                tmem_wait16(cur);
-                for (int col = 0; col < bn; col += 16) {
-                    const bool more = col + 16 < bn;
-                    if (more) tmem_ld16_issue(tacc + (uint32_t)(col + 16), nxt);
-                    float* mp = mine + (int64_t)(t0 + col) * ldy + n;
-                    const int lim = min(16, tn - col);
-#pragma unroll
-                    for (int j = 0; j < 16; j++)
-                        if (j < lim) mp[(int64_t)j * ldy] = __uint_as_float(cur[j]);
-                    if (more) {
-                        tmem_wait16(nxt);
-#pragma unroll
-                        for (int j = 0; j < 16; j++) cur[j] = nxt[j];
-                    }
+                drain_cols(tacc, 0, bn, DR_RAW, lane, q, n, tile, t0, tn, tpad, ldy, mine, nullptr, g_xs_out);
+                __threadfence();
+                epi_bar();
+                if (warp == 4 && lane == 0) {
+                    int* ctr = g_ctr + tile * ttiles + tt;
+                    int old = atomicAdd(ctr, 1);
+                    int is_last = old == splits - 1;
+                    if (is_last) atomicExch(ctr, 0);
+                    *last_flag = is_last;
                 }
-                if (epi == EPI_PARTIAL) {  // the consumer adds both halves
-                    last = false;
-                } else {
+                epi_bar();
+                const bool last = *last_flag != 0;
+                epi_bar();  // the flag is re-used by the next unit
+                if (last) {
                     __threadfence();
-                    epi_bar();
-                    if (warp == 4 && lane == 0) {
-                        int* ctr = g_ctr + tile * ttiles + tt;
-                        int old = atomicAdd(ctr, 1);
-                        int is_last = old == splits - 1;
-                        if (is_last) atomicExch(ctr, 0);
-                        *last_flag = is_last;
-                    }
-                    epi_bar();
-                    last = *last_flag != 0;
-                    epi_bar();  // the flag is re-used by the next unit
-                    if (last) __threadfence();
+                    drain_cols(tacc, 0, bn, epi == EPI_ADD ? DR_ADD : DR_STORE, lane, q, n, tile, t0, tn, tpad, ldy, g_y,
+                               g_ws + (int64_t)(1 - sp) * T * ldy, g_xs_out);
                 }
-            }
-            if (last) {
-                uint32_t cur[16], nxt[16];
-                tmem_ld16_issue(tacc, cur);
-                tmem_wait16(cur);
-                for (int col = 0; col < bn; col += 16) {
-                    const bool more = col + 16 < bn;
-                    if (more) tmem_ld16_issue(tacc + (uint32_t)(col + 16), nxt);
-                    if (epi == EPI_SWIGLU) {
-                        // Kernels.SwiGlu (reference src/Jevstral/Numerics/Kernels.cs:82-89):
-                        // up <- g*u; s <- 1/(1+exp(-g)); y <- s*up. Lanes 0-15 hold gate rows,
-                        // lanes 16-31 the matching up rows: one shuffle pairs them, lane l < 16
-                        // writes columns 0-7 of the chunk, lane l + 16 columns 8-15.
-                        const int jf = tile * 64 + q * 16 + (lane & 15);
-                        const bool hi = lane >= 16;
-                        float o[16];
-#pragma unroll
-                        for (int j = 0; j < 16; j++) o[j] = __shfl_xor_sync(0xffffffffu, __uint_as_float(cur[j]), 16);
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            const int jj = hi ? j + 8 : j;
-                            const float mv = hi ? __uint_as_float(cur[j + 8]) : __uint_as_float(cur[j]);
-                            const float ov = hi ? o[j + 8] : o[j];
-                            const float gg = hi ? ov : mv;
-                            const float uu = hi ? mv : ov;
-                            const float up = __fmul_rn(gg, uu);
-                            const float sg = __frcp_rn(__fadd_rn(1.0f, __expf(-gg)));
-                            if (col + jj < tn)
-                                g_xs_out[kslab_offset(t0 + col + jj, jf, tpad)] = __float2half_rn(__fmul_rn(sg, up));
-                        }
-                    } else {
-                        // Row pointers step by ldy per token; the mode is uniform per launch.
-                        float* yp = g_y + (int64_t)(t0 + col) * ldy + n;
-                        const int lim = min(16, tn - col);
-                        if (other) {
-                            const float* op = other + (int64_t)(t0 + col) * ldy + n;
-                            float o[16], yv[16];
-#pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                o[j] = j < lim ? __ldcg(op + (int64_t)j * ldy) : 0.f;
-                                yv[j] = (epi == EPI_ADD && j < lim) ? yp[(int64_t)j * ldy] : 0.f;
-                            }
-#pragma unroll
-                            for (int j = 0; j < 16; j++)
-                                if (j < lim) {
-                                    const float s = __fadd_rn(__uint_as_float(cur[j]), o[j]);
-                                    yp[(int64_t)j * ldy] = epi == EPI_ADD ? __fadd_rn(yv[j], s) : s;
-                                }
-                        } else if (epi == EPI_ADD) {
-                            float yv[16];
-#pragma unroll
-                            for (int j = 0; j < 16; j++) yv[j] = j < lim ? yp[(int64_t)j * ldy] : 0.f;
-#pragma unroll
-                            for (int j = 0; j < 16; j++)
-                                if (j < lim) yp[(int64_t)j * ldy] = __fadd_rn(yv[j], __uint_as_float(cur[j]));
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 16; j++)
-                                if (j < lim) yp[(int64_t)j * ldy] = __uint_as_float(cur[j]);
-                        }
-                    }
-                    if (more) {
-                        tmem_wait16(nxt);
-#pragma unroll
-                        for (int j = 0; j < 16; j++) cur[j] = nxt[j];
-                    }
-                }
+            } else {
+                const int cend = u + (int)gridDim.x >= units ? drain_share(bn, 1) : bn;  // last unit: share 0
+                const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
+                drain_cols(tacc, 0, cend, kind, lane, q, n, tile, t0, tn, tpad, ldy, epi == EPI_PARTIAL ? mine : g_y, nullptr,
+                           g_xs_out);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+        }
+    }
+    // The decoder warps, done with the main loop, drain two thirds of the last unit's columns
+    // (the epilogue warps drain the first third), so the tail after the last MMA is short.
+    if (warp >= DEC_WARP0 && !(splits > 1 && epi != EPI_PARTIAL) && (int)blockIdx.x < units) {
+        const int my_units = (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+        const int il = my_units - 1, ul = (int)blockIdx.x + il * (int)gridDim.x;
+        int tile, tt, sp;
+        unit_coords(ul, splits, ttiles, tile, tt, sp);
+        const int ab = il & 1, q = warp & 3, grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
+        const bool ready = mbar_wait(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
+        tc_fence_after();
+        if (ready) {
+            const int t0 = tt * bn;
+            const uint32_t tacc = tmem + (uint32_t)(ab * ncols) + ((uint32_t)(q * 32) << 16);
+            const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
+            drain_cols(tacc, drain_share(bn, grp + 1), drain_share(bn, grp + 2), kind, lane, q, tile * 128 + q * 32 + lane, tile,
+                       t0, min(bn, T - t0), tpad, ldy, epi == EPI_PARTIAL ? g_ws + (int64_t)sp * T * ldy : g_y, nullptr,
+                       g_xs_out);
+        } else {
+            atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
         }
     }
     tc_fence_before();
