@@ -191,28 +191,50 @@ def run_b200(args, rank, world, local_rank, dist):
     if args.config == "c1":
         gen = lambda r: ([1] + r.integers(1000, VOCAB, 255).tolist(), None)  # noqa: E731
     if args.config == "c3":
+        # decision 1: 4096-token trunk + 9 x 48; decision 2 shares the trunk's pages and, per
+        # the decider's never-empty-trunk rule, re-runs its last token before 9 fresh branches
         gen = lambda r: ([1] + r.integers(1000, VOCAB, 4095).tolist(),  # noqa: E731
+                         [r.integers(1000, VOCAB, 48).tolist() for _ in range(9)],
                          [r.integers(1000, VOCAB, 48).tolist() for _ in range(9)])
     work = [gen(rng) for _ in range(args.warmup + args.steps)]
 
-    def step(trunk, branches):
+    def step(trunk, branches, second=None):
         ctx.kv_cache.reset()
         if branches is None:  # C1: causal prefill, verdict rows of the last position
             v = ctx.forward_selected(trunk, ROWS)[None, :]
         else:
             v = ctx.forward_tree(trunk, branches, ROWS)
         z = jv.margins_from_verdicts(v, 1)
-        return jv.decision_probs(z)
+        p = jv.decision_probs(z)
+        if second is not None:
+            ctx.kv_cache.truncate(len(trunk) - 1)
+            v2 = ctx.forward_tree([trunk[-1]], second, ROWS)
+            p = jv.decision_probs(jv.margins_from_verdicts(v2, 1))
+        return p
 
-    for trunk, branches in work[: args.warmup]:
-        step(trunk, branches)
+    for w in work[: args.warmup]:
+        step(*w)
     torch.cuda.synchronize()
 
     timed = work[args.warmup:]
-    tokens = sum(len(t) + (sum(len(b) for b in br) if br else 0) for t, br in timed)
-    pairs = sum(attention_pairs(len(t), [len(b) for b in br] if br else []) for t, br in timed)
-    h2d = sum(4 * 3 * (len(t) + (sum(len(b) for b in br) if br else 0)) for t, br in timed) // len(timed)
-    d2h = 4 * len(ROWS) * (len(timed[0][1]) if timed[0][1] else 1)
+
+    def toks_of(w):
+        n = len(w[0]) + (sum(len(b) for b in w[1]) if w[1] else 0)
+        if len(w) > 2:
+            n += 1 + sum(len(b) for b in w[2])
+        return n
+
+    def pairs_of(w):
+        p = attention_pairs(len(w[0]), [len(b) for b in w[1]] if w[1] else [])
+        if len(w) > 2:  # the re-run trunk token sees the trunk; each branch the trunk, that token and itself
+            L = len(w[0])
+            p += L + sum(b * L + b * (b + 1) // 2 for b in (len(x) for x in w[2]))
+        return p
+
+    tokens = sum(toks_of(w) for w in timed)
+    pairs = sum(pairs_of(w) for w in timed)
+    h2d = sum(4 * 3 * toks_of(w) for w in timed) // len(timed)
+    d2h = 4 * len(ROWS) * (len(timed[0][1]) if timed[0][1] else 1) * (2 if len(timed[0]) > 2 else 1)
 
     ctx.profile(True)
     ctx.profile_reset()
@@ -224,8 +246,8 @@ def run_b200(args, rank, world, local_rank, dist):
     with ClockSampler(local_rank) as clocks:
         t0 = time.perf_counter()
         ev0.record(stream)
-        for trunk, branches in timed:
-            step(trunk, branches)
+        for w in timed:
+            step(*w)
         ev1.record(stream)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
@@ -351,7 +373,7 @@ def gemm_traffic_per_launch():
 WORKLOADS = {
     "c1": "C1: single 256-token causal prefill (BOS + 255), verdict rows at the last position, Q8_0",
     "c2": "C2: one tree decision, 512-token trunk + 5 branches x 32, 2 verdict rows per branch, Q8_0",
-    "c3": "C3: long-trunk tree, 4096-token trunk + 9 branches x 48, Q5_1",
+    "c3": "C3: long-trunk tree, 4096-token trunk + 9 branches x 48, then a second decision on the same trunk pages (last trunk token re-run + 9 fresh branches x 48), Q5_1",
     "c4": "C4: greedy decode after a 1024-token prompt, full LM head + argmax, Q4_0, batch 1",
     "c5": "C5: random trees (trunk U[128,4096], 2-9 branches of U[16,64]), Q8_0",
 }
