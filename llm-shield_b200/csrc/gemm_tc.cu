@@ -384,6 +384,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    // The weights do not depend on the previous kernel: their stream and decode start now;
+    // the activation loads and every global write wait for it (pdl_wait in those roles).
+    pdl_launch_dependents();
 
     if (warp == 0 || warp == 3) {
         if (lane == 0) {  // ----------------------------------------------- producers
@@ -397,6 +400,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             Ring r(depth);
             bool ok = true;
             int issued = 0;
+            if (!weights) pdl_wait();
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 int tile, tt, sp;
                 unit_coords(u, splits, ttiles, tile, tt, sp);
@@ -499,6 +503,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         // a third of the columns each (see drain_share).
         const int q = warp & 3;
         const bool counter_split = splits > 1 && epi != EPI_PARTIAL;
+        pdl_wait();
         int i = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, i++) {
             int tile, tt, sp;
@@ -555,6 +560,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         int tile, tt, sp;
         unit_coords(ul, splits, ttiles, tile, tt, sp);
         const int ab = il & 1, q = warp & 3, grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
+        pdl_wait();
         const bool ready = mbar_wait(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
         tc_fence_after();
         if (ready) {
@@ -631,7 +637,7 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
         JV_CUDA(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
     }
     int grid = std::min(p.units, g_sm_count);
-    k_gemm_tc<TYPE><<<grid, GEMM_THREADS, smem, s>>>(p);
+    launch_pdl(k_gemm_tc<TYPE>, dim3(grid), dim3(GEMM_THREADS), smem, s, p);
     note_launch();
 }
 

@@ -251,6 +251,30 @@ int64_t launches_total();
 
 void note_launch(int n = 1);
 
+#ifdef __CUDACC__
+// Programmatic dependent launch. A kernel launched with launch_pdl may start while the
+// previous kernel in the stream is finishing: it calls pdl_launch_dependents() to let the
+// kernel after it do the same, and pdl_wait() before it touches anything the previous
+// kernel writes (every read of a previous output, and every write, comes after pdl_wait).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    JV_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...));
+}
+#endif
+
 // The calling thread's jv_last_error() message; returns code.
 int api_error(int code, const std::string& msg);
 // A re-tiled quantized matrix described by the QuantMatMul C ABI; throws on bad arguments.

@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
     __half* Ks = Qs + ATT_ROWS * ATT_HD;            // [2][64][128]
     __half* Vs = Ks + 2 * ATT_KEYS * ATT_HD;        // [2][64][128]
 
+    pdl_launch_dependents();
+    pdl_wait();
     const AttnItem it = a.items[blockIdx.x];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int group = a.heads / a.kv_heads;  // 4 for Ministral-3 (asserted on the host)
@@ -288,7 +290,7 @@ void launch_attention(const AttnArgs& a, cudaStream_t s) {
         JV_CUDA(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured = smem;
     }
-    k_attention<<<a.n_items, ATT_THREADS, smem, s>>>(a);
+    launch_pdl(k_attention, dim3(a.n_items), dim3(ATT_THREADS), smem, s, a);
     note_launch();
 }
 

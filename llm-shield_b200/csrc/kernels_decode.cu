@@ -144,10 +144,6 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
     return red[32];
 }
 
-// Programmatic dependent launch: let the next kernel in the stream start its independent
-// prologue (weight streaming) now / wait until the previous kernel's writes are visible.
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void dg_mbar_init(uint32_t bar, uint32_t count) {
@@ -639,23 +635,6 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
     if (threadIdx.x == 0) a.counters[kvh] = 0;
 }
 
-// Launch with programmatic stream serialization: the kernel's CTAs may start while the
-// previous kernel finishes; each one streams its weights, then waits for that kernel.
-template <class K, class A>
-void launch_pdl(K kernel, dim3 grid, int threads, size_t smem, cudaStream_t s, const A& args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(threads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    JV_CUDA(cudaLaunchKernelEx(&cfg, kernel, args));
-}
-
 template <int TYPE>
 size_t dec_smem(int ksteps, int splits) {
     const int per = (ksteps + splits - 1) / splits;
@@ -671,7 +650,7 @@ void launch_dec_typed(const DecGemvArgs& a, int splits, cudaStream_t s) {
         JV_CUDA(cudaFuncSetAttribute(k_dec_gemv<TYPE, MODE, NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured = smem;
     }
-    launch_pdl(k_dec_gemv<TYPE, MODE, NORM>, dim3(a.rows / 128, splits), DG_THREADS, smem, s, a);
+    launch_pdl(k_dec_gemv<TYPE, MODE, NORM>, dim3(a.rows / 128, splits), dim3(DG_THREADS), smem, s, a);
 }
 
 template <int MODE, bool NORM>
@@ -713,7 +692,7 @@ void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int sp
 void launch_dec_attn(const DecAttnArgs& a, int splits, cudaStream_t s) {
     const int group = a.heads / a.kv_heads;
     if (group < 1 || group > 8 || a.heads % a.kv_heads) throw Error(JV_ERR_UNSUPPORTED, "decode attention: group size");
-    launch_pdl(k_dec_attn, dim3(a.kv_heads, splits), 32 * group, 0, s, a);
+    launch_pdl(k_dec_attn, dim3(a.kv_heads, splits), dim3(32 * group), 0, s, a);
     note_launch();
 }
 

@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_resid(float* __restric
                                                                  const float* __restrict__ w, int n, float eps,
                                                                  __half* __restrict__ xs, int tpad, int64_t plane) {
     __shared__ double red[33];
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x, n4 = n >> 2;
     float4* hr = (float4*)(h + (int64_t)t * n);
     const float4* p0 = resid ? (const float4*)(resid + (int64_t)t * n) : nullptr;
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_resid(float* __restric
 void launch_rmsnorm_resid(float* h, const float* resid, const float* w, int T, int n, float eps, __half* xs, int tpad,
                           cudaStream_t s) {
     if (n % 4 != 0 || n > 4 * RN_VEC * NORM_THREADS) throw Error(JV_ERR_UNSUPPORTED, "rmsnorm: row width");
-    k_rmsnorm_resid<<<T, NORM_THREADS, 0, s>>>(h, resid, w, n, eps, xs, tpad, (int64_t)T * n);
+    launch_pdl(k_rmsnorm_resid, dim3(T), dim3(NORM_THREADS), 0, s, h, resid, w, n, eps, xs, tpad, (int64_t)T * n);
     note_launch();
 }
 
@@ -174,50 +176,74 @@ __device__ __forceinline__ __half* kv_addr(__half* pool, const int32_t* page_tab
 // RotateQueries / StoreKeys / StoreValues / ApplyPositionScale (MinistralModel.cs:638-682):
 // adjacent-pair rotation at position[t] (x0*cos - x1*sin, x0*sin + x1*cos with separate
 // roundings), the llama-4 temperature on q, then q to the attention operand and k, v to
-// their KV page slots as fp16.
-__global__ void k_rope_kv(RopeArgs a) {
-    int t = blockIdx.x;
-    int hd = a.head_dim, half = hd / 2;
-    int qdim = a.heads * hd, kvdim = a.kv_heads * hd;
-    int pos = a.pos[t], slot = a.slot[t];
+// their KV page slots as fp16. One CTA per token; each thread takes 4 consecutive elements
+// (two pairs) per step, every load of the token issued up front; the token's KV page is
+// looked up once.
+__device__ __forceinline__ void rope_pair2(const float4 x, const float4 cs, float temp, float* r) {
+    r[0] = __fsub_rn(__fmul_rn(x.x, cs.x), __fmul_rn(x.y, cs.y));
+    r[1] = __fadd_rn(__fmul_rn(x.x, cs.y), __fmul_rn(x.y, cs.x));
+    r[2] = __fsub_rn(__fmul_rn(x.z, cs.z), __fmul_rn(x.w, cs.w));
+    r[3] = __fadd_rn(__fmul_rn(x.z, cs.w), __fmul_rn(x.w, cs.z));
+    if (temp != 1.0f)
+        for (int e = 0; e < 4; e++) r[e] = __fmul_rn(r[e], temp);
+}
+
+__global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int t = blockIdx.x;
+    const int hd = a.head_dim, half = hd / 2;
+    const int qdim = a.heads * hd, kvdim = a.kv_heads * hd;
+    const int pos = a.pos[t], slot = a.slot[t];
     const float* row = a.qkv + (int64_t)t * (qdim + 2 * kvdim);
-    const float2* tab = a.table + (int64_t)pos * half;
+    const float4* tab4 = (const float4*)(a.table + (int64_t)pos * half);  // two (cos, sin) pairs each
     float temp = 1.0f;
     if (a.orig_ctx > 0 && a.temperature_scale != 0.f) {
         float interval = floorf(__fdiv_rn((float)pos, (float)a.orig_ctx));
         if (interval != 0.f) temp = __fadd_rn(1.0f, __fmul_rn(a.temperature_scale, logf(__fadd_rn(1.0f, interval))));
     }
-    // q and k pairs
-    int npairs = (qdim + kvdim) / 2;
-    for (int p = threadIdx.x; p < npairs; p += blockDim.x) {
-        int e = 2 * p;
-        int i = (e % hd) / 2;
-        float2 cs = tab[i];
-        float x0 = row[e], x1 = row[e + 1];
-        float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-        float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-        if (e < qdim) {
-            if (temp != 1.0f) { r0 = __fmul_rn(r0, temp); r1 = __fmul_rn(r1, temp); }
-            if (a.q16) *(__half2*)(a.q16 + (int64_t)t * qdim + e) = __floats2half2_rn(r0, r1);
-            if (a.q32) { a.q32[(int64_t)t * qdim + e] = r0; a.q32[(int64_t)t * qdim + e + 1] = r1; }
-        } else {
-            int ke = e - qdim, head = ke / hd, d = ke % hd;
-            __half* dst = kv_addr(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, head, 0, slot);
-            *(__half2*)(dst + d) = __floats2half2_rn(r0, r1);
-            if (a.k32) { a.k32[(int64_t)t * kvdim + ke] = r0; a.k32[(int64_t)t * kvdim + ke + 1] = r1; }
+    // this token's slot row, K plane of (layer, kv head 0); heads and V are fixed offsets
+    const int page = a.page_table[slot / a.page_slots];
+    char* kv0 = (char*)a.kv_pool + (int64_t)page * a.page_bytes +
+                ((int64_t)(a.layer * a.kv_heads * 2) * a.page_slots + (slot % a.page_slots)) * 256;
+    const int64_t head_stride = (int64_t)2 * a.page_slots * 256, v_off = (int64_t)a.page_slots * 256;
+    const int nq4 = qdim / 4, nk4 = kvdim / 4;
+    for (int i = threadIdx.x; i < nq4 + 2 * nk4; i += blockDim.x) {
+        const float4 x = *(const float4*)(row + 4 * i);
+        if (i < nq4 + nk4) {
+            const int e = 4 * i;  // q, then k
+            const int d = e % hd;
+            const float4 cs = tab4[d / 4];
+            float r[4];
+            rope_pair2(x, cs, i < nq4 ? temp : 1.0f, r);
+            if (i < nq4) {
+                if (a.q16) {
+                    __half2 lo = __floats2half2_rn(r[0], r[1]), hi = __floats2half2_rn(r[2], r[3]);
+                    uint2 pk;
+                    pk.x = *reinterpret_cast<uint32_t*>(&lo);
+                    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+                    *(uint2*)(a.q16 + (int64_t)t * qdim + e) = pk;
+                }
+                if (a.q32) *(float4*)(a.q32 + (int64_t)t * qdim + e) = make_float4(r[0], r[1], r[2], r[3]);
+            } else {
+                const int ke = e - qdim, head = ke / hd;
+                __half2* dst = (__half2*)(kv0 + head * head_stride) + d / 2;
+                dst[0] = __floats2half2_rn(r[0], r[1]);
+                dst[1] = __floats2half2_rn(r[2], r[3]);
+                if (a.k32) *(float4*)(a.k32 + (int64_t)t * kvdim + ke) = make_float4(r[0], r[1], r[2], r[3]);
+            }
+        } else {  // v: straight copy to its slot
+            const int ve = 4 * i - qdim - kvdim, head = ve / hd, d = ve % hd;
+            __half2* dst = (__half2*)(kv0 + head * head_stride + v_off) + d / 2;
+            dst[0] = __floats2half2_rn(x.x, x.y);
+            dst[1] = __floats2half2_rn(x.z, x.w);
         }
-    }
-    // v: straight copy to its slot
-    for (int e = threadIdx.x * 2; e < kvdim; e += blockDim.x * 2) {
-        int head = e / hd, d = e % hd;
-        float v0 = row[qdim + kvdim + e], v1 = row[qdim + kvdim + e + 1];
-        __half* dst = kv_addr(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, head, 1, slot);
-        *(__half2*)(dst + d) = __floats2half2_rn(v0, v1);
     }
 }
 
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
-    k_rope_kv<<<a.T, 256, 0, s>>>(a);
+    if (a.head_dim % 4 != 0) throw Error(JV_ERR_UNSUPPORTED, "rope: head_dim must be a multiple of 4");
+    launch_pdl(k_rope_kv, dim3(a.T), dim3(256), 0, s, a);
     note_launch();
 }
 
