@@ -583,7 +583,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
 }
 
 int gemm_bn_for(int T) {
+    // At least two token tiles from 128 tokens on, so that the 48-tile QKV and the split
+    // 24-tile projections still cover most SMs when T is a few hundred.
     int tiles = (T + 255) / 256;
+    if (T >= 128 && tiles < 2) tiles = 2;
     int per = (T + tiles - 1) / tiles;
     int bn = (per + 15) / 16 * 16;
     return bn < 16 ? 16 : bn;

@@ -140,7 +140,8 @@ struct RopeArgs {
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s);
 void launch_rope_table(float2* table, const float* freqs, int half, int pos0, int npos, float mscale, cudaStream_t s);
 
-struct AttnItem {  // one query tile: up to 16 consecutive tokens of one segment, one KV head
+constexpr int ATT_ITEM_TOKENS = 32;  // tokens per prefill attention item (x 4 query heads = 128 rows)
+struct AttnItem {  // one query tile: up to 32 consecutive tokens of one segment, one KV head
     int32_t t0, ntok, kv_head, slot0, shared, segment, nblocks, pad;
 };
 struct AttnArgs {

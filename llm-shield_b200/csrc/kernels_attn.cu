@@ -13,16 +13,18 @@
 // exactly 1, probabilities exactly 0), a token's output is bit-identical across all three
 // (the reference's DeciderTests.BranchesMatchRunningEachContinuationAlone property).
 //
-// Prefill kernel: one CTA = one KV head × up to 16 tokens of one segment; its 4 query
-// heads ride in the M dimension (64 rows = 16 tokens × 4 heads), so every K/V byte read
-// feeds all the heads that share it. fp16 operands, fp32 accumulation and online softmax.
+// Prefill kernel: one CTA = one KV head × up to 32 tokens of one segment; its 4 query
+// heads ride in the M dimension (128 rows = 32 tokens × 4 heads, 8 warps), so every K/V byte
+// read feeds all the heads that share it. K/V blocks of 64 keys stream through a 3-deep
+// cp.async ring. fp16 operands, fp32 accumulation and online softmax.
 #include "jv_internal.h"
 
 namespace jv {
 
-constexpr int ATT_THREADS = 128;
-constexpr int ATT_KEYS = 64;
-constexpr int ATT_ROWS = 64;
+constexpr int ATT_THREADS = 256;  // 8 warps x 16 query rows
+constexpr int ATT_KEYS = 64;      // keys per block
+constexpr int ATT_ROWS = 128;     // query rows per CTA: ATT_ITEM_TOKENS tokens x 4 heads
+constexpr int ATT_STAGES = 3;     // K/V blocks in flight: the one being used and two ahead
 constexpr int ATT_HD = 128;
 constexpr float LOG2E = 1.4426950408889634f;
 
@@ -71,8 +73,8 @@ __device__ __forceinline__ const __half* kv_row(const __half* pool, const int32_
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
     extern __shared__ __align__(128) unsigned char att_smem[];
     __half* Qs = (__half*)att_smem;                 // [64][128]
-    __half* Ks = Qs + ATT_ROWS * ATT_HD;            // [2][64][128]
-    __half* Vs = Ks + 2 * ATT_KEYS * ATT_HD;        // [2][64][128]
+    __half* Ks = Qs + ATT_ROWS * ATT_HD;                 // [stages][64][128]
+    __half* Vs = Ks + ATT_STAGES * ATT_KEYS * ATT_HD;    // [stages][64][128]
 
     pdl_launch_dependents();
     pdl_wait();
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
 
     // Where every visible key lives, looked up once: (physical page << 8) | slot in page, so
     // that the block loads below issue their copies without a dependent page-table read.
-    uint32_t* tab = (uint32_t*)(Vs + 2 * ATT_KEYS * ATT_HD);
+    uint32_t* tab = (uint32_t*)(Vs + ATT_STAGES * ATT_KEYS * ATT_HD);
     for (int L0 = tid; L0 < max_limit; L0 += 4 * ATT_THREADS) {
         int slot[4], page[4];
 #pragma unroll
@@ -135,7 +137,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
             cp_async16(vd + swz(r, c), vs, bytes);
         }
     };
+    // Blocks 0 and 1 in flight before the loop; each iteration issues block blk + 2 (an empty
+    // group past the end), so waiting for all but the two newest groups means block blk landed.
     load_block(0, 0);
+    cp_async_commit();
+    if (it.nblocks > 1) load_block(1, 1);
     cp_async_commit();
 
     // Per-thread rows: r0 = 16*warp + g, r1 = r0 + 8.
@@ -153,14 +159,10 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
     uint32_t qa[8][4];
 
     for (int blk = 0; blk < it.nblocks; blk++) {
-        int buf = blk & 1;
-        if (blk + 1 < it.nblocks) {
-            load_block(blk + 1, buf ^ 1);
-            cp_async_commit();
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        const int buf = blk % ATT_STAGES;
+        if (blk + 2 < it.nblocks) load_block(blk + 2, (blk + 2) % ATT_STAGES);
+        cp_async_commit();
+        cp_async_wait<2>();
         __syncthreads();
         if (blk == 0) {
 #pragma unroll
@@ -283,7 +285,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
 void launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.n_items <= 0) return;
     if (a.page_slots > 256) throw Error(JV_ERR_UNSUPPORTED, "attention: pages of more than 256 slots");
-    size_t smem = (size_t)(ATT_ROWS + 4 * ATT_KEYS) * ATT_HD * sizeof(__half) + (size_t)a.max_keys * 4;
+    size_t smem = (size_t)(ATT_ROWS + 2 * ATT_STAGES * ATT_KEYS) * ATT_HD * sizeof(__half) + (size_t)a.max_keys * 4;
     if (smem > 227 * 1024) throw Error(JV_ERR_UNSUPPORTED, "attention: too many visible keys for one pass");
     static size_t configured = 0;
     if (smem > configured) {

@@ -866,13 +866,13 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     const float scale = 1.f / std::sqrt((float)c.head_dim);
 
     // Attention work items: runs of consecutive tokens that share (shared, segment) and have
-    // consecutive slots, cut into 16-token tiles, one per KV head; longest first.
+    // consecutive slots, cut into ATT_ITEM_TOKENS-token tiles, one per KV head; longest first.
     std::vector<AttnItem> items;
     if (!decode) {
         int t = 0;
         while (t < T) {
             int n = 1;
-            while (n < 16 && t + n < T && L->shared[t + n] == L->shared[t] && L->seg[t + n] == L->seg[t] &&
+            while (n < ATT_ITEM_TOKENS && t + n < T && L->shared[t + n] == L->shared[t] && L->seg[t + n] == L->seg[t] &&
                    L->slot[t + n] == L->slot[t] + n)
                 n++;
             int lim = L->shared[t] + (L->slot[t] + n - 1 - L->seg[t] + 1);
