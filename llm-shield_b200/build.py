@@ -48,7 +48,7 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 
 def build(verbose: bool = False, ptxas: bool = False, force: bool = False) -> Path:
     OUT.mkdir(exist_ok=True)
-    headers = list(CSRC.glob("*.h")) + [PKG.parent / "include" / "jv.h"]
+    headers = list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + [PKG.parent / "include" / "jv.h"]
     jobs = []
     objs = []
     for src in SOURCES:
