@@ -217,6 +217,16 @@ def run_b200(args, rank, world, local_rank, dist):
     torch.cuda.synchronize()
 
     timed = work[args.warmup:]
+    shard = None
+    if args.config == "c5":
+        # C5: one seeded list of world x steps random trees, the same on every rank, sharded
+        # longest-first by estimated cost (jevstral_b200.dp); the z_i come back to rank 0.
+        grng = np.random.default_rng(4242)
+        glob = [c5_decision(grng) for _ in range(world * args.steps)]
+        costs = [jv.dp.decision_cost(len(t), [len(b) for b in br]) for t, br in glob]
+        shard = jv.dp.shard_decisions(costs, world)[rank]
+        timed = [glob[i] for i in shard]
+    results = []
 
     def toks_of(w):
         n = len(w[0]) + (sum(len(b) for b in w[1]) if w[1] else 0)
@@ -245,7 +255,7 @@ def run_b200(args, rank, world, local_rank, dist):
         t0 = time.perf_counter()
         ev0.record(stream)
         for w in timed:
-            step(*w)
+            results.append(step(*w))
         ev1.record(stream)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
@@ -268,6 +278,15 @@ def run_b200(args, rank, world, local_rank, dist):
         t = torch.tensor([dev_s, wall], dtype=torch.float64, device=f"cuda:{local_rank}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_s, wall = t.tolist()
+        # the whole job's tokens: ranks may hold different shares (C5 shards by cost)
+        tt = torch.tensor([float(tokens), float(len(timed))], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        job_tokens, job_decisions = tt.tolist()
+    else:
+        job_tokens, job_decisions = float(tokens), float(len(timed))
+    gathered = None
+    if shard is not None:
+        gathered = jv.dp.gather_results(dist, rank, world, list(zip(shard, [r.tolist() for r in results])))
 
     res = None
     if rank == 0:
@@ -278,7 +297,7 @@ def run_b200(args, rank, world, local_rank, dist):
         n_dec = len(timed)
         res = {
             "metric": f"tree-decision prefill tokens/s ({args.config.upper()})",
-            "value": world * tokens / dev_s,
+            "value": job_tokens / dev_s,
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
@@ -292,8 +311,8 @@ def run_b200(args, rank, world, local_rank, dist):
             "config": {"workload": WORKLOADS[args.config], "weights": qtype, "tokens_per_step": tokens // n_dec,
                        "parallelism": f"dp{world} (independent replicas, no collective)",
                        "l2": "weights (3.2+ GB) exceed the 126 MB L2 and stream from HBM every step"},
-            "decisions_per_s": world * n_dec / dev_s,
-            "linear_tflops": world * tokens * LINEAR_FLOPS_PER_TOKEN * args.layers / 26 / dev_s / 1e12,
+            "decisions_per_s": job_decisions / dev_s,
+            "linear_tflops": job_tokens * LINEAR_FLOPS_PER_TOKEN * args.layers / 26 / dev_s / 1e12,
             "attention_pairs_per_step": pairs // n_dec,
             "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (all four projections)",
                          "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
@@ -306,12 +325,14 @@ def run_b200(args, rank, world, local_rank, dist):
                             "tflops": (v["flops"] / (v["ms"] / 1e3) / 1e12) if v["ms"] else None,
                             "gbs": (v["bytes"] / (v["ms"] / 1e3) / 1e9) if v["ms"] else None}
                         for k, v in prof.items()},
-            "e2e": {"value": world * tokens / wall, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "e2e": {"value": job_tokens / wall, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "how": "host wall-clock around the public C-ABI calls (jv_forward_tree) with host buffers"},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
+        if gathered is not None:
+            res["gathered_decisions"] = len(gathered)  # z_i of every rank's shard, collected on rank 0
     ctx.close()
     model.close()
     return res

@@ -11,3 +11,4 @@ from .decider import (DecisionResult, TokenDecider, decision_probs, margins_from
                       softmax)
 from .layout import TokenLayout  # noqa: F401
 from .model import KvCache, MinistralModel, Model, ModelConfig, Snapshot, device_count, kernel_launches  # noqa: F401
+from . import dp  # noqa: F401,E402
