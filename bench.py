@@ -226,6 +226,9 @@ def run_b200(args, rank, world, local_rank, dist):
         costs = [jv.dp.decision_cost(len(t), [len(b) for b in br]) for t, br in glob]
         shard = jv.dp.shard_decisions(costs, world)[rank]
         timed = [glob[i] for i in shard]
+        # size every buffer before the clock starts: the shard's largest tree once
+        step(*max(timed, key=lambda w: len(w[0]) + sum(len(b) for b in w[1])))
+        torch.cuda.synchronize()
     results = []
 
     def toks_of(w):
@@ -450,7 +453,8 @@ def main():
         import torch.distributed as tdist
 
         torch.cuda.set_device(local_rank)
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                 device_id=torch.device("cuda", local_rank))
         dist = tdist
     res = run_b200(args, rank, world, local_rank, dist)
     if rank == 0 and res is not None:
