@@ -158,8 +158,10 @@ struct AttnArgs {
     int tpad;
     float* ctx32;               // optional [T][qdim]
     int max_keys = 0;           // largest visible-key count of any item (sizes the key table)
+    int* err = nullptr;         // device error word (tensor-core kernel's bounded waits)
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
+void launch_attention_tc(const AttnArgs& a, cudaStream_t s);
 
 struct DecodeAttnArgs {
     const float* q32;           // [heads*hd]

@@ -612,6 +612,16 @@ void observe_kslab(jv_ctx* x, const std::string& name, const __half* xs, int T, 
     observe(x, name, tmp, T, K);
 }
 
+// JV_ATTN_KERNEL=mma selects the mma.sync prefill attention (kernels_attn.cu) instead of the
+// tcgen05 one (attn_tc.cu): the cross-check of the tensor-core kernel.
+bool attention_on_mma_sync() {
+    static const bool v = [] {
+        const char* e = getenv("JV_ATTN_KERNEL");
+        return e != nullptr && strcmp(e, "mma") == 0;
+    }();
+    return v;
+}
+
 void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float* y, int ldy, int epi,
           __half* xs_out = nullptr) {
     static const bool use_ref = getenv("JV_GEMM_REFERENCE") != nullptr;
@@ -1064,9 +1074,13 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         aa.tpad = tpad;
         aa.ctx32 = capture ? x->ctx32.get((size_t)T * qdim) : nullptr;
         aa.max_keys = max_item_keys;
+        aa.err = x->d_err;
         {
             ProfScope ps(x, JV_PROF_ATTENTION, attn_flops, attn_bytes);
-            launch_attention(aa, s);
+            if (attention_on_mma_sync())
+                launch_attention(aa, s);
+            else
+                launch_attention_tc(aa, s);
         }
         if (capture) observe(x, p + "attn_weighted", aa.ctx32, T, qdim);
         if (capture) {

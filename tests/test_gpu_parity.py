@@ -295,6 +295,46 @@ def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
         assert e < 2e-3, (k, errs)
 
 
+def test_tensor_core_attention_matches_the_mma_sync_attention(model_factory):
+    """The tcgen05 prefill attention against the mma.sync one on the same cache: a 1100-token
+    causal trunk (nine 128-key blocks, ragged last block) and then a tree over it, per layer."""
+    path = model_factory(WIDE_CFG, "Q8_0", seed=6)
+    code = (
+        "import sys, numpy as np; sys.path[:0] = sys.argv[2:];"
+        "import jevstral_b200 as jv;"
+        "m = jv.Model(sys.argv[1], kv_pool_mb=512); c = jv.MinistralModel(m); caps = {};"
+        "c.set_activation_sink(lambda n, a: caps.__setitem__('t.' + n, a));"
+        "trunk = [1] + [(7 * i) % 16000 + 100 for i in range(1099)];"
+        "c.forward(trunk);"
+        "c.set_activation_sink(lambda n, a: caps.__setitem__('b.' + n, a));"
+        "z = c.forward_tree([5, 6, 7], [[11, 12, 13, 14], [21], [31, 32]], [40, 41, 42]);"
+        "caps['z'] = np.asarray(z, dtype=np.float32);"
+        "np.savez(sys.stdout.buffer, **{k: v for k, v in caps.items() if k == 'z' or k.endswith('attn_weighted')})"
+    )
+    import io
+
+    from conftest import REPO
+
+    paths = [str(REPO / "llm-shield_b200"), str(REPO)]
+    outs = []
+    for kernel in ("tc", "mma"):
+        env = dict(os.environ)
+        env["JV_ATTN_KERNEL"] = kernel
+        r = subprocess.run([sys.executable, "-c", code, str(path)] + paths, env=env, capture_output=True, timeout=900)
+        assert r.returncode == 0, r.stderr.decode()[-2000:]
+        outs.append(np.load(io.BytesIO(r.stdout)))
+    tc, mma = outs
+    # Layer 0 sees identical Q/K/V in both runs (exp rounding and summation order differ);
+    # later layers also inherit fp16 re-rounding of slightly different activations.
+    errs = {k: rel_l2(tc[k], mma[k]) for k in mma.files if k != "z"}
+    assert len(errs) == 2 * WIDE_CFG.layers
+    for k in ("t.blk.0.attn_weighted", "b.blk.0.attn_weighted"):
+        assert errs[k] < 2e-3, (k, errs)
+    for k, e in errs.items():
+        assert e < 1e-2, (k, errs)
+    assert np.abs(tc["z"] - mma["z"]).max() < 2e-2
+
+
 def test_kernel_launches_are_counted(small):
     before = jv.kernel_launches()
     with ctx(small) as c:
