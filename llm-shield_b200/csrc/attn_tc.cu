@@ -12,10 +12,15 @@
 //   P  = exp2(S * scale * log2 e - m)   softmax warps, one query row per thread, online max/sum,
 //                                        O rescaled in TMEM when the row maximum moves
 //   O += P V        M = 128, N = 128 dims, K = 128 keys; V read through an MN-major descriptor
-// Warps 0-3 run the softmax and the output, warps 4-7 load Q and the K/V blocks (cp.async into
-// a 2-deep ring, SWIZZLE_128B placement), warp 8 owns TMEM and issues the MMAs. S is double
-// buffered, so the next block's Q K^T runs while this block's softmax does. Every wait is
-// bounded (2 s of %globaltimer); on expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
+// Warps 0-3 run the softmax and the output. Warp 4 fills a 2-deep K ring and warp 5 a 2-deep V
+// ring: KV pages store their rows in the operand swizzle (kv_chunk_offset), so each run of
+// consecutive slots inside one page is two bulk copies (one per 64-dim half); a run whose
+// first row sits at a different position modulo 8 in the page than in the tile (a branch
+// segment starting off a multiple of 8) goes chunk by chunk through cp.async instead. Warp 6
+// owns TMEM and issues the MMAs from an event loop: P V(b) as soon as P(b) and V(b) are in
+// place, S(b) as soon as K(b) and an S buffer are free (S is double buffered, so the next
+// block's Q K^T runs while this block's softmax does). Every wait is bounded (2 s of
+// %globaltimer); on expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
 #include "tc_common.cuh"
 
 namespace jv {
@@ -23,8 +28,9 @@ namespace {
 
 constexpr int AT_ROWS = 128;                 // 32 tokens x 4 query heads
 constexpr int AT_KEYS = 128;                 // keys per block
-constexpr int AT_THREADS = 288;              // 9 warps
+constexpr int AT_THREADS = 224;              // 7 warps
 constexpr int AT_TILE = 128 * 128 * 2;       // one [128][128] fp16 tile, two 16 KB halves
+constexpr int AT_PAGES = 1024;               // page-table entries staged in shared memory
 constexpr float AT_LOG2E = 1.4426950408889634f;
 
 // Byte offset of 16-byte chunk c (0..15) of row r in a [128][128] fp16 tile stored as two
@@ -94,18 +100,32 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
 
+__device__ __forceinline__ void mbar_add_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     extern __shared__ uint8_t at_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)at_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* Qs = sm;                       // [128 rows][128 dims]
     uint8_t* Ps = sm + AT_TILE;             // [128 rows][128 keys]
-    uint8_t* KV = sm + 2 * AT_TILE;         // stage s: K tile at KV + s * 2 * AT_TILE, V tile after it
-    uint32_t* tabs = (uint32_t*)(KV + 4 * AT_TILE);  // [2 stages][128 keys] (page << 8) | slot in page
-    uint64_t* bars = (uint64_t*)(tabs + 2 * AT_KEYS);
-    const uint32_t q_full = s_addr(bars), kv_full = q_full + 8, kv_empty = kv_full + 16, s_full = kv_empty + 16;
-    const uint32_t s_empty = s_full + 16, p_full = s_empty + 16, o_done = p_full + 8;
-    uint32_t* tslot = (uint32_t*)(bars + 11);
-    volatile uint32_t* flags = tslot + 1;  // [2] loader stage verdicts
+    uint8_t* Ks = sm + 2 * AT_TILE;         // 2 stages of [128 keys][128 dims]
+    uint8_t* Vs = sm + 4 * AT_TILE;         // 2 stages of [128 keys][128 dims]
+    int32_t* pg = (int32_t*)(sm + 6 * AT_TILE);  // physical pages of the item's keys
+    uint64_t* bars = (uint64_t*)(pg + AT_PAGES);
+    const uint32_t q_full = s_addr(bars), k_full = q_full + 8, k_empty = k_full + 16, v_full = k_empty + 16;
+    const uint32_t v_empty = v_full + 16, s_full = v_empty + 16, s_empty = s_full + 16, p_full = s_empty + 16;
+    const uint32_t o_done = p_full + 8;
+    uint32_t* tslot = (uint32_t*)(bars + 15);
 
     pdl_launch_dependents();
     pdl_wait();
@@ -113,14 +133,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int group = a.heads / a.kv_heads;  // 4 (checked on the host)
     const int qdim = a.heads * 128;
+    const int ps = a.page_slots;
     const int max_limit = it.shared + (it.slot0 + it.ntok - 1 - it.segment + 1);
     const int nb = (max_limit + AT_KEYS - 1) / AT_KEYS;
+    // keys below `shared` (region A) are slots 0.., the rest (region B) slots segment..
+    const int nA = min(it.shared, max_limit), nBk = max_limit - nA;
+    const int pagesA = (nA + ps - 1) / ps;
+    const int pB0 = nBk > 0 ? it.segment / ps : 0;
+    const int pagesB = nBk > 0 ? (it.segment + nBk - 1) / ps - pB0 + 1 : 0;
 
     if (tid == 0) {
-        mbar_init(q_full, 128);
+        mbar_init(q_full, 64);
         for (int i = 0; i < 2; i++) {
-            mbar_init(kv_full + 8 * i, 128);
-            mbar_init(kv_empty + 8 * i, 1);
+            mbar_init(k_full + 8 * i, 32);
+            mbar_init(k_empty + 8 * i, 1);
+            mbar_init(v_full + 8 * i, 32);
+            mbar_init(v_empty + 8 * i, 1);
             mbar_init(s_full + 8 * i, 1);
             mbar_init(s_empty + 8 * i, 4);
         }
@@ -128,18 +156,23 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
         mbar_init(o_done, 1);
         fence_barrier_init();
     }
-    if (warp == 8) tmem_alloc(s_addr(tslot), 512);
+    if (warp == 6) tmem_alloc(s_addr(tslot), 512);
+    if (warp == 4 || warp == 5) {
+        // stage the page-table entries of both key regions (the host keeps them <= AT_PAGES)
+        for (int i = tid - 128; i < pagesA + pagesB; i += 64)
+            pg[i] = __ldg(a.page_table + (i < pagesA ? i : pB0 + (i - pagesA)));
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;  // O at columns 0-127, S buffers at 128-255 and 256-383
     int* err = a.err;
 
-    if (warp >= 4 && warp < 8) {
+    if (warp == 4 || warp == 5) {
         // ----------------------------------------------------------------- loaders
         const int lt = tid - 128;
         // Q: row r = token r / 4 x head r % 4 of this KV head
-        for (int id = lt; id < AT_ROWS * 16; id += 128) {
+        for (int id = lt; id < AT_ROWS * 16; id += 64) {
             const int r = id >> 4, c = id & 15;
             const int tl = r / group, j = r % group;
             const bool ok = tl < it.ntok;
@@ -149,85 +182,104 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
         cp_wait_all();
         fence_proxy_async();
         mbar_arrive(q_full);
-        const int64_t head_off = (int64_t)((a.layer * a.kv_heads + it.kv_head) * 2) * a.page_slots * 256;
-        const int64_t v_off = (int64_t)a.page_slots * 256;
-        // where key lt of block b lives; the page-table read for block b + 1 is issued a block early
-        auto lookup = [&](int b, int& page, int& sub) {
-            const int L = b * AT_KEYS + lt;
-            page = -1;
-            sub = 0;
-            if (L < max_limit) {
-                const int slot = L < it.shared ? L : it.segment + (L - it.shared);
-                page = __ldg(a.page_table + slot / a.page_slots);
-                sub = slot % a.page_slots;
-            }
-        };
-        int page, sub;
-        lookup(0, page, sub);
+        const int kv = warp - 4;  // 0: K ring, 1: V ring
+        const char* pool = (const char*)a.kv_pool + kv_plane_offset(a.layer, a.kv_heads, it.kv_head, kv, ps);
+        const uint32_t full = kv ? v_full : k_full, empty = kv ? v_empty : k_empty;
+        const uint32_t ring = s_addr(kv ? Vs : Ks);
         for (int b = 0; b < nb; b++) {
             const int s = b & 1;
-            tabs[s * AT_KEYS + lt] = page < 0 ? 0xFFFFFFFFu : ((uint32_t)page << 8) | (uint32_t)sub;
-            if (b + 1 < nb) lookup(b + 1, page, sub);
-            // one thread waits for the stage; the named barrier hands its verdict (one flag per
-            // stage, so a flag is rewritten only after every loader has read it) to the others
-            if (lt == 0) flags[s] = mbar_wait(kv_empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u) ? 1u : 0u;
-            asm volatile("bar.sync 1, 128;\n" ::: "memory");
-            if (!flags[s]) {
-                if (lt == 0) atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u);
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+                if (lane == 0) atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
                 break;
             }
-            const uint32_t kd = s_addr(KV + s * 2 * AT_TILE), vd = kd + AT_TILE;
-            const int c = lt & 15;
-#pragma unroll 4
-            for (int key = lt >> 4; key < AT_KEYS; key += 8) {
-                const uint32_t e = tabs[s * AT_KEYS + key];
-                const char* row = (const char*)a.kv_pool;
-                int bytes = 0;
-                if (e != 0xFFFFFFFFu) {
-                    row = (const char*)a.kv_pool + (int64_t)(e >> 8) * a.page_bytes + (int64_t)(e & 255u) * 256 + head_off;
-                    bytes = 16;
+            const uint32_t tile = ring + (uint32_t)(s * AT_TILE);
+            const int L0 = b * AT_KEYS, nvalid = min(AT_KEYS, max_limit - L0);
+            // runs of consecutive slots inside one page: region A, then region B
+#pragma unroll 1
+            for (int reg = 0; reg < 2; reg++) {
+                int La = reg == 0 ? L0 : max(L0, nA);
+                const int Lb = reg == 0 ? min(L0 + nvalid, nA) : L0 + nvalid;
+                while (La < Lb) {
+                    const int slot = reg == 0 ? La : it.segment + (La - nA);
+                    const int row = slot % ps;
+                    const int n = min(Lb - La, ps - row);
+                    const int page = reg == 0 ? pg[slot / ps] : pg[pagesA + slot / ps - pB0];
+                    const char* plane = pool + (int64_t)page * a.page_bytes;
+                    const int key0 = La - L0;
+                    if (((key0 - row) & 7) == 0) {
+                        if (lane == 0) {
+                            mbar_add_tx(full + 8 * s, (uint32_t)(2 * n * 128));
+                            bulk_g2s(tile + (uint32_t)(key0 * 128), plane + row * 128, (uint32_t)(n * 128), full + 8 * s);
+                            bulk_g2s(tile + 16384u + (uint32_t)(key0 * 128), plane + ps * 128 + row * 128,
+                                     (uint32_t)(n * 128), full + 8 * s);
+                        }
+                    } else {
+                        for (int i = lane; i < n * 16; i += 32) {
+                            const int r = i >> 4, c = i & 15;
+                            cp16(tile + tile_off(key0 + r, c), plane + kv_chunk_offset(row + r, c, ps), 16);
+                        }
+                    }
+                    La += n;
                 }
-                cp16(kd + tile_off(key, c), row + c * 16, bytes);
-                cp16(vd + tile_off(key, c), row + v_off + c * 16, bytes);
+            }
+            // rows past the last visible key: zeros, so 0-probability keys add exact zeros
+            for (int i = lane; i < (AT_KEYS - nvalid) * 16; i += 32) {
+                const int r = nvalid + (i >> 4), c = i & 15;
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(tile + tile_off(r, c)), "r"(0u) : "memory");
             }
             cp_wait_all();
             fence_proxy_async();
-            mbar_arrive(kv_full + 8 * s);
+            mbar_arrive(full + 8 * s);
         }
         cp_wait_all();
-    } else if (warp == 8) {
+    } else if (warp == 6) {
         if (lane == 0) {  // ------------------------------------------------------- MMA
             const uint32_t id_s = idesc_f16(AT_KEYS, AT_ROWS);
             const uint32_t id_pv = idesc_f16(128, AT_ROWS) | (1u << 16);  // B (V) MN-major
             bool ok = mbar_wait(q_full, 0);
-            auto issue_s = [&](int b) -> bool {
-                const int s = b & 1;
-                if (!mbar_wait(kv_full + 8 * s, (uint32_t)((b >> 1) & 1))) return false;
-                if (!mbar_wait(s_empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u)) return false;
-                tc_fence_after();
-                const uint32_t q = s_addr(Qs), k = s_addr(KV + s * 2 * AT_TILE);
-                const uint32_t d = tmem + 128u + (uint32_t)(s * 128);
+            tc_fence_after();
+            int ns = 0, np = 0;  // next S to issue, next P V to issue
+            uint64_t idle_since = gtimer();
+            while (ok && np < nb) {
+                bool did = false;
+                if (np < ns && mbar_test(p_full, (uint32_t)(np & 1)) &&
+                    mbar_test(v_full + 8 * (np & 1), (uint32_t)((np >> 1) & 1))) {
+                    tc_fence_after();
+                    const int s = np & 1;
+                    const uint32_t p = s_addr(Ps), v = s_addr(Vs + s * AT_TILE);
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                    umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
-                }
-                umma_commit(s_full + 8 * s);
-                return true;
-            };
-            if (ok) ok = issue_s(0);
-            for (int b = 0; b < nb && ok; b++) {
-                if (b + 1 < nb && !issue_s(b + 1)) { ok = false; break; }
-                if (!mbar_wait(p_full, (uint32_t)(b & 1))) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t p = s_addr(Ps), v = s_addr(KV + (b & 1) * 2 * AT_TILE + AT_TILE);
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                        umma(tmem, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (np > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(v_empty + 8 * s);
+                    umma_commit(o_done);  // last: its arrival implies the stage release before it
+                    np++;
+                    did = true;
+                } else if (ns < nb && mbar_test(k_full + 8 * (ns & 1), (uint32_t)((ns >> 1) & 1)) &&
+                           mbar_test(s_empty + 8 * (ns & 1), (uint32_t)((ns >> 1) & 1) ^ 1u)) {
+                    tc_fence_after();
+                    const int s = ns & 1;
+                    const uint32_t q = s_addr(Qs), k = s_addr(Ks + s * AT_TILE);
+                    const uint32_t d = tmem + 128u + (uint32_t)(s * 128);
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                    umma(tmem, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (b > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                        umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(k_empty + 8 * s);
+                    umma_commit(s_full + 8 * s);
+                    ns++;
+                    did = true;
                 }
-                umma_commit(kv_empty + 8 * (b & 1));
-                umma_commit(o_done);  // last: its arrival implies the stage release before it
+                if (did) {
+                    idle_since = gtimer();
+                } else {
+                    __nanosleep(32);
+                    if (gtimer() - idle_since > WAIT_NS) ok = false;
+                }
             }
             if (!ok) atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
         }
@@ -349,7 +401,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 8) {
+    if (warp == 6) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
@@ -357,12 +409,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
 
 }  // namespace
 
-constexpr size_t AT_SMEM = (size_t)6 * AT_TILE + 2 * AT_KEYS * 4 + 128 + 1024;
+constexpr size_t AT_SMEM = (size_t)6 * AT_TILE + AT_PAGES * 4 + 128 + 1024;
+
+// Page-table entries the item with the most visible keys needs: both key regions rounded out to
+// whole pages. Items are runs of at most ATT_ITEM_TOKENS consecutive slots.
+bool attention_tc_fits(int max_keys, int page_slots) { return max_keys / page_slots + 3 <= AT_PAGES; }
 
 void launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
     if (a.n_items <= 0) return;
-    if (a.page_slots > 256) throw Error(JV_ERR_UNSUPPORTED, "attention: pages of more than 256 slots");
+    if (a.page_slots % 8 != 0 || a.page_slots > 256) throw Error(JV_ERR_UNSUPPORTED, "attention: page slots");
     if (a.heads != 4 * a.kv_heads) throw Error(JV_ERR_UNSUPPORTED, "attention: 4 query heads per KV head expected");
+    if (!attention_tc_fits(a.max_keys, a.page_slots))
+        throw Error(JV_ERR_UNSUPPORTED, "attention: too many visible keys for the tensor-core kernel");
     static bool configured = false;
     if (!configured) {
         JV_CUDA(cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT_SMEM));

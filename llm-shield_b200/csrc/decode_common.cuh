@@ -177,12 +177,12 @@ __device__ __forceinline__ bool dec_better(float v, int i, float bv, int bi) {
     return v > bv || (v == bv && i < bi);
 }
 
-__device__ __forceinline__ __half* kv_slot(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots,
-                                           int layer, int kv_heads, int head, int kv, int slot) {
-    int page = page_table[slot / page_slots];
-    int64_t off = (int64_t)page * page_bytes +
-                  ((int64_t)((layer * kv_heads + head) * 2 + kv) * page_slots + (slot % page_slots)) * 256;
-    return (__half*)((char*)pool + off);
+// The (layer, head, K|V) plane of the page holding `slot` (rows inside it are swizzled: see
+// kv_chunk_offset / kv_elem_offset).
+__device__ __forceinline__ char* kv_plane(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots,
+                                          int layer, int kv_heads, int head, int kv, int slot) {
+    return (char*)pool + (int64_t)page_table[slot / page_slots] * page_bytes +
+           kv_plane_offset(layer, kv_heads, head, kv, page_slots);
 }
 
 }  // namespace

@@ -69,6 +69,26 @@ __host__ __device__ inline size_t kslab_offset(int t, int k, int tpad) {
     return ((size_t)kb * tpad + t) * 64 + c * 8 + (kk & 7);
 }
 
+// ----------------------------------------------------------------- KV pages
+
+// A KV page holds page_slots consecutive cache slots (a multiple of 8) of every (layer, kv
+// head): the plane of (layer, head, K = 0 | V = 1) starts at kv_plane_offset bytes into the
+// page. A plane is two halves (dims 0-63, then 64-127) of page_slots rows x 128 bytes, and
+// inside a row the 16-byte chunk of dims 8c..8c+7 sits at chunk position c ^ (row & 7): the
+// same 128-byte swizzle as the K-slab, so a run of rows whose first row is a multiple of 8
+// away from its tile row copies straight into a tensor-core operand tile.
+__host__ __device__ inline int64_t kv_plane_offset(int layer, int kv_heads, int head, int kv, int page_slots) {
+    return (int64_t)((layer * kv_heads + head) * 2 + kv) * page_slots * 256;
+}
+// Byte offset inside a plane of the 16-byte chunk holding dims 8c..8c+7 (c < 16) of row `row`.
+__host__ __device__ inline int kv_chunk_offset(int row, int c, int page_slots) {
+    return (c >> 3) * page_slots * 128 + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+}
+// Byte offset inside a plane of dim d of row `row`.
+__host__ __device__ inline int kv_elem_offset(int row, int d, int page_slots) {
+    return kv_chunk_offset(row, d >> 3, page_slots) + (d & 7) * 2;
+}
+
 // ------------------------------------------------------------ GEMM plans
 
 // EPI_SWIGLU: the fused gate/up matrix (each 128-row tile = 64 gate rows then the 64 matching
@@ -162,6 +182,7 @@ struct AttnArgs {
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 void launch_attention_tc(const AttnArgs& a, cudaStream_t s);
+bool attention_tc_fits(int max_keys, int page_slots);  // the tensor-core kernel takes this pass
 
 struct DecodeAttnArgs {
     const float* q32;           // [heads*hd]

@@ -62,12 +62,13 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 // Row r of a [rows][128] fp16 tile: 16-byte chunk c lives at chunk c ^ (r & 7).
 __device__ __forceinline__ int swz(int r, int c) { return r * ATT_HD + ((c ^ (r & 7)) << 3); }
 
-__device__ __forceinline__ const __half* kv_row(const __half* pool, const int32_t* page_table, int64_t page_bytes,
-                                                int page_slots, int layer, int kv_heads, int head, int kv, int slot) {
-    int page = page_table[slot / page_slots];
-    int64_t off = (int64_t)page * page_bytes +
-                  ((int64_t)((layer * kv_heads + head) * 2 + kv) * page_slots + (slot % page_slots)) * 256;
-    return (const __half*)((const char*)pool + off);
+// The (layer, head, K|V) plane of the page holding `slot`, and the slot's row in it.
+__device__ __forceinline__ const char* kv_plane(const __half* pool, const int32_t* page_table, int64_t page_bytes,
+                                                int page_slots, int layer, int kv_heads, int head, int kv, int slot,
+                                                int& row) {
+    row = slot % page_slots;
+    return (const char*)pool + (int64_t)page_table[slot / page_slots] * page_bytes +
+           kv_plane_offset(layer, kv_heads, head, kv, page_slots);
 }
 
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
@@ -128,9 +129,10 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
             int bytes = 0;
             if (L < max_limit) {
                 const uint32_t e = tab[L];
-                const char* row = (const char*)a.kv_pool + (int64_t)(e >> 8) * a.page_bytes + (int64_t)(e & 255u) * 256 + head_off;
-                ks = (const __half*)row + c * 8;
-                vs = (const __half*)(row + v_off) + c * 8;
+                const char* plane = (const char*)a.kv_pool + (int64_t)(e >> 8) * a.page_bytes + head_off;
+                const int off = kv_chunk_offset((int)(e & 255u), c, a.page_slots);
+                ks = (const __half*)(plane + off);
+                vs = (const __half*)(plane + v_off + off);
                 bytes = 16;
             }
             cp_async16(kd + swz(r, c), ks, bytes);
@@ -321,10 +323,11 @@ __global__ void k_decode_attention(DecodeAttnArgs a) {
     for (int i = lane; i < nk; i += 32) {
         int L = k0 + i;
         int slot = L < a.shared ? L : a.segment + (L - a.shared);
-        const __half* k = kv_row(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot);
+        int row;
+        const char* k = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot, row);
         float acc = 0.f;
         for (int d = 0; d < ATT_HD; d += 8) {
-            int4 raw = *(const int4*)(k + d);
+            int4 raw = *(const int4*)(k + kv_chunk_offset(row, d >> 3, a.page_slots));
             const __half2* kh = (const __half2*)&raw;
 #pragma unroll
             for (int e = 0; e < 4; e++) {
@@ -351,9 +354,10 @@ __global__ void k_decode_attention(DecodeAttnArgs a) {
     for (int i = 0; i < nk; i++) {
         int L = k0 + i;
         int slot = L < a.shared ? L : a.segment + (L - a.shared);
-        const __half* v = kv_row(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot);
+        int row;
+        const char* v = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot, row);
         float p = ps[h * DEC_KEYS + i];
-        uint2 raw = *(const uint2*)(v + lane * 4);
+        uint2 raw = *(const uint2*)(v + kv_elem_offset(row, lane * 4, a.page_slots));
         const __half2* vh = (const __half2*)&raw;
         float2 v01 = __half22float2(vh[0]), v23 = __half22float2(vh[1]);
         acc[0] = fmaf(p, v01.x, acc[0]);

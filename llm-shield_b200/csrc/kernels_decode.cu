@@ -246,12 +246,12 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
                     a.q32[tile * 128 + 2 * t] = r0;
                     a.q32[tile * 128 + 2 * t + 1] = r1;
                 } else {
-                    __half* dst = kv_slot(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq, 0, st.slot);
-                    *(__half2*)(dst + 2 * t) = __floats2half2_rn(r0, r1);
+                    char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq, 0, st.slot);
+                    *(__half2*)(dst + kv_elem_offset(st.slot % a.page_slots, 2 * t, a.page_slots)) = __floats2half2_rn(r0, r1);
                 }
             } else {
-                __half* dst = kv_slot(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq - hk, 1, st.slot);
-                *(__half2*)(dst + 2 * t) = __floats2half2_rn(x0, x1);
+                char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq - hk, 1, st.slot);
+                *(__half2*)(dst + kv_elem_offset(st.slot % a.page_slots, 2 * t, a.page_slots)) = __floats2half2_rn(x0, x1);
             }
         }
     } else if (MODE == DEC_HEAD) {
@@ -337,8 +337,9 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
     __shared__ __align__(16) float qs[8 * 128];
     __shared__ float ps[8 * DA_KEYS];
     __shared__ int s_last;
-    __shared__ const __half* krow[DA_KEYS];
-    __shared__ const __half* vrow[DA_KEYS];
+    __shared__ const char* krow[DA_KEYS];  // K and V planes of each key's page, and its row there
+    __shared__ const char* vrow[DA_KEYS];
+    __shared__ int krowi[DA_KEYS];
     pdl_launch_dependents();
     pdl_wait();
     const DecodeStep st = *a.step;
@@ -357,15 +358,17 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
             const int L = k0 + threadIdx.x;
             const int slot = L < st.shared ? L : st.segment + (L - st.shared);
             __half* pool = const_cast<__half*>(a.kv_pool);
-            krow[threadIdx.x] = kv_slot(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot);
-            vrow[threadIdx.x] = kv_slot(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot);
+            krow[threadIdx.x] = kv_plane(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot);
+            vrow[threadIdx.x] = kv_plane(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot);
+            krowi[threadIdx.x] = slot % a.page_slots;
         }
         for (int i = threadIdx.x; i < group * 128; i += nthreads) qs[i] = a.q32[kvh * group * 128 + i];
         __syncthreads();
         for (int i = threadIdx.x; i < nk * 16; i += nthreads) {
             const int key = i >> 4, c = i & 15;
-            cp_async16(ks + key * DA_STRIDE + c * 8, krow[key] + c * 8);
-            cp_async16(vs + key * 128 + c * 8, vrow[key] + c * 8);
+            const int off = kv_chunk_offset(krowi[key], c, a.page_slots);
+            cp_async16(ks + key * DA_STRIDE + c * 8, krow[key] + off);
+            cp_async16(vs + key * 128 + c * 8, vrow[key] + off);
         }
         cp_async_wait_all();
         __syncthreads();

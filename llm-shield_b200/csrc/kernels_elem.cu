@@ -165,14 +165,6 @@ void launch_rope_table(float2* table, const float* freqs, int half, int pos0, in
     note_launch();
 }
 
-__device__ __forceinline__ __half* kv_addr(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots,
-                                           int layer, int kv_heads, int head, int kv, int slot) {
-    int page = page_table[slot / page_slots];
-    int64_t off = (int64_t)page * page_bytes +
-                  ((int64_t)((layer * kv_heads + head) * 2 + kv) * page_slots + (slot % page_slots)) * 256;
-    return (__half*)((char*)pool + off);
-}
-
 // RotateQueries / StoreKeys / StoreValues / ApplyPositionScale (MinistralModel.cs:638-682):
 // adjacent-pair rotation at position[t] (x0*cos - x1*sin, x0*sin + x1*cos with separate
 // roundings), the llama-4 temperature on q, then q to the attention operand and k, v to
@@ -202,10 +194,10 @@ __global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
         float interval = floorf(__fdiv_rn((float)pos, (float)a.orig_ctx));
         if (interval != 0.f) temp = __fadd_rn(1.0f, __fmul_rn(a.temperature_scale, logf(__fadd_rn(1.0f, interval))));
     }
-    // this token's slot row, K plane of (layer, kv head 0); heads and V are fixed offsets
-    const int page = a.page_table[slot / a.page_slots];
-    char* kv0 = (char*)a.kv_pool + (int64_t)page * a.page_bytes +
-                ((int64_t)(a.layer * a.kv_heads * 2) * a.page_slots + (slot % a.page_slots)) * 256;
+    // K plane of (layer, kv head 0) in this token's page; heads and V are fixed plane offsets,
+    // the slot's row inside a plane is swizzled (kv_elem_offset)
+    const int page = a.page_table[slot / a.page_slots], row_in_page = slot % a.page_slots;
+    char* kv0 = (char*)a.kv_pool + (int64_t)page * a.page_bytes + kv_plane_offset(a.layer, a.kv_heads, 0, 0, a.page_slots);
     const int64_t head_stride = (int64_t)2 * a.page_slots * 256, v_off = (int64_t)a.page_slots * 256;
     const int nq4 = qdim / 4, nk4 = kvdim / 4;
     for (int i = threadIdx.x; i < nq4 + 2 * nk4; i += blockDim.x) {
@@ -227,14 +219,14 @@ __global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
                 if (a.q32) *(float4*)(a.q32 + (int64_t)t * qdim + e) = make_float4(r[0], r[1], r[2], r[3]);
             } else {
                 const int ke = e - qdim, head = ke / hd;
-                __half2* dst = (__half2*)(kv0 + head * head_stride) + d / 2;
+                __half2* dst = (__half2*)(kv0 + head * head_stride + kv_elem_offset(row_in_page, d, a.page_slots));
                 dst[0] = __floats2half2_rn(r[0], r[1]);
                 dst[1] = __floats2half2_rn(r[2], r[3]);
                 if (a.k32) *(float4*)(a.k32 + (int64_t)t * kvdim + ke) = make_float4(r[0], r[1], r[2], r[3]);
             }
         } else {  // v: straight copy to its slot
             const int ve = 4 * i - qdim - kvdim, head = ve / hd, d = ve % hd;
-            __half2* dst = (__half2*)(kv0 + head * head_stride + v_off) + d / 2;
+            __half2* dst = (__half2*)(kv0 + head * head_stride + v_off + kv_elem_offset(row_in_page, d, a.page_slots));
             dst[0] = __floats2half2_rn(x.x, x.y);
             dst[1] = __floats2half2_rn(x.z, x.w);
         }
@@ -316,8 +308,9 @@ __global__ void k_kv_export(const __half* __restrict__ pool, const int32_t* __re
         int kv = (int)(r / layers);
         int page = page_table[p / page_slots];
         const __half* src = (const __half*)((const char*)pool + (int64_t)page * page_bytes +
-                                             ((int64_t)((l * kv_heads + h) * 2 + kv) * page_slots + p % page_slots) * 256);
-        out[i] = __half2float(src[d]);
+                                             kv_plane_offset(l, kv_heads, h, kv, page_slots) +
+                                             kv_elem_offset(p % page_slots, d, page_slots));
+        out[i] = __half2float(*src);
     }
 }
 
@@ -334,9 +327,9 @@ __global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict
         int l = (int)(r % layers);
         int kv = (int)(r / layers);
         int page = page_table[p / page_slots];
-        __half* dst = (__half*)((char*)pool + (int64_t)page * page_bytes +
-                                ((int64_t)((l * kv_heads + h) * 2 + kv) * page_slots + p % page_slots) * 256);
-        dst[d] = __float2half_rn(in[i]);
+        __half* dst = (__half*)((char*)pool + (int64_t)page * page_bytes + kv_plane_offset(l, kv_heads, h, kv, page_slots) +
+                                kv_elem_offset(p % page_slots, d, page_slots));
+        *dst = __float2half_rn(in[i]);
     }
 }
 

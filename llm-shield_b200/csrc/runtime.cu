@@ -1077,7 +1077,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         aa.err = x->d_err;
         {
             ProfScope ps(x, JV_PROF_ATTENTION, attn_flops, attn_bytes);
-            if (attention_on_mma_sync())
+            if (attention_on_mma_sync() || !attention_tc_fits(max_item_keys, m->page_slots))
                 launch_attention(aa, s);
             else
                 launch_attention_tc(aa, s);
