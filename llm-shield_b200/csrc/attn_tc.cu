@@ -6,29 +6,32 @@
 // blocks cut on logical indices, so a token's output is bit-identical whether it runs in a
 // tree, alone after the trunk, or after a cached prefix.
 //
-// One CTA = one KV head x up to 32 tokens of one segment; the 4 query heads of the KV head ride
-// in M (128 rows = TMEM lanes). Per block of 128 keys:
+// One CTA = one KV head x up to 64 consecutive tokens of one segment, as two query tiles X = A
+// (tokens 0-31) and B (32-63); in a tile the 4 query heads of the KV head ride in M (128 rows =
+// TMEM lanes). Both tiles share every K/V block. Per tile and block of 128 keys:
 //   S  = Q K^T      tcgen05.mma kind::f16, M = 128, N = 128 keys, K = 128 dims -> TMEM (fp32)
-//   P  = exp2(S * scale * log2 e - m)   softmax warps, one query row per thread, online max/sum,
-//                                        O rescaled in TMEM when the row maximum moves
-//   O += P V        M = 128, N = 128 dims, K = 128 keys; V read through an MN-major descriptor
-// Warps 0-3 run the softmax and the output. Warp 4 fills a 2-deep K ring and warp 5 a 2-deep V
-// ring: KV pages store their rows in the operand swizzle (kv_chunk_offset), so each run of
-// consecutive slots inside one page is two bulk copies (one per 64-dim half); a run whose
-// first row sits at a different position modulo 8 in the page than in the tile (a branch
-// segment starting off a multiple of 8) goes chunk by chunk through cp.async instead. Warp 6
-// owns TMEM and issues the MMAs from an event loop: P V(b) as soon as P(b) and V(b) are in
-// place, S(b) as soon as K(b) and an S buffer are free (S is double buffered, so the next
-// block's Q K^T runs while this block's softmax does). Every wait is bounded (2 s of
-// %globaltimer); on expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
+//   P  = exp2(S * scale * log2 e - m)   one query row per softmax thread, online max/sum, O
+//                                        rescaled in TMEM when the row maximum moves; P is
+//                                        written back as fp16 pairs over the tile's own S columns
+//   O += P V        A = P straight from TMEM, B = V through an MN-major SWIZZLE_128B descriptor
+// TMEM: O_A, O_B, S_A (P_A), S_B (P_B), 128 columns each. Warps 0-3 run tile A's softmax, warps
+// 4-7 tile B's, so the two tiles' exponentials interleave on each scheduler while the tensor
+// core works on the other tile. Warp 8 fills a 2-deep K ring and warp 9 a 2-deep V ring: KV
+// pages store their rows in the operand swizzle (kv_chunk_offset), so each run of consecutive
+// slots inside one page is two bulk copies (one per 64-dim half); a run whose first row sits at
+// a different position modulo 8 in the page than in the tile (a branch segment starting off a
+// multiple of 8) goes chunk by chunk through cp.async instead. Warp 10 owns TMEM and issues the
+// MMAs from an event loop: P V_X(b) as soon as P_X(b) and V(b) are in place, then S_X(b + 1)
+// behind it (it overwrites P_X(b); tcgen05.mma from one thread run in issue order). Every wait
+// is bounded (2 s of %globaltimer); on expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
 #include "tc_common.cuh"
 
 namespace jv {
 namespace {
 
-constexpr int AT_ROWS = 128;                 // 32 tokens x 4 query heads
+constexpr int AT_ROWS = 128;                 // 32 tokens x 4 query heads per tile
 constexpr int AT_KEYS = 128;                 // keys per block
-constexpr int AT_THREADS = 224;              // 7 warps
+constexpr int AT_THREADS = 352;              // 11 warps
 constexpr int AT_TILE = 128 * 128 * 2;       // one [128][128] fp16 tile, two 16 KB halves
 constexpr int AT_PAGES = 1024;               // page-table entries staged in shared memory
 constexpr float AT_LOG2E = 1.4426950408889634f;
@@ -113,18 +116,25 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// D (TMEM) (+)= A (TMEM, 16-bit elements two to a column) x B (shared memory descriptor).
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "r"(tmem_a), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
 __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     extern __shared__ uint8_t at_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)at_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* Qs = sm;                       // [128 rows][128 dims]
-    uint8_t* Ps = sm + AT_TILE;             // [128 rows][128 keys]
+    uint8_t* Qs = sm;                       // 2 tiles of [128 rows][128 dims]
     uint8_t* Ks = sm + 2 * AT_TILE;         // 2 stages of [128 keys][128 dims]
     uint8_t* Vs = sm + 4 * AT_TILE;         // 2 stages of [128 keys][128 dims]
     int32_t* pg = (int32_t*)(sm + 6 * AT_TILE);  // physical pages of the item's keys
     uint64_t* bars = (uint64_t*)(pg + AT_PAGES);
     const uint32_t q_full = s_addr(bars), k_full = q_full + 8, k_empty = k_full + 16, v_full = k_empty + 16;
-    const uint32_t v_empty = v_full + 16, s_full = v_empty + 16, s_empty = s_full + 16, p_full = s_empty + 16;
-    const uint32_t o_done = p_full + 8;
+    const uint32_t v_empty = v_full + 16, s_full = v_empty + 16, p_full = s_full + 16, o_done = p_full + 16;
     uint32_t* tslot = (uint32_t*)(bars + 15);
 
     pdl_launch_dependents();
@@ -134,8 +144,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     const int group = a.heads / a.kv_heads;  // 4 (checked on the host)
     const int qdim = a.heads * 128;
     const int ps = a.page_slots;
-    const int max_limit = it.shared + (it.slot0 + it.ntok - 1 - it.segment + 1);
-    const int nb = (max_limit + AT_KEYS - 1) / AT_KEYS;
+    // per tile: tokens, visible keys of its last token, blocks
+    const int ntA = min(it.ntok, 32), ntB = it.ntok - ntA;
+    const int limA = it.shared + (it.slot0 + ntA - 1 - it.segment + 1);
+    const int limB = ntB > 0 ? it.shared + (it.slot0 + it.ntok - 1 - it.segment + 1) : 0;
+    const int nbA = (limA + AT_KEYS - 1) / AT_KEYS, nbB = (limB + AT_KEYS - 1) / AT_KEYS;
+    const int max_limit = max(limA, limB), nb = max(nbA, nbB);
     // keys below `shared` (region A) are slots 0.., the rest (region B) slots segment..
     const int nA = min(it.shared, max_limit), nBk = max_limit - nA;
     const int pagesA = (nA + ps - 1) / ps;
@@ -143,141 +157,149 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     const int pagesB = nBk > 0 ? (it.segment + nBk - 1) / ps - pB0 + 1 : 0;
 
     if (tid == 0) {
-        mbar_init(q_full, 64);
+        mbar_init(q_full, 96);
         for (int i = 0; i < 2; i++) {
             mbar_init(k_full + 8 * i, 32);
             mbar_init(k_empty + 8 * i, 1);
             mbar_init(v_full + 8 * i, 32);
             mbar_init(v_empty + 8 * i, 1);
             mbar_init(s_full + 8 * i, 1);
-            mbar_init(s_empty + 8 * i, 4);
+            mbar_init(p_full + 8 * i, 4);
+            mbar_init(o_done + 8 * i, 1);
         }
-        mbar_init(p_full, 4);
-        mbar_init(o_done, 1);
         fence_barrier_init();
     }
-    if (warp == 6) tmem_alloc(s_addr(tslot), 512);
-    if (warp == 4 || warp == 5) {
+    if (warp == 10) tmem_alloc(s_addr(tslot), 512);
+    if (warp >= 8) {
         // stage the page-table entries of both key regions (the host keeps them <= AT_PAGES)
-        for (int i = tid - 128; i < pagesA + pagesB; i += 64)
+        for (int i = tid - 256; i < pagesA + pagesB; i += 96)
             pg[i] = __ldg(a.page_table + (i < pagesA ? i : pB0 + (i - pagesA)));
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tslot;  // O at columns 0-127, S buffers at 128-255 and 256-383
+    const uint32_t tmem = *tslot;  // O_A 0-127, O_B 128-255, S_A 256-383, S_B 384-511
     int* err = a.err;
 
-    if (warp == 4 || warp == 5) {
-        // ----------------------------------------------------------------- loaders
-        const int lt = tid - 128;
-        // Q: row r = token r / 4 x head r % 4 of this KV head
-        for (int id = lt; id < AT_ROWS * 16; id += 64) {
-            const int r = id >> 4, c = id & 15;
-            const int tl = r / group, j = r % group;
+    if (warp >= 8) {
+        // --------------------------------------------------------- Q, then K / V rings
+        const int lt = tid - 256;
+        // Q row r of tile X = token 32 X + r / 4, head r % 4 of this KV head
+        for (int id = lt; id < 2 * AT_ROWS * 16; id += 96) {
+            const int x = id >> 11, r = (id >> 4) & 127, c = id & 15;
+            const int tl = 32 * x + r / group, j = r % group;
             const bool ok = tl < it.ntok;
             const __half* src = ok ? a.q16 + (int64_t)(it.t0 + tl) * qdim + (it.kv_head * group + j) * 128 + c * 8 : a.q16;
-            cp16(s_addr(Qs) + tile_off(r, c), src, ok ? 16 : 0);
+            cp16(s_addr(Qs + x * AT_TILE) + tile_off(r, c), src, ok ? 16 : 0);
         }
         cp_wait_all();
         fence_proxy_async();
         mbar_arrive(q_full);
-        const int kv = warp - 4;  // 0: K ring, 1: V ring
-        const char* pool = (const char*)a.kv_pool + kv_plane_offset(a.layer, a.kv_heads, it.kv_head, kv, ps);
-        const uint32_t full = kv ? v_full : k_full, empty = kv ? v_empty : k_empty;
-        const uint32_t ring = s_addr(kv ? Vs : Ks);
-        for (int b = 0; b < nb; b++) {
-            const int s = b & 1;
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u);
-            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
-                if (lane == 0) atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
-                break;
-            }
-            const uint32_t tile = ring + (uint32_t)(s * AT_TILE);
-            const int L0 = b * AT_KEYS, nvalid = min(AT_KEYS, max_limit - L0);
-            // runs of consecutive slots inside one page: region A, then region B
-#pragma unroll 1
-            for (int reg = 0; reg < 2; reg++) {
-                int La = reg == 0 ? L0 : max(L0, nA);
-                const int Lb = reg == 0 ? min(L0 + nvalid, nA) : L0 + nvalid;
-                while (La < Lb) {
-                    const int slot = reg == 0 ? La : it.segment + (La - nA);
-                    const int row = slot % ps;
-                    const int n = min(Lb - La, ps - row);
-                    const int page = reg == 0 ? pg[slot / ps] : pg[pagesA + slot / ps - pB0];
-                    const char* plane = pool + (int64_t)page * a.page_bytes;
-                    const int key0 = La - L0;
-                    if (((key0 - row) & 7) == 0) {
-                        if (lane == 0) {
-                            mbar_add_tx(full + 8 * s, (uint32_t)(2 * n * 128));
-                            bulk_g2s(tile + (uint32_t)(key0 * 128), plane + row * 128, (uint32_t)(n * 128), full + 8 * s);
-                            bulk_g2s(tile + 16384u + (uint32_t)(key0 * 128), plane + ps * 128 + row * 128,
-                                     (uint32_t)(n * 128), full + 8 * s);
-                        }
-                    } else {
-                        for (int i = lane; i < n * 16; i += 32) {
-                            const int r = i >> 4, c = i & 15;
-                            cp16(tile + tile_off(key0 + r, c), plane + kv_chunk_offset(row + r, c, ps), 16);
-                        }
-                    }
-                    La += n;
+        if (warp == 8 || warp == 9) {
+            const int kv = warp - 8;  // 0: K ring, 1: V ring
+            const char* pool = (const char*)a.kv_pool + kv_plane_offset(a.layer, a.kv_heads, it.kv_head, kv, ps);
+            const uint32_t full = kv ? v_full : k_full, empty = kv ? v_empty : k_empty;
+            const uint32_t ring = s_addr(kv ? Vs : Ks);
+            for (int b = 0; b < nb; b++) {
+                const int s = b & 1;
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u);
+                if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+                    if (lane == 0) atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+                    break;
                 }
-            }
-            // rows past the last visible key: zeros, so 0-probability keys add exact zeros
-            for (int i = lane; i < (AT_KEYS - nvalid) * 16; i += 32) {
-                const int r = nvalid + (i >> 4), c = i & 15;
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(tile + tile_off(r, c)), "r"(0u) : "memory");
+                const uint32_t tile = ring + (uint32_t)(s * AT_TILE);
+                const int L0 = b * AT_KEYS, nvalid = min(AT_KEYS, max_limit - L0);
+                // runs of consecutive slots inside one page: region A, then region B
+#pragma unroll 1
+                for (int reg = 0; reg < 2; reg++) {
+                    int La = reg == 0 ? L0 : max(L0, nA);
+                    const int Lb = reg == 0 ? min(L0 + nvalid, nA) : L0 + nvalid;
+                    while (La < Lb) {
+                        const int slot = reg == 0 ? La : it.segment + (La - nA);
+                        const int row = slot % ps;
+                        const int n = min(Lb - La, ps - row);
+                        const int page = reg == 0 ? pg[slot / ps] : pg[pagesA + slot / ps - pB0];
+                        const char* plane = pool + (int64_t)page * a.page_bytes;
+                        const int key0 = La - L0;
+                        if (((key0 - row) & 7) == 0) {
+                            if (lane == 0) {
+                                mbar_add_tx(full + 8 * s, (uint32_t)(2 * n * 128));
+                                bulk_g2s(tile + (uint32_t)(key0 * 128), plane + row * 128, (uint32_t)(n * 128), full + 8 * s);
+                                bulk_g2s(tile + 16384u + (uint32_t)(key0 * 128), plane + ps * 128 + row * 128,
+                                         (uint32_t)(n * 128), full + 8 * s);
+                            }
+                        } else {
+                            for (int i = lane; i < n * 16; i += 32) {
+                                const int r = i >> 4, c = i & 15;
+                                cp16(tile + tile_off(key0 + r, c), plane + kv_chunk_offset(row + r, c, ps), 16);
+                            }
+                        }
+                        La += n;
+                    }
+                }
+                // rows past the last visible key: zeros, so 0-probability keys add exact zeros
+                for (int i = lane; i < (AT_KEYS - nvalid) * 16; i += 32) {
+                    const int r = nvalid + (i >> 4), c = i & 15;
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};\n" ::"r"(tile + tile_off(r, c)), "r"(0u) : "memory");
+                }
+                cp_wait_all();
+                fence_proxy_async();
+                mbar_arrive(full + 8 * s);
             }
             cp_wait_all();
-            fence_proxy_async();
-            mbar_arrive(full + 8 * s);
-        }
-        cp_wait_all();
-    } else if (warp == 6) {
-        if (lane == 0) {  // ------------------------------------------------------- MMA
+        } else if (warp == 10 && lane == 0) {
+            // ------------------------------------------------------------------- MMA
             const uint32_t id_s = idesc_f16(AT_KEYS, AT_ROWS);
             const uint32_t id_pv = idesc_f16(128, AT_ROWS) | (1u << 16);  // B (V) MN-major
             bool ok = mbar_wait(q_full, 0);
             tc_fence_after();
-            int ns = 0, np = 0;  // next S to issue, next P V to issue
+            int ns[2] = {0, 0}, np[2] = {0, 0};  // per tile: next S, next P V
+            const int nbx[2] = {nbA, nbB};
             uint64_t idle_since = gtimer();
-            while (ok && np < nb) {
+            while (ok && (np[0] < nbA || np[1] < nbB)) {
                 bool did = false;
-                if (np < ns && mbar_test(p_full, (uint32_t)(np & 1)) &&
-                    mbar_test(v_full + 8 * (np & 1), (uint32_t)((np >> 1) & 1))) {
-                    tc_fence_after();
-                    const int s = np & 1;
-                    const uint32_t p = s_addr(Ps), v = s_addr(Vs + s * AT_TILE);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                        umma(tmem, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (np > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    umma_commit(v_empty + 8 * s);
-                    umma_commit(o_done);  // last: its arrival implies the stage release before it
-                    np++;
-                    did = true;
-                } else if (ns < nb && mbar_test(k_full + 8 * (ns & 1), (uint32_t)((ns >> 1) & 1)) &&
-                           mbar_test(s_empty + 8 * (ns & 1), (uint32_t)((ns >> 1) & 1) ^ 1u)) {
-                    tc_fence_after();
-                    const int s = ns & 1;
-                    const uint32_t q = s_addr(Qs), k = s_addr(Ks + s * AT_TILE);
-                    const uint32_t d = tmem + 128u + (uint32_t)(s * 128);
+                for (int x = 0; x < 2 && !did; x++) {
+                    const int b = np[x];
+                    if (b < ns[x] && mbar_test(p_full + 8 * x, (uint32_t)(b & 1)) &&
+                        mbar_test(v_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) {
+                        tc_fence_after();
+                        const uint32_t v = s_addr(Vs + (b & 1) * AT_TILE);
+                        const uint32_t o = tmem + (uint32_t)(x * 128), pt = tmem + 256u + (uint32_t)(x * 128);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                        umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
+                        for (int kk = 0; kk < 8; kk++)
+                            umma_ts(o, pt + (uint32_t)(kk * 8), sdesc_mn(v + kk * 2048), id_pv, (b > 0 || kk > 0) ? 1u : 0u);
+                        // the V stage is free once every tile that uses block b is past it
+                        if (b >= nbx[x ^ 1] || np[x ^ 1] > b) umma_commit(v_empty + 8 * (b & 1));
+                        umma_commit(o_done + 8 * x);
+                        np[x] = b + 1;
+                        did = true;
                     }
-                    umma_commit(k_empty + 8 * s);
-                    umma_commit(s_full + 8 * s);
-                    ns++;
-                    did = true;
+                }
+#pragma unroll
+                for (int x = 0; x < 2 && !did; x++) {
+                    const int b = ns[x];
+                    // S_X(b) overwrites P_X(b - 1): only behind P V_X(b - 1)
+                    if (b < nbx[x] && np[x] == b && mbar_test(k_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) {
+                        tc_fence_after();
+                        const uint32_t q = s_addr(Qs + x * AT_TILE), k = s_addr(Ks + (b & 1) * AT_TILE);
+                        const uint32_t d = tmem + 256u + (uint32_t)(x * 128);
+#pragma unroll
+                        for (int kk = 0; kk < 8; kk++) {
+                            const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                            umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
+                        }
+                        if (b >= nbx[x ^ 1] || ns[x ^ 1] > b) umma_commit(k_empty + 8 * (b & 1));
+                        umma_commit(s_full + 8 * x);
+                        ns[x] = b + 1;
+                        did = true;
+                    }
                 }
                 if (did) {
                     idle_since = gtimer();
                 } else {
-                    __nanosleep(32);
+                    __nanosleep(20);
                     if (gtimer() - idle_since > WAIT_NS) ok = false;
                 }
             }
@@ -285,36 +307,39 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
         }
     } else {
         // --------------------------------------------------- softmax and the output
-        const int r = tid;  // query row = TMEM lane
-        const int tl = r / group, j = r % group;
+        const int x = warp >> 2;  // tile
+        const int r = tid & 127;  // query row = TMEM lane
+        const int tl = 32 * x + r / group, j = r % group;
+        const int nbt = x ? nbB : nbA;
         const int lim = tl < it.ntok ? it.shared + (it.slot0 + tl - it.segment + 1) : 1;
         const float sl2 = a.scale * AT_LOG2E;
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        float m = -INFINITY, l = 0.f;  // running maximum (log2 units) and sum
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t o_col = tmem + lane_base + (uint32_t)(x * 128);
+        const uint32_t s_col = tmem + lane_base + 256u + (uint32_t)(x * 128);
+        // m: the row's reference maximum (log2 units). It moves only when the block maximum
+        // exceeds it by more than 8, so probabilities stay below 2^8 (fine in fp16) and O is
+        // rescaled rarely; the sequence of m depends on the row's own scores in logical block
+        // order only, so the bit-identity across tree / alone / cached holds.
+        float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int b = 0; b < nb; b++) {
-            const int s = b & 1;
-            if (!warp_wait(s_full + 8 * s, (uint32_t)((b >> 1) & 1))) { ok = false; break; }
+        for (int b = 0; b < nbt; b++) {
+            if (!warp_wait(s_full + 8 * x, (uint32_t)(b & 1))) { ok = false; break; }
             tc_fence_after();
             uint32_t v[128];
             {
-                const uint32_t sb = tmem + lane_base + 128u + (uint32_t)(s * 128);
                 uint32_t(&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[0]);
                 uint32_t(&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[32]);
                 uint32_t(&v2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[64]);
                 uint32_t(&v3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[96]);
-                tld32(sb, v0);
-                tld32(sb + 32u, v1);
-                tld32(sb + 64u, v2);
-                tld32(sb + 96u, v3);
+                tld32(s_col, v0);
+                tld32(s_col + 32u, v1);
+                tld32(s_col + 64u, v2);
+                tld32(s_col + 96u, v3);
                 tld_wait(v0);
                 tld_wait(v1);
                 tld_wait(v2);
                 tld_wait(v3);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_empty + 8 * s);  // S buffer s may take block b + 2
             // keys at or past the row's limit are invisible
             const int vis = lim - b * AT_KEYS;
             if (vis < AT_KEYS) {
@@ -324,75 +349,80 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             }
             float bm = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < 128; e++) bm = fmaxf(bm, __uint_as_float(v[e]));
-            const float mn = fmaxf(m, bm * sl2);  // finite: key 0 is visible to every row
-            const float alpha = ex2(m - mn);      // 0 on the first block, where O is overwritten
+            for (int e = 0; e < 128; e += 2) bm = fmaxf(bm, fmaxf(__uint_as_float(v[e]), __uint_as_float(v[e + 1])));
+            bm *= sl2;                                  // finite: key 0 is visible to every row
+            const bool move = bm > m + 8.f;             // always on the first block (m = -inf)
+            const float mn = move ? bm : m;
+            const float alpha = move ? ex2(m - mn) : 1.f;  // 0 on the first block, where O is overwritten
+            // probabilities as fp16 pairs (keys 2c, 2c + 1 in column c), packed in place, and their sum
             float rs = 0.f;
-            uint32_t pk[64];
 #pragma unroll
             for (int e = 0; e < 128; e += 2) {
                 const float p0 = ex2(fmaf(__uint_as_float(v[e]), sl2, -mn));
                 const float p1 = ex2(fmaf(__uint_as_float(v[e + 1]), sl2, -mn));
                 rs += p0 + p1;
                 __half2 hp = __floats2half2_rn(p0, p1);
-                pk[e >> 1] = *reinterpret_cast<uint32_t*>(&hp);
+                v[e >> 1] = *reinterpret_cast<uint32_t*>(&hp);
             }
+            tst32(s_col, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+            tst32(s_col + 32u, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
             l = l * alpha + rs;
             m = mn;
-            // P may be overwritten and O rescaled once the previous block's P V has finished
-            if (b > 0) {
-                if (!warp_wait(o_done, (uint32_t)((b - 1) & 1))) { ok = false; break; }
-                tc_fence_after();
-            }
-#pragma unroll
-            for (int c = 0; c < 16; c++)
-                *(uint4*)(Ps + tile_off(r, c)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-            // O *= alpha where the maximum moved (an exact no-op where alpha is 1)
+            // O *= alpha for rows whose maximum moved. P V_X(b - 1) has finished: S_X(b), issued
+            // behind it, has.
             if (b > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-                for (int h = 0; h < 4; h++) {
-                    uint32_t o[32];
-                    tld32(tmem + lane_base + (uint32_t)(h * 32), o);
-                    tld_wait(o);
+#pragma unroll 1
+                for (int h = 0; h < 2; h++) {
+                    uint32_t o0[32], o1[32];
+                    tld32(o_col + (uint32_t)(h * 64), o0);
+                    tld32(o_col + (uint32_t)(h * 64 + 32), o1);
+                    tld_wait(o0);
+                    tld_wait(o1);
 #pragma unroll
-                    for (int e = 0; e < 32; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                    tst32(tmem + lane_base + (uint32_t)(h * 32), o);
+                    for (int e = 0; e < 32; e++) {
+                        o0[e] = __float_as_uint(__uint_as_float(o0[e]) * alpha);
+                        o1[e] = __float_as_uint(__uint_as_float(o1[e]) * alpha);
+                    }
+                    tst32(o_col + (uint32_t)(h * 64), o0);
+                    tst32(o_col + (uint32_t)(h * 64 + 32), o1);
                 }
-                tst_wait();
             }
-            fence_proxy_async();  // P stores -> visible to the tensor core
+            tst_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(p_full + 8 * x);
         }
-        if (ok && !warp_wait(o_done, (uint32_t)((nb - 1) & 1))) ok = false;
-        if (!ok) {
-            atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
-        } else {
-            tc_fence_after();
-            const float inv = 1.f / l;
-            const int t = it.t0 + tl, head = it.kv_head * group + j;
-            for (int h = 0; h < 4; h++) {
-                uint32_t o[32];
-                tld32(tmem + lane_base + (uint32_t)(h * 32), o);
-                tld_wait(o);
-                if (tl < it.ntok) {
+        if (nbt > 0) {
+            if (ok && !warp_wait(o_done + 8 * x, (uint32_t)((nbt - 1) & 1))) ok = false;
+            if (!ok) {
+                atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+            } else {
+                tc_fence_after();
+                const float inv = 1.f / l;
+                const int t = it.t0 + tl, head = it.kv_head * group + j;
+                for (int h = 0; h < 4; h++) {
+                    uint32_t o[32];
+                    tld32(o_col + (uint32_t)(h * 32), o);
+                    tld_wait(o);
+                    if (tl < it.ntok) {
 #pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        const int col = head * 128 + h * 32 + c * 8;
-                        float f[8];
+                        for (int c = 0; c < 4; c++) {
+                            const int col = head * 128 + h * 32 + c * 8;
+                            float f[8];
 #pragma unroll
-                        for (int e = 0; e < 8; e++) f[e] = __uint_as_float(o[8 * c + e]) * inv;
-                        if (a.ctx16) {
-                            __half2 q0 = __floats2half2_rn(f[0], f[1]), q1 = __floats2half2_rn(f[2], f[3]);
-                            __half2 q2 = __floats2half2_rn(f[4], f[5]), q3 = __floats2half2_rn(f[6], f[7]);
-                            *(uint4*)(a.ctx16 + kslab_offset(t, col, a.tpad)) =
-                                make_uint4(*reinterpret_cast<uint32_t*>(&q0), *reinterpret_cast<uint32_t*>(&q1),
-                                           *reinterpret_cast<uint32_t*>(&q2), *reinterpret_cast<uint32_t*>(&q3));
-                        }
-                        if (a.ctx32) {
-                            float* dst = a.ctx32 + (int64_t)t * qdim + col;
-                            *(float4*)dst = make_float4(f[0], f[1], f[2], f[3]);
-                            *(float4*)(dst + 4) = make_float4(f[4], f[5], f[6], f[7]);
+                            for (int e = 0; e < 8; e++) f[e] = __uint_as_float(o[8 * c + e]) * inv;
+                            if (a.ctx16) {
+                                __half2 q0 = __floats2half2_rn(f[0], f[1]), q1 = __floats2half2_rn(f[2], f[3]);
+                                __half2 q2 = __floats2half2_rn(f[4], f[5]), q3 = __floats2half2_rn(f[6], f[7]);
+                                *(uint4*)(a.ctx16 + kslab_offset(t, col, a.tpad)) =
+                                    make_uint4(*reinterpret_cast<uint32_t*>(&q0), *reinterpret_cast<uint32_t*>(&q1),
+                                               *reinterpret_cast<uint32_t*>(&q2), *reinterpret_cast<uint32_t*>(&q3));
+                            }
+                            if (a.ctx32) {
+                                float* dst = a.ctx32 + (int64_t)t * qdim + col;
+                                *(float4*)dst = make_float4(f[0], f[1], f[2], f[3]);
+                                *(float4*)(dst + 4) = make_float4(f[4], f[5], f[6], f[7]);
+                            }
                         }
                     }
                 }
@@ -401,7 +431,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 6) {
+    if (warp == 10) {
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
@@ -412,7 +442,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
 constexpr size_t AT_SMEM = (size_t)6 * AT_TILE + AT_PAGES * 4 + 128 + 1024;
 
 // Page-table entries the item with the most visible keys needs: both key regions rounded out to
-// whole pages. Items are runs of at most ATT_ITEM_TOKENS consecutive slots.
+// whole pages.
 bool attention_tc_fits(int max_keys, int page_slots) { return max_keys / page_slots + 3 <= AT_PAGES; }
 
 void launch_attention_tc(const AttnArgs& a, cudaStream_t s) {

@@ -877,12 +877,17 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
 
     // Attention work items: runs of consecutive tokens that share (shared, segment) and have
     // consecutive slots, cut into ATT_ITEM_TOKENS-token tiles, one per KV head; longest first.
+    // The tensor-core kernel takes two 32-token tiles per item (they share every K/V block).
+    int pass_keys = 0;
+    for (int t = 0; t < T; t++) pass_keys = std::max(pass_keys, L->shared[t] + (L->slot[t] - L->seg[t] + 1));
+    const bool attn_tc = !attention_on_mma_sync() && attention_tc_fits(pass_keys + 64, m->page_slots);
+    const int item_tokens = attn_tc ? 2 * ATT_ITEM_TOKENS : ATT_ITEM_TOKENS;
     std::vector<AttnItem> items;
     if (!decode) {
         int t = 0;
         while (t < T) {
             int n = 1;
-            while (n < ATT_ITEM_TOKENS && t + n < T && L->shared[t + n] == L->shared[t] && L->seg[t + n] == L->seg[t] &&
+            while (n < item_tokens && t + n < T && L->shared[t + n] == L->shared[t] && L->seg[t + n] == L->seg[t] &&
                    L->slot[t + n] == L->slot[t] + n)
                 n++;
             int lim = L->shared[t] + (L->slot[t] + n - 1 - L->seg[t] + 1);
@@ -1077,10 +1082,10 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         aa.err = x->d_err;
         {
             ProfScope ps(x, JV_PROF_ATTENTION, attn_flops, attn_bytes);
-            if (attention_on_mma_sync() || !attention_tc_fits(max_item_keys, m->page_slots))
-                launch_attention(aa, s);
-            else
+            if (attn_tc)
                 launch_attention_tc(aa, s);
+            else
+                launch_attention(aa, s);
         }
         if (capture) observe(x, p + "attn_weighted", aa.ctx32, T, qdim);
         if (capture) {
