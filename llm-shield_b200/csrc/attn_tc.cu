@@ -10,20 +10,21 @@
 // (tokens 0-31) and B (32-63); in a tile the 4 query heads of the KV head ride in M (128 rows =
 // TMEM lanes). Both tiles share every K/V block. Per tile and block of 128 keys:
 //   S  = Q K^T      tcgen05.mma kind::f16, M = 128, N = 128 keys, K = 128 dims -> TMEM (fp32)
-//   P  = exp2(S * scale * log2 e - m)   one query row per softmax thread, online max/sum, O
-//                                        rescaled in TMEM when the row maximum moves; P is
-//                                        written back as fp16 pairs over the tile's own S columns
-//   O += P V        A = P straight from TMEM, B = V through an MN-major SWIZZLE_128B descriptor
-// TMEM: O_A, O_B, S_A (P_A), S_B (P_B), 128 columns each. Warps 0-3 run tile A's softmax, warps
-// 4-7 tile B's, so the two tiles' exponentials interleave on each scheduler while the tensor
-// core works on the other tile. Warp 8 fills a 2-deep K ring and warp 9 a 2-deep V ring: KV
+//   P  = exp2(S * scale * log2 e - m)   one query row per softmax thread, online max/sum; the
+//                                        reference maximum m moves only when a block exceeds it
+//                                        by more than 2^8, and O is rescaled in TMEM then
+//   O += P V        P from shared memory (K-major), V through an MN-major SWIZZLE_128B descriptor
+// TMEM: O_A, O_B, S_A, S_B, 128 columns each. Warps 0-3 run tile A's softmax, warps 4-7 tile B's;
+// a softmax hands its S columns back as soon as it has read them, so the next block's Q K^T runs
+// while it computes the exponentials. The tiles take the single P buffer in turn (A(0), B(0),
+// A(1), B(1), ..., then B alone). Warp 8 fills a 2-deep K ring and warp 9 a 2-deep V ring: KV
 // pages store their rows in the operand swizzle (kv_chunk_offset), so each run of consecutive
 // slots inside one page is two bulk copies (one per 64-dim half); a run whose first row sits at
 // a different position modulo 8 in the page than in the tile (a branch segment starting off a
 // multiple of 8) goes chunk by chunk through cp.async instead. Warp 10 owns TMEM and issues the
-// MMAs from an event loop: P V_X(b) as soon as P_X(b) and V(b) are in place, then S_X(b + 1)
-// behind it (it overwrites P_X(b); tcgen05.mma from one thread run in issue order). Every wait
-// is bounded (2 s of %globaltimer); on expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
+// MMAs from an event loop: the next P V as soon as its P and V are in place, S_X(b) as soon as
+// K(b) is and the softmax has read S_X(b - 1). Every wait is bounded (2 s of %globaltimer); on
+// expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
 #include "tc_common.cuh"
 
 namespace jv {
@@ -33,7 +34,7 @@ constexpr int AT_ROWS = 128;                 // 32 tokens x 4 query heads per ti
 constexpr int AT_KEYS = 128;                 // keys per block
 constexpr int AT_THREADS = 352;              // 11 warps
 constexpr int AT_TILE = 128 * 128 * 2;       // one [128][128] fp16 tile, two 16 KB halves
-constexpr int AT_PAGES = 1024;               // page-table entries staged in shared memory
+constexpr int AT_PAGES = 448;                // page-table entries staged in shared memory
 constexpr float AT_LOG2E = 1.4426950408889634f;
 
 // Byte offset of 16-byte chunk c (0..15) of row r in a [128][128] fp16 tile stored as two
@@ -116,26 +117,19 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// D (TMEM) (+)= A (TMEM, 16-bit elements two to a column) x B (shared memory descriptor).
-__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bd, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
-            tmem_d),
-        "r"(tmem_a), "l"(bd), "r"(idesc), "r"(acc)
-        : "memory");
-}
-
 __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     extern __shared__ uint8_t at_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)at_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* Qs = sm;                       // 2 tiles of [128 rows][128 dims]
     uint8_t* Ks = sm + 2 * AT_TILE;         // 2 stages of [128 keys][128 dims]
     uint8_t* Vs = sm + 4 * AT_TILE;         // 2 stages of [128 keys][128 dims]
-    int32_t* pg = (int32_t*)(sm + 6 * AT_TILE);  // physical pages of the item's keys
+    uint8_t* Ps = sm + 6 * AT_TILE;         // [128 rows][128 keys]: one tile's P at a time
+    int32_t* pg = (int32_t*)(sm + 7 * AT_TILE);  // physical pages of the item's keys
     uint64_t* bars = (uint64_t*)(pg + AT_PAGES);
     const uint32_t q_full = s_addr(bars), k_full = q_full + 8, k_empty = k_full + 16, v_full = k_empty + 16;
-    const uint32_t v_empty = v_full + 16, s_full = v_empty + 16, p_full = s_full + 16, o_done = p_full + 16;
-    uint32_t* tslot = (uint32_t*)(bars + 15);
+    const uint32_t v_empty = v_full + 16, s_full = v_empty + 16, s_free = s_full + 16, p_full = s_free + 16;
+    const uint32_t o_done = p_full + 8;
+    uint32_t* tslot = (uint32_t*)(bars + 16);
 
     pdl_launch_dependents();
     pdl_wait();
@@ -155,6 +149,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     const int pagesA = (nA + ps - 1) / ps;
     const int pB0 = nBk > 0 ? it.segment / ps : 0;
     const int pagesB = nBk > 0 ? (it.segment + nBk - 1) / ps - pB0 + 1 : 0;
+    const bool staged = pagesA + pagesB <= AT_PAGES;  // else the loaders read the page table
 
     if (tid == 0) {
         mbar_init(q_full, 96);
@@ -164,14 +159,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             mbar_init(v_full + 8 * i, 32);
             mbar_init(v_empty + 8 * i, 1);
             mbar_init(s_full + 8 * i, 1);
-            mbar_init(p_full + 8 * i, 4);
+            mbar_init(s_free + 8 * i, 4);
             mbar_init(o_done + 8 * i, 1);
         }
+        mbar_init(p_full, 4);
         fence_barrier_init();
     }
     if (warp == 10) tmem_alloc(s_addr(tslot), 512);
-    if (warp >= 8) {
-        // stage the page-table entries of both key regions (the host keeps them <= AT_PAGES)
+    if (warp >= 8 && staged) {
+        // stage the page-table entries of both key regions
         for (int i = tid - 256; i < pagesA + pagesB; i += 96)
             pg[i] = __ldg(a.page_table + (i < pagesA ? i : pB0 + (i - pagesA)));
     }
@@ -219,7 +215,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                         const int slot = reg == 0 ? La : it.segment + (La - nA);
                         const int row = slot % ps;
                         const int n = min(Lb - La, ps - row);
-                        const int page = reg == 0 ? pg[slot / ps] : pg[pagesA + slot / ps - pB0];
+                        const int page = !staged ? __ldg(a.page_table + slot / ps)
+                                         : reg == 0 ? pg[slot / ps] : pg[pagesA + slot / ps - pB0];
                         const char* plane = pool + (int64_t)page * a.page_bytes;
                         const int key0 = La - L0;
                         if (((key0 - row) & 7) == 0) {
@@ -254,34 +251,41 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             const uint32_t id_pv = idesc_f16(128, AT_ROWS) | (1u << 16);  // B (V) MN-major
             bool ok = mbar_wait(q_full, 0);
             tc_fence_after();
-            int ns[2] = {0, 0}, np[2] = {0, 0};  // per tile: next S, next P V
+            // P V follows the order the tiles take the P buffer in: A(0), B(0), A(1), B(1), ...,
+            // then B alone for the blocks past tile A's last (tile A never sees more keys than B).
+            int ns[2] = {0, 0};  // per tile: next S
             const int nbx[2] = {nbA, nbB};
+            const int nuses = nbA + nbB;
+            int u = 0;  // next P V
             uint64_t idle_since = gtimer();
-            while (ok && (np[0] < nbA || np[1] < nbB)) {
+            while (ok && u < nuses) {
                 bool did = false;
-#pragma unroll
-                for (int x = 0; x < 2 && !did; x++) {
-                    const int b = np[x];
-                    if (b < ns[x] && mbar_test(p_full + 8 * x, (uint32_t)(b & 1)) &&
+                {
+                    const int x = (nbB == 0 || u >= 2 * nbA) ? (nbB == 0 ? 0 : 1) : (u & 1);
+                    const int b = nbB == 0 ? u : u < 2 * nbA ? (u >> 1) : u - nbA;
+                    if (ns[x] > b && mbar_test(p_full, (uint32_t)(u & 1)) &&
                         mbar_test(v_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) {
                         tc_fence_after();
-                        const uint32_t v = s_addr(Vs + (b & 1) * AT_TILE);
-                        const uint32_t o = tmem + (uint32_t)(x * 128), pt = tmem + 256u + (uint32_t)(x * 128);
+                        const uint32_t p = s_addr(Ps), v = s_addr(Vs + (b & 1) * AT_TILE);
+                        const uint32_t o = tmem + (uint32_t)(x * 128);
 #pragma unroll
-                        for (int kk = 0; kk < 8; kk++)
-                            umma_ts(o, pt + (uint32_t)(kk * 8), sdesc_mn(v + kk * 2048), id_pv, (b > 0 || kk > 0) ? 1u : 0u);
-                        // the V stage is free once every tile that uses block b is past it
-                        if (b >= nbx[x ^ 1] || np[x ^ 1] > b) umma_commit(v_empty + 8 * (b & 1));
-                        umma_commit(o_done + 8 * x);
-                        np[x] = b + 1;
+                        for (int kk = 0; kk < 8; kk++) {
+                            const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                            umma(o, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (b > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        // tile B's P V is the last use of V(b) wherever B takes the block
+                        if (x == 1 || nbB == 0) umma_commit(v_empty + 8 * (b & 1));
+                        umma_commit(o_done + 8 * x);  // last: its arrival implies the release before it
+                        u++;
                         did = true;
                     }
                 }
 #pragma unroll
-                for (int x = 0; x < 2 && !did; x++) {
+                for (int x = 0; x < 2; x++) {
                     const int b = ns[x];
-                    // S_X(b) overwrites P_X(b - 1): only behind P V_X(b - 1)
-                    if (b < nbx[x] && np[x] == b && mbar_test(k_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) {
+                    // S_X(b) overwrites S_X(b - 1): only once the softmax has read that
+                    if (!did && b < nbx[x] && mbar_test(k_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1)) &&
+                        (b == 0 || mbar_test(s_free + 8 * x, (uint32_t)((b - 1) & 1)))) {
                         tc_fence_after();
                         const uint32_t q = s_addr(Qs + x * AT_TILE), k = s_addr(Ks + (b & 1) * AT_TILE);
                         const uint32_t d = tmem + 256u + (uint32_t)(x * 128);
@@ -340,6 +344,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 tld_wait(v2);
                 tld_wait(v3);
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free + 8 * x);  // S_X(b + 1) may overwrite S_X(b)
             // keys at or past the row's limit are invisible
             const int vis = lim - b * AT_KEYS;
             if (vis < AT_KEYS) {
@@ -364,12 +371,30 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 __half2 hp = __floats2half2_rn(p0, p1);
                 v[e >> 1] = *reinterpret_cast<uint32_t*>(&hp);
             }
-            tst32(s_col, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-            tst32(s_col + 32u, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
             l = l * alpha + rs;
             m = mn;
-            // O *= alpha for rows whose maximum moved. P V_X(b - 1) has finished: S_X(b), issued
-            // behind it, has.
+            // The P buffer is free once the P V of its previous user has finished: tile B's block
+            // b - 1 for A(b) (A's own for a lone tile), tile A's block b for B(b) while A takes
+            // blocks, else B's own block b - 1. That P V completing implies every earlier one has,
+            // P V_X(b - 1) included, so O_X may be rescaled too. Each of these barriers is at
+            // most one phase behind the one awaited (this warp's previous wait covered the one
+            // before it), so the parity test is exact.
+            {
+                int wt = -1, wb = 0;
+                if (x == 0) {
+                    if (b > 0) { wt = nbB > 0 ? 1 : 0; wb = b - 1; }
+                } else if (b < nbA) {
+                    wt = 0; wb = b;
+                } else if (b > 0) {
+                    wt = 1; wb = b - 1;
+                }
+                if (wt >= 0 && !warp_wait(o_done + 8 * wt, (uint32_t)(wb & 1))) { ok = false; break; }
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 16; c++)
+                *(uint4*)(Ps + tile_off(r, c)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+            // O *= alpha for rows whose maximum moved
             if (b > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
                 for (int h = 0; h < 2; h++) {
@@ -388,9 +413,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 }
             }
             tst_wait();
+            fence_proxy_async();  // P stores -> visible to the tensor core
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full + 8 * x);
+            if (lane == 0) mbar_arrive(p_full);
         }
         if (nbt > 0) {
             if (ok && !warp_wait(o_done + 8 * x, (uint32_t)((nbt - 1) & 1))) ok = false;
@@ -439,18 +465,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
 
 }  // namespace
 
-constexpr size_t AT_SMEM = (size_t)6 * AT_TILE + AT_PAGES * 4 + 128 + 1024;
+constexpr size_t AT_SMEM = (size_t)7 * AT_TILE + AT_PAGES * 4 + 160 + 1024;
 
-// Page-table entries the item with the most visible keys needs: both key regions rounded out to
-// whole pages.
-bool attention_tc_fits(int max_keys, int page_slots) { return max_keys / page_slots + 3 <= AT_PAGES; }
+// Any pass: the page table is staged in shared memory when it fits, else read by the loaders.
+bool attention_tc_fits(int, int) { return true; }
 
 void launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
     if (a.n_items <= 0) return;
     if (a.page_slots % 8 != 0 || a.page_slots > 256) throw Error(JV_ERR_UNSUPPORTED, "attention: page slots");
     if (a.heads != 4 * a.kv_heads) throw Error(JV_ERR_UNSUPPORTED, "attention: 4 query heads per KV head expected");
-    if (!attention_tc_fits(a.max_keys, a.page_slots))
-        throw Error(JV_ERR_UNSUPPORTED, "attention: too many visible keys for the tensor-core kernel");
     static bool configured = false;
     if (!configured) {
         JV_CUDA(cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT_SMEM));
