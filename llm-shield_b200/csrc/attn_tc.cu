@@ -131,8 +131,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     const uint32_t o_done = p_full + 8;
     uint32_t* tslot = (uint32_t*)(bars + 16);
 
+    // Items and the page table were uploaded before the pass: set-up reads them before waiting
+    // for the previous kernel, which wrote Q and this pass's K/V.
     pdl_launch_dependents();
-    pdl_wait();
     const AttnItem it = a.items[blockIdx.x];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int group = a.heads / a.kv_heads;  // 4 (checked on the host)
@@ -176,21 +177,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     tc_fence_after();
     const uint32_t tmem = *tslot;  // O_A 0-127, O_B 128-255, S_A 256-383, S_B 384-511
     int* err = a.err;
+    pdl_wait();
 
     if (warp >= 8) {
-        // --------------------------------------------------------- Q, then K / V rings
+        // ------------------------------------------------- K / V rings, and Q alongside
         const int lt = tid - 256;
-        // Q row r of tile X = token 32 X + r / 4, head r % 4 of this KV head
-        for (int id = lt; id < 2 * AT_ROWS * 16; id += 96) {
-            const int x = id >> 11, r = (id >> 4) & 127, c = id & 15;
-            const int tl = 32 * x + r / group, j = r % group;
-            const bool ok = tl < it.ntok;
-            const __half* src = ok ? a.q16 + (int64_t)(it.t0 + tl) * qdim + (it.kv_head * group + j) * 128 + c * 8 : a.q16;
-            cp16(s_addr(Qs + x * AT_TILE) + tile_off(r, c), src, ok ? 16 : 0);
-        }
-        cp_wait_all();
-        fence_proxy_async();
-        mbar_arrive(q_full);
+        // Q row r of tile X = token 32 X + r / 4, head r % 4 of this KV head; warps 8 and 9 join
+        // in once their first K / V block is on its way
+        auto load_q = [&]() {
+            for (int id = lt; id < 2 * AT_ROWS * 16; id += 96) {
+                const int x = id >> 11, r = (id >> 4) & 127, c = id & 15;
+                const int tl = 32 * x + r / group, j = r % group;
+                const bool ok = tl < it.ntok;
+                const __half* src = ok ? a.q16 + (int64_t)(it.t0 + tl) * qdim + (it.kv_head * group + j) * 128 + c * 8 : a.q16;
+                cp16(s_addr(Qs + x * AT_TILE) + tile_off(r, c), src, ok ? 16 : 0);
+            }
+            cp_wait_all();
+            fence_proxy_async();
+            mbar_arrive(q_full);
+        };
+        if (warp == 10) load_q();
         if (warp == 8 || warp == 9) {
             const int kv = warp - 8;  // 0: K ring, 1: V ring
             const char* pool = (const char*)a.kv_pool + kv_plane_offset(a.layer, a.kv_heads, it.kv_head, kv, ps);
@@ -198,6 +204,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             const uint32_t ring = s_addr(kv ? Vs : Ks);
             for (int b = 0; b < nb; b++) {
                 const int s = b & 1;
+                if (b == 1) load_q();
                 bool ok = true;
                 if (lane == 0) ok = mbar_wait(empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u);
                 if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
@@ -244,6 +251,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 fence_proxy_async();
                 mbar_arrive(full + 8 * s);
             }
+            if (nb < 2) load_q();
             cp_wait_all();
         } else if (warp == 10 && lane == 0) {
             // ------------------------------------------------------------------- MMA
