@@ -119,7 +119,9 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 
 __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     extern __shared__ uint8_t at_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)at_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-aligned for the SWIZZLE_128B tiles; pointer arithmetic on the shared array keeps the
+    // pointer in the shared state space (plain ld/st.shared rather than generic accesses)
+    uint8_t* sm = at_raw + ((1024u - (s_addr(at_raw) & 1023u)) & 1023u);
     uint8_t* Qs = sm;                       // 2 tiles of [128 rows][128 dims]
     uint8_t* Ks = sm + 2 * AT_TILE;         // 2 stages of [128 keys][128 dims]
     uint8_t* Vs = sm + 4 * AT_TILE;         // 2 stages of [128 keys][128 dims]

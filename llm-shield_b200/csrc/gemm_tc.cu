@@ -241,7 +241,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     const int splits = p.splits, ttiles = p.ttiles, units = p.units, nr_ = p.nr, ns_ = p.ns;
     const int raw_off = p.raw_off, b_off = p.b_off, bar_off = p.bar_off;
     extern __shared__ uint8_t gsm_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-aligned for the SWIZZLE_128B tiles; pointer arithmetic on the shared array keeps the
+    // pointer in the shared state space (plain ld/st.shared rather than generic accesses)
+    uint8_t* sm = gsm_raw + ((1024u - (s_addr(gsm_raw) & 1023u)) & 1023u);
     const int cb = chunk_bytes(TYPE);
     const int NR = nr_, NS = ns_;
     uint8_t* As = sm;               // NS x 16 KB decoded weights
