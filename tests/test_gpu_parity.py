@@ -335,6 +335,21 @@ def test_tensor_core_attention_matches_the_mma_sync_attention(model_factory):
     assert np.abs(tc["z"] - mma["z"]).max() < 2e-2
 
 
+def test_long_context_prefill_matches_the_decode_path(small):
+    """A prefill past ~28.6K visible keys, where the tensor-core attention reads the page table from
+    global memory instead of its staged copy: the last position's logits against prefilling all but
+    the last token and running that one through the single-token path (a separate attention kernel)."""
+    n = 29_500
+    tokens = [1] + toks(n - 1, 21)
+    with ctx(small, cap=n + 8) as c1:
+        full = c1.forward(tokens)
+    with ctx(small, cap=n + 8) as c2:
+        c2.prefill(tokens[:-1])
+        last = c2.forward([tokens[-1]])
+    assert rel_l2(full, last) < HIDDEN_TOL
+    assert int(np.argmax(full)) == int(np.argmax(last))
+
+
 def test_kernel_launches_are_counted(small):
     before = jv.kernel_launches()
     with ctx(small) as c:
