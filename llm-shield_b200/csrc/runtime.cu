@@ -876,34 +876,65 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     const float scale = 1.f / std::sqrt((float)c.head_dim);
 
     // Attention work items: runs of consecutive tokens that share (shared, segment) and have
-    // consecutive slots, cut into ATT_ITEM_TOKENS-token tiles, one per KV head; longest first.
-    // The tensor-core kernel takes two 32-token tiles per item (they share every K/V block).
+    // consecutive slots, cut into ATT_ITEM_TOKENS-token tiles, one item per tile (or pair of
+    // tiles) and KV head; longest first. The tensor-core kernel can take two consecutive tiles of
+    // a run per item (they share every K/V block); pairing halves the K/V traffic but doubles the
+    // item's time, so a pass that fits one wave of single tiles pairs none, one that fits a wave
+    // only when paired pairs its shortest tiles until it does, and a longer pass pairs them all.
     int pass_keys = 0;
     for (int t = 0; t < T; t++) pass_keys = std::max(pass_keys, L->shared[t] + (L->slot[t] - L->seg[t] + 1));
     const bool attn_tc = !attention_on_mma_sync() && attention_tc_fits(pass_keys + 64, m->page_slots);
-    const int item_tokens = attn_tc ? 2 * ATT_ITEM_TOKENS : ATT_ITEM_TOKENS;
     std::vector<AttnItem> items;
     if (!decode) {
-        int t = 0;
-        while (t < T) {
+        struct Tile { int t0, n, lim; bool cont; };  // cont: full, and the run goes on in the next tile
+        std::vector<Tile> tiles;
+        auto same_run = [&](int a, int b) {
+            return L->shared[b] == L->shared[a] && L->seg[b] == L->seg[a] && L->slot[b] == L->slot[a] + (b - a);
+        };
+        for (int t = 0; t < T;) {
             int n = 1;
-            while (n < item_tokens && t + n < T && L->shared[t + n] == L->shared[t] && L->seg[t + n] == L->seg[t] &&
-                   L->slot[t + n] == L->slot[t] + n)
-                n++;
-            int lim = L->shared[t] + (L->slot[t] + n - 1 - L->seg[t] + 1);
+            while (n < ATT_ITEM_TOKENS && t + n < T && same_run(t, t + n)) n++;
+            const bool cont = n == ATT_ITEM_TOKENS && t + n < T && same_run(t, t + n);
+            tiles.push_back({t, n, L->shared[t] + (L->slot[t] + n - 1 - L->seg[t] + 1), cont});
+            t += n;
+        }
+        std::vector<char> paired(tiles.size(), 0);  // tile i takes tile i + 1 as its second tile
+        if (attn_tc) {
+            std::vector<int> cand;
+            for (size_t i = 0; i + 1 < tiles.size(); i++)
+                if (tiles[i].cont) cand.push_back((int)i++);
+            const int64_t kvh = c.kv_heads, sms = m->sm_count;
+            const int64_t n_single = (int64_t)tiles.size() * kvh, n_all = ((int64_t)tiles.size() - (int64_t)cand.size()) * kvh;
+            if (n_all > sms) {
+                for (int i : cand) paired[i] = 1;
+            } else if (n_single > sms) {
+                std::stable_sort(cand.begin(), cand.end(), [&](int a, int b) { return tiles[a + 1].lim < tiles[b + 1].lim; });
+                int64_t n = n_single;
+                for (int i : cand) {
+                    if (n <= sms) break;
+                    paired[i] = 1;
+                    n -= kvh;
+                }
+            }
+        }
+        for (size_t i = 0; i < tiles.size(); i++) {
+            const Tile& a = tiles[i];
+            const bool two = paired[i] != 0;
+            const int n = two ? a.n + tiles[i + 1].n : a.n;
+            const int lim = two ? tiles[i + 1].lim : a.lim;
             for (int g = 0; g < c.kv_heads; g++) {
                 AttnItem it;
-                it.t0 = t;
+                it.t0 = a.t0;
                 it.ntok = n;
                 it.kv_head = g;
-                it.slot0 = L->slot[t];
-                it.shared = L->shared[t];
-                it.segment = L->seg[t];
+                it.slot0 = L->slot[a.t0];
+                it.shared = L->shared[a.t0];
+                it.segment = L->seg[a.t0];
                 it.nblocks = (lim + 63) / 64;
                 it.pad = 0;
                 items.push_back(it);
             }
-            t += n;
+            if (two) i++;
         }
         std::stable_sort(items.begin(), items.end(), [](const AttnItem& a, const AttnItem& b) { return a.nblocks > b.nblocks; });
     }
