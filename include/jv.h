@@ -133,6 +133,19 @@ int jv_forward_tree(jv_ctx* ctx, const int32_t* trunk, int32_t n_trunk, const in
                     const int32_t* branch_lengths, int32_t n_branches, const int32_t* rows,
                     int32_t n_rows, float* out);
 
+/* Many independent ForwardTreeAsync decisions in one pass: the batch entry of the data-parallel
+ * path (no single reference member; each decision is what MinistralModel.cs:198-219 computes
+ * for its trunk and branches on an empty cache). Decision d has trunk_lengths[d] trunk tokens
+ * and branch_counts[d] branches; `tokens` holds each decision's trunk and then its branches,
+ * decision after decision, and branch_lengths every branch in that order. A decision sees only
+ * its own tokens (not the cache's contents, not the other decisions). out[sum of branch_counts]
+ * [n_rows] = logits of `rows` at each branch's last token, in branch order; each row is
+ * bit-identical to that decision run alone by jv_forward_tree on an empty cache. The cache is
+ * left as it was (its length is restored after the pass). */
+int jv_decide_batch(jv_ctx* ctx, int32_t n_decisions, const int32_t* tokens, const int32_t* trunk_lengths,
+                    const int32_t* branch_counts, const int32_t* branch_lengths, const int32_t* rows,
+                    int32_t n_rows, float* out);
+
 /* The private ForwardAsync(tokens, capture, options, computeLogits, layout, selectedRows,
  * selectedOut) every public overload funnels into (MinistralModel.cs:301-435).
  * layout == NULL means a causal append at the cache end. With rows != NULL, out receives

@@ -1,8 +1,8 @@
 // attn_tc.cu — tree-masked GQA prefill attention on the 5th-generation tensor cores.
 //
 // Semantics are those of k_attention (kernels_attn.cu; reference MinistralModel.cs:446-636):
-// query row (token t, head h) sees logical keys L < limit(t), logical key L being cache slot L
-// below `shared` and slot segment + (L - shared) above; keys are walked in logical order in
+// query row (token t, head h) sees logical keys L < limit(t), logical key L being cache slot
+// base + L below `shared` and slot segment + (L - shared) above; keys are walked in logical order in
 // blocks cut on logical indices, so a token's output is bit-identical whether it runs in a
 // tree, alone after the trunk, or after a cached prefix.
 //
@@ -147,9 +147,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     const int limB = ntB > 0 ? it.shared + (it.slot0 + it.ntok - 1 - it.segment + 1) : 0;
     const int nbA = (limA + AT_KEYS - 1) / AT_KEYS, nbB = (limB + AT_KEYS - 1) / AT_KEYS;
     const int max_limit = max(limA, limB), nb = max(nbA, nbB);
-    // keys below `shared` (region A) are slots 0.., the rest (region B) slots segment..
+    // keys below `shared` (region A) are slots base.., the rest (region B) slots segment..
     const int nA = min(it.shared, max_limit), nBk = max_limit - nA;
-    const int pagesA = (nA + ps - 1) / ps;
+    const int pA0 = it.base / ps;
+    const int pagesA = nA > 0 ? (it.base + nA - 1) / ps - pA0 + 1 : 0;
     const int pB0 = nBk > 0 ? it.segment / ps : 0;
     const int pagesB = nBk > 0 ? (it.segment + nBk - 1) / ps - pB0 + 1 : 0;
     const bool staged = pagesA + pagesB <= AT_PAGES;  // else the loaders read the page table
@@ -172,7 +173,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     if (warp >= 8 && staged) {
         // stage the page-table entries of both key regions
         for (int i = tid - 256; i < pagesA + pagesB; i += 96)
-            pg[i] = __ldg(a.page_table + (i < pagesA ? i : pB0 + (i - pagesA)));
+            pg[i] = __ldg(a.page_table + (i < pagesA ? pA0 + i : pB0 + (i - pagesA)));
     }
     tc_fence_before();
     __syncthreads();
@@ -221,11 +222,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                     int La = reg == 0 ? L0 : max(L0, nA);
                     const int Lb = reg == 0 ? min(L0 + nvalid, nA) : L0 + nvalid;
                     while (La < Lb) {
-                        const int slot = reg == 0 ? La : it.segment + (La - nA);
+                        const int slot = reg == 0 ? it.base + La : it.segment + (La - nA);
                         const int row = slot % ps;
                         const int n = min(Lb - La, ps - row);
                         const int page = !staged ? __ldg(a.page_table + slot / ps)
-                                         : reg == 0 ? pg[slot / ps] : pg[pagesA + slot / ps - pB0];
+                                         : reg == 0 ? pg[slot / ps - pA0] : pg[pagesA + slot / ps - pB0];
                         const char* plane = pool + (int64_t)page * a.page_bytes;
                         const int key0 = La - L0;
                         if (((key0 - row) & 7) == 0) {

@@ -161,8 +161,12 @@ void launch_rope_kv(const RopeArgs& a, cudaStream_t s);
 void launch_rope_table(float2* table, const float* freqs, int half, int pos0, int npos, float mscale, cudaStream_t s);
 
 constexpr int ATT_ITEM_TOKENS = 32;  // tokens per prefill attention item (x 4 query heads = 128 rows)
-struct AttnItem {  // one query tile: up to 32 consecutive tokens of one segment, one KV head
-    int32_t t0, ntok, kv_head, slot0, shared, segment, nblocks, pad;
+// One query item: consecutive tokens of one segment, one KV head. The tokens see logical keys
+// L < shared (slot base + L, the shared region) and then their own segment (slot segment + L -
+// shared), in that order; base is 0 except in a batch of independent trees, where each tree's
+// shared region starts at its own slot.
+struct AttnItem {
+    int32_t t0, ntok, kv_head, slot0, shared, segment, nblocks, base;
 };
 struct AttnArgs {
     const __half* q16;          // [T][heads*hd]

@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int L = L0 + j * ATT_THREADS;
-            slot[j] = L < it.shared ? L : it.segment + (L - it.shared);
+            slot[j] = L < it.shared ? it.base + L : it.segment + (L - it.shared);
             page[j] = L < max_limit ? a.page_table[slot[j] / a.page_slots] : 0;
         }
 #pragma unroll

@@ -573,6 +573,7 @@ void ctx_release_pages(jv_ctx* x) {
 
 struct HostLayout {
     std::vector<int32_t> slot, pos, shared, seg, outputs;
+    std::vector<int32_t> base;  // first slot of each token's shared region; empty = 0 (TokenLayout's case)
     int end = 0;
 };
 
@@ -857,6 +858,15 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     }
     for (int o : L->outputs)
         if (o < 0 || o >= T) throw Error(JV_ERR_ARG, "output index out of range");
+    // Token t sees slots [base, shared) and then [segment, slot]: sh[t] shared keys from bs[t].
+    std::vector<int> bs(T, 0), sh(T);
+    for (int t = 0; t < T; t++) {
+        if (!L->base.empty()) bs[t] = L->base[t];
+        if (bs[t] < 0 || bs[t] > L->shared[t]) throw Error(JV_ERR_ARG, "layout entry " + std::to_string(t) + " is inconsistent");
+        sh[t] = L->shared[t] - bs[t];
+    }
+    if (T == 1 && bs[0] != 0 && sh[0] != 0)
+        throw Error(JV_ERR_UNSUPPORTED, "a single-token step must see its shared keys from slot 0");
 
     // KvCache.EnsureCapacity(end); copy-on-write for the pages this pass writes.
     ctx_ensure_capacity(x, end);
@@ -882,20 +892,20 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     // item's time, so a pass that fits one wave of single tiles pairs none, one that fits a wave
     // only when paired pairs its shortest tiles until it does, and a longer pass pairs them all.
     int pass_keys = 0;
-    for (int t = 0; t < T; t++) pass_keys = std::max(pass_keys, L->shared[t] + (L->slot[t] - L->seg[t] + 1));
+    for (int t = 0; t < T; t++) pass_keys = std::max(pass_keys, sh[t] + (L->slot[t] - L->seg[t] + 1));
     const bool attn_tc = !attention_on_mma_sync() && attention_tc_fits(pass_keys + 64, m->page_slots);
     std::vector<AttnItem> items;
     if (!decode) {
         struct Tile { int t0, n, lim; bool cont; };  // cont: full, and the run goes on in the next tile
         std::vector<Tile> tiles;
         auto same_run = [&](int a, int b) {
-            return L->shared[b] == L->shared[a] && L->seg[b] == L->seg[a] && L->slot[b] == L->slot[a] + (b - a);
+            return L->shared[b] == L->shared[a] && bs[b] == bs[a] && L->seg[b] == L->seg[a] && L->slot[b] == L->slot[a] + (b - a);
         };
         for (int t = 0; t < T;) {
             int n = 1;
             while (n < ATT_ITEM_TOKENS && t + n < T && same_run(t, t + n)) n++;
             const bool cont = n == ATT_ITEM_TOKENS && t + n < T && same_run(t, t + n);
-            tiles.push_back({t, n, L->shared[t] + (L->slot[t] + n - 1 - L->seg[t] + 1), cont});
+            tiles.push_back({t, n, sh[t] + (L->slot[t] + n - 1 - L->seg[t] + 1), cont});
             t += n;
         }
         std::vector<char> paired(tiles.size(), 0);  // tile i takes tile i + 1 as its second tile
@@ -928,10 +938,10 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
                 it.ntok = n;
                 it.kv_head = g;
                 it.slot0 = L->slot[a.t0];
-                it.shared = L->shared[a.t0];
+                it.shared = sh[a.t0];
                 it.segment = L->seg[a.t0];
                 it.nblocks = (lim + 63) / 64;
-                it.pad = 0;
+                it.base = bs[a.t0];
                 items.push_back(it);
             }
             if (two) i++;
@@ -942,7 +952,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     for (const AttnItem& it : items) max_item_keys = std::max(max_item_keys, it.nblocks * 64);
     // Algorithmic attention work: QK^T and PV over exactly the visible (query, key) pairs.
     double attn_flops = 0, attn_bytes = 2.0 * 2 * T * qdim;
-    for (int t = 0; t < T; t++) attn_flops += 4.0 * c.heads * c.head_dim * (L->shared[t] + (L->slot[t] - L->seg[t] + 1));
+    for (int t = 0; t < T; t++) attn_flops += 4.0 * c.heads * c.head_dim * (sh[t] + (L->slot[t] - L->seg[t] + 1));
     for (const AttnItem& it : items)
         attn_bytes += (double)(it.shared + (it.slot0 + it.ntok - 1 - it.segment + 1)) * c.head_dim * 2 * 2;
 
@@ -970,9 +980,9 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         st.token = tokens[0];
         st.slot = L->slot[0];
         st.pos = L->pos[0];
-        st.shared = L->shared[0];
+        st.shared = sh[0];
         st.segment = L->seg[0];
-        st.n_keys = dec_keys = L->shared[0] + (L->slot[0] - L->seg[0] + 1);
+        st.n_keys = dec_keys = sh[0] + (L->slot[0] - L->seg[0] + 1);
         std::memcpy(hin + step_off, &st, sizeof st);
     }
     JV_CUDA(cudaMemcpyAsync(din, hin, sizeof(int32_t) * total_words, cudaMemcpyHostToDevice, x->stream));
@@ -1040,9 +1050,9 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
             da.layer = l;
             da.heads = c.heads;
             da.kv_heads = c.kv_heads;
-            da.shared = L->shared[0];
+            da.shared = sh[0];
             da.segment = L->seg[0];
-            da.n_keys = L->shared[0] + (L->slot[0] - L->seg[0] + 1);
+            da.n_keys = sh[0] + (L->slot[0] - L->seg[0] + 1);
             da.scale = scale;
             da.splits = (da.n_keys + 63) / 64;
             da.partial = x->tmp32.get((size_t)c.heads * da.splits * (2 + c.head_dim));
@@ -1458,6 +1468,51 @@ int jv_forward_tree(jv_ctx* x, const int32_t* trunk, int32_t n_trunk, const int3
         std::memcpy(tokens.data() + n_trunk, branch_tokens, sizeof(int32_t) * (total - n_trunk));
         HostLayout L = layout_tree(x->length, n_trunk, offsets, total);
         forward(x, tokens.data(), total, &L, rows, n_rows, rows == nullptr, out, false, nullptr);
+    });
+}
+
+int jv_decide_batch(jv_ctx* x, int32_t n_decisions, const int32_t* tokens, const int32_t* trunk_lengths,
+                    const int32_t* branch_counts, const int32_t* branch_lengths, const int32_t* rows, int32_t n_rows,
+                    float* out) {
+    if (!x || !tokens || !trunk_lengths || !branch_counts || !branch_lengths || !rows || !out)
+        return set_error(JV_ERR_ARG, "NULL argument");
+    return guarded([&] {
+        if (n_decisions <= 0) throw Error(JV_ERR_ARG, "No decisions to forward.");
+        // Decision d occupies slots [base_d, base_d + its tokens) after the cache's current end;
+        // its trunk is causal from base_d with positions from 0, each branch sees the trunk and
+        // itself (TokenLayout.Tree per decision, with the shared region starting at base_d).
+        const int start = x->length;
+        HostLayout L;
+        int cursor = start, t = 0, br = 0;
+        for (int d = 0; d < n_decisions; d++) {
+            const int trunk = trunk_lengths[d], nb = branch_counts[d];
+            if (trunk < 0) throw Error(JV_ERR_ARG, "Decision " + std::to_string(d) + " has a negative trunk length.");
+            if (nb <= 0) throw Error(JV_ERR_ARG, "Decision " + std::to_string(d) + " has no branches.");
+            const int base = cursor;
+            for (int i = 0; i < trunk; i++, t++) {
+                L.slot.push_back(cursor++);
+                L.pos.push_back(i);
+                L.base.push_back(base);
+                L.shared.push_back(base);
+                L.seg.push_back(base);
+            }
+            for (int b = 0; b < nb; b++, br++) {
+                const int n = branch_lengths[br];
+                if (n <= 0) throw Error(JV_ERR_ARG, "Branch " + std::to_string(b) + " of decision " + std::to_string(d) + " is empty.");
+                const int seg = cursor;
+                for (int i = 0; i < n; i++, t++) {
+                    L.slot.push_back(cursor++);
+                    L.pos.push_back(trunk + i);
+                    L.base.push_back(base);
+                    L.shared.push_back(base + trunk);
+                    L.seg.push_back(seg);
+                }
+                L.outputs.push_back(t - 1);
+            }
+        }
+        L.end = cursor;
+        forward(x, tokens, t, &L, rows, n_rows, false, out, false, nullptr);
+        x->length = start;  // the batch's slots are scratch: the cache is left as it was
     });
 }
 

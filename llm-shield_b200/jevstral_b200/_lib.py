@@ -56,6 +56,7 @@ SIGNATURES = [
     ("jv_forward", C.c_int, [vp, i32p, i32, f32p]),
     ("jv_forward_selected", C.c_int, [vp, i32p, i32, i32p, i32, f32p]),
     ("jv_forward_tree", C.c_int, [vp, i32p, i32, i32p, i32p, i32, i32p, i32, f32p]),
+    ("jv_decide_batch", C.c_int, [vp, i32, i32p, i32p, i32p, i32p, i32p, i32, f32p]),
     ("jv_forward_layout", C.c_int, [vp, i32p, i32, C.POINTER(JvLayout), i32p, i32, i32, f32p, i32, f32p]),
     ("jv_decode_greedy", C.c_int, [vp, i32, i32, i32p]),
     ("jv_qweight_bytes", i64, [i32, i32, i32]),

@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass
-from typing import Callable, Optional, Sequence
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -262,6 +262,29 @@ class MinistralModel:
         check(lib.jv_forward_tree(self._h, _p(tr), tr.size, _p(flat), _p(lens), len(branches), _p(r), r.size,
                                   _p(out, C.c_float)))
         return out
+
+    def decide_batch(self, decisions: Sequence[Tuple[Sequence[int], Sequence[Sequence[int]]]],
+                     vocab_rows: Sequence[int]) -> List[np.ndarray]:
+        """Many independent tree decisions in one pass (jv_decide_batch): for each (trunk, branches)
+        the [branches][rows] logits ForwardTreeAsync gives it on an empty cache. The cache is left
+        as it was."""
+        flat, trunks, counts, lens = [], [], [], []
+        for trunk, branches in decisions:
+            flat.extend(int(v) for v in trunk)
+            trunks.append(len(trunk))
+            counts.append(len(branches))
+            for b in branches:
+                flat.extend(int(v) for v in b)
+                lens.append(len(b))
+        t, tr, cn, ln, r = _i32(flat), _i32(trunks), _i32(counts), _i32(lens), _i32(vocab_rows)
+        out = np.empty((len(lens), r.size), dtype=np.float32)
+        check(lib.jv_decide_batch(self._h, len(decisions), _p(t), _p(tr), _p(cn), _p(ln), _p(r), r.size,
+                                  _p(out, C.c_float)))
+        res, i = [], 0
+        for n in counts:
+            res.append(out[i:i + n])
+            i += n
+        return res
 
     def forward_branches(self, branches, vocab_rows) -> np.ndarray:
         return self.forward_tree([], branches, vocab_rows)

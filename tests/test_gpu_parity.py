@@ -335,6 +335,26 @@ def test_tensor_core_attention_matches_the_mma_sync_attention(model_factory):
     assert np.abs(tc["z"] - mma["z"]).max() < 2e-2
 
 
+def test_decision_batch_is_bit_identical_to_single_decisions(small):
+    """jv_decide_batch: each decision of a batch (trunks of different lengths, branches of odd
+    lengths so segments start off multiples of 8, one decision without a trunk) gives exactly the
+    logits it gives alone on an empty cache, and the cache is left as it was."""
+    rng = np.random.default_rng(77)
+    decisions = []
+    for trunk_len, blens in [(37, [5, 11]), (130, [3, 9, 17]), (0, [4]), (300, [33, 1, 7, 40]), (64, [32, 32])]:
+        trunk = ([1] + toks(trunk_len - 1, int(rng.integers(1 << 30)))) if trunk_len else []
+        decisions.append((trunk, [toks(n, int(rng.integers(1 << 30))) for n in blens]))
+    with ctx(small, cap=2048) as c:
+        c.forward([1] + toks(20, 5))  # something in the cache that the batch must neither see nor disturb
+        before = c.cached_token_count
+        got = c.decide_batch(decisions, VERDICT_ROWS)
+        assert c.cached_token_count == before
+    for (trunk, branches), g in zip(decisions, got):
+        with ctx(small, cap=2048) as c:
+            want = c.forward_tree(trunk, branches, VERDICT_ROWS)
+        assert np.array_equal(g, want)
+
+
 def test_long_context_prefill_matches_the_decode_path(small):
     """A prefill past ~28.6K visible keys, where the tensor-core attention reads the page table from
     global memory instead of its staged copy: the last position's logits against prefilling all but
