@@ -226,8 +226,41 @@ def run_b200(args, rank, world, local_rank, dist):
         costs = [jv.dp.decision_cost(len(t), [len(b) for b in br]) for t, br in glob]
         shard = jv.dp.shard_decisions(costs, world)[rank]
         timed = [glob[i] for i in shard]
-        # size every buffer before the clock starts: the shard's largest tree once
-        step(*max(timed, key=lambda w: len(w[0]) + sum(len(b) for b in w[1])))
+    # C5 runs its shard through jv_decide_batch: consecutive decisions are grouped into one pass of
+    # at most --c5-batch-tokens tokens (each decision bit-identical to running it alone).
+    batches = None
+    if args.config == "c5" and args.c5_batch_tokens > 0:
+        batches, cur, n = [], [], 0
+        for w in timed:
+            k = len(w[0]) + sum(len(b) for b in w[1])
+            if cur and n + k > args.c5_batch_tokens:
+                batches.append(cur)
+                cur, n = [], 0
+            cur.append(w)
+            n += k
+        if cur:
+            batches.append(cur)
+
+    def run_all():
+        out = []
+        if batches is None:
+            for w in timed:
+                out.append(step(*w))
+            return out
+        for bt in batches:
+            ctx.kv_cache.reset()
+            for v in ctx.decide_batch(bt, ROWS):
+                out.append(jv.decision_probs(jv.margins_from_verdicts(v, 1)))
+        return out
+
+    if args.config == "c5":
+        # size every buffer before the clock starts: the shard's largest tree (or batch) once
+        if batches is None:
+            step(*max(timed, key=lambda w: len(w[0]) + sum(len(b) for b in w[1])))
+        else:
+            big = max(batches, key=lambda bt: sum(len(w[0]) + sum(len(b) for b in w[1]) for w in bt))
+            ctx.kv_cache.reset()
+            ctx.decide_batch(big, ROWS)
         torch.cuda.synchronize()
     results = []
 
@@ -257,8 +290,7 @@ def run_b200(args, rank, world, local_rank, dist):
     with ClockSampler(local_rank) as clocks:
         t0 = time.perf_counter()
         ev0.record(stream)
-        for w in timed:
-            results.append(step(*w))
+        results = run_all()
         ev1.record(stream)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
@@ -271,8 +303,7 @@ def run_b200(args, rank, world, local_rank, dist):
     # serialise launches that otherwise overlap).
     ctx.profile(True)
     ctx.profile_reset()
-    for w in timed:
-        step(*w)
+    run_all()
     torch.cuda.synchronize()
     prof = {k: ctx.profile_read(k) for k in ("gemm", "attention", "gemv")}
     ctx.profile(False)
@@ -313,7 +344,9 @@ def run_b200(args, rank, world, local_rank, dist):
             "data": "synthetic (random-init Ministral-3 3B, N(0,0.02) weights, uniform token ids, seeded)",
             "config": {"workload": WORKLOADS[args.config], "weights": qtype, "tokens_per_step": tokens // n_dec,
                        "parallelism": f"dp{world} (independent replicas, no collective)",
-                       "l2": "weights (3.2+ GB) exceed the 126 MB L2 and stream from HBM every step"},
+                       "l2": "weights (3.2+ GB) exceed the 126 MB L2 and stream from HBM every step",
+                       **({"batching": f"jv_decide_batch, {len(batches)} passes of up to {args.c5_batch_tokens} tokens"}
+                          if batches is not None else {})},
             "decisions_per_s": job_decisions / dev_s,
             "linear_tflops": job_tokens * LINEAR_FLOPS_PER_TOKEN * args.layers / 26 / dev_s / 1e12,
             "attention_pairs_per_step": pairs // n_dec,
@@ -330,7 +363,8 @@ def run_b200(args, rank, world, local_rank, dist):
                         for k, v in prof.items()},
             "e2e": {"value": job_tokens / wall, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "how": "host wall-clock around the public C-ABI calls (jv_forward_tree) with host buffers"},
+                    "how": "host wall-clock around the public C-ABI calls ("
+                           + ("jv_decide_batch" if batches is not None else "jv_forward_tree") + ") with host buffers"},
             "gpu_launches": launches,
             "clocks": clocks.summary(),
         }
@@ -419,6 +453,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=26, help="fewer layers of the same width (profiling only)")
     ap.add_argument("--kv-pool-mb", type=int, default=4096)
+    ap.add_argument("--c5-batch-tokens", type=int, default=0,
+                    help="C5: group decisions into jv_decide_batch passes of at most this many tokens "
+                         "(0, the default: one jv_forward_tree per decision; measured no faster at C5's sizes)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
