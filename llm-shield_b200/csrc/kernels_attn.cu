@@ -5,8 +5,8 @@
 // [0, shared) and [segment, slot], in that order, and nothing else — the trunk is causal,
 // each branch sees the whole trunk plus its own earlier tokens and never a sibling.
 //
-// Keys are walked in *logical* order: logical index L < shared is slot L, L >= shared is
-// slot segment + (L - shared). Blocks of 64 keys are cut on logical indices, so a token
+// Keys are walked in *logical* order: logical index L < shared is slot base + L (base is 0 except
+// in a batch of independent trees), L >= shared is slot segment + (L - shared). Blocks of 64 keys are cut on logical indices, so a token
 // meets exactly the same key blocks, in the same order and at the same positions inside
 // each block, whether it runs in a tree, alone after the trunk, or after a cached prefix.
 // With a block that a row cannot see being an exact no-op (max unchanged, rescale factor
