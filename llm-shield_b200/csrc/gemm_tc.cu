@@ -226,7 +226,7 @@ __device__ __forceinline__ void drain_cols(uint32_t tacc, int c0, int c1, int ki
     }
 }
 
-template <int TYPE>
+template <int TYPE, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     // Every parameter in a register or a restrict pointer: nothing below takes the address of
     // the parameter block, so no access is re-read after a store.
@@ -237,7 +237,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     __half* __restrict__ g_xs_out = p.xs_out;
     float* g_ws = p.ws;
     int* __restrict__ g_ctr = p.counters;
-    const int ksteps = p.ksteps, T = p.T, tpad = p.tpad, bn = p.bn, ldy = p.ldy, epi = p.epilogue, ncols = p.ncols;
+    // The epilogue is a template parameter: each instantiation carries only its own drain code.
+    constexpr int epi = EPI;
+    const int ksteps = p.ksteps, T = p.T, tpad = p.tpad, bn = p.bn, ldy = p.ldy, ncols = p.ncols;
     const int splits = p.splits, ttiles = p.ttiles, units = p.units, nr_ = p.nr, ns_ = p.ns;
     const int raw_off = p.raw_off, b_off = p.b_off, bar_off = p.bar_off;
     extern __shared__ uint8_t gsm_raw[];
@@ -493,7 +495,7 @@ int gemm_tpad_for(int T) {
 
 static int g_sm_count = 0;
 
-template <int TYPE>
+template <int TYPE, int EPI>
 static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     const QWeight& w = *a.w;
     TcParams p;
@@ -528,15 +530,26 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.raw_off = p.b_off + a.bn * 128 * p.ns;
     p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
     size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
-    JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (g_sm_count == 0) {
         int dev = 0;
         JV_CUDA(cudaGetDevice(&dev));
         JV_CUDA(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
     }
     int grid = std::min(p.units, g_sm_count);
-    launch_pdl(k_gemm_tc<TYPE>, dim3(grid), dim3(GEMM_THREADS), smem, s, p);
+    launch_pdl(k_gemm_tc<TYPE, EPI>, dim3(grid), dim3(GEMM_THREADS), smem, s, p);
     note_launch();
+}
+
+template <int TYPE>
+static void launch_tc_epi(const GemmArgs& a, cudaStream_t s) {
+    switch (a.epilogue) {
+        case EPI_STORE: launch_tc_typed<TYPE, EPI_STORE>(a, s); break;
+        case EPI_ADD: launch_tc_typed<TYPE, EPI_ADD>(a, s); break;
+        case EPI_SWIGLU: launch_tc_typed<TYPE, EPI_SWIGLU>(a, s); break;
+        case EPI_PARTIAL: launch_tc_typed<TYPE, EPI_PARTIAL>(a, s); break;
+        default: throw Error(JV_ERR_ARG, "gemm: bad epilogue");
+    }
 }
 
 int gemm_splits_for(const QWeight& w) {
@@ -553,9 +566,9 @@ void launch_gemm(const GemmArgs& a, cudaStream_t s) {
     if (a.epilogue == EPI_SWIGLU && (a.splits != 1 || !a.xs_out))
         throw Error(JV_ERR_ARG, "gemm: the SwiGLU epilogue needs an unsplit product and an output slab");
     switch (a.w->type) {
-        case T_Q8_0: launch_tc_typed<T_Q8_0>(a, s); break;
-        case T_Q4_0: launch_tc_typed<T_Q4_0>(a, s); break;
-        case T_Q5_1: launch_tc_typed<T_Q5_1>(a, s); break;
+        case T_Q8_0: launch_tc_epi<T_Q8_0>(a, s); break;
+        case T_Q4_0: launch_tc_epi<T_Q4_0>(a, s); break;
+        case T_Q5_1: launch_tc_epi<T_Q5_1>(a, s); break;
         default: throw Error(JV_ERR_UNSUPPORTED, "gemm: weight type not on the B200 path");
     }
 }
