@@ -226,7 +226,7 @@ __device__ __forceinline__ void drain_cols(uint32_t tacc, int c0, int c1, int ki
     }
 }
 
-template <int TYPE, int EPI>
+template <int TYPE, int EPI, bool CSPLIT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     // Every parameter in a register or a restrict pointer: nothing below takes the address of
     // the parameter block, so no access is re-read after a store.
@@ -238,6 +238,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     float* g_ws = p.ws;
     int* __restrict__ g_ctr = p.counters;
     // The epilogue is a template parameter: each instantiation carries only its own drain code.
+    // CSPLIT: a K-split store/add whose halves are combined through the counters (the
+    // activation-capture path; the hot path splits only with EPI_PARTIAL).
     constexpr int epi = EPI;
     const int ksteps = p.ksteps, T = p.T, tpad = p.tpad, bn = p.bn, ldy = p.ldy, ncols = p.ncols;
     const int splits = p.splits, ttiles = p.ttiles, units = p.units, nr_ = p.nr, ns_ = p.ns;
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         // last unit is drained by these warps and the (then idle) decoder warps together,
         // a third of the columns each (see drain_share).
         const int q = warp & 3;
-        const bool counter_split = splits > 1 && epi != EPI_PARTIAL;
+        constexpr bool counter_split = CSPLIT;
         pdl_wait();
         int i = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, i++) {
@@ -451,7 +453,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     }
     // The decoder warps, done with the main loop, drain two thirds of the last unit's columns
     // (the epilogue warps drain the first third), so the tail after the last MMA is short.
-    if (warp >= DEC_WARP0 && !(splits > 1 && epi != EPI_PARTIAL) && (int)blockIdx.x < units) {
+    if (warp >= DEC_WARP0 && !CSPLIT && (int)blockIdx.x < units) {
         const int my_units = (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
         const int il = my_units - 1, ul = (int)blockIdx.x + il * (int)gridDim.x;
         int tile, tt, sp;
@@ -495,7 +497,7 @@ int gemm_tpad_for(int T) {
 
 static int g_sm_count = 0;
 
-template <int TYPE, int EPI>
+template <int TYPE, int EPI, bool CSPLIT>
 static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     const QWeight& w = *a.w;
     TcParams p;
@@ -530,24 +532,25 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.raw_off = p.b_off + a.bn * 128 * p.ns;
     p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
     size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
-    JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE, EPI, CSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (g_sm_count == 0) {
         int dev = 0;
         JV_CUDA(cudaGetDevice(&dev));
         JV_CUDA(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
     }
     int grid = std::min(p.units, g_sm_count);
-    launch_pdl(k_gemm_tc<TYPE, EPI>, dim3(grid), dim3(GEMM_THREADS), smem, s, p);
+    launch_pdl(k_gemm_tc<TYPE, EPI, CSPLIT>, dim3(grid), dim3(GEMM_THREADS), smem, s, p);
     note_launch();
 }
 
 template <int TYPE>
 static void launch_tc_epi(const GemmArgs& a, cudaStream_t s) {
+    const bool cs = a.splits > 1;
     switch (a.epilogue) {
-        case EPI_STORE: launch_tc_typed<TYPE, EPI_STORE>(a, s); break;
-        case EPI_ADD: launch_tc_typed<TYPE, EPI_ADD>(a, s); break;
-        case EPI_SWIGLU: launch_tc_typed<TYPE, EPI_SWIGLU>(a, s); break;
-        case EPI_PARTIAL: launch_tc_typed<TYPE, EPI_PARTIAL>(a, s); break;
+        case EPI_STORE: cs ? launch_tc_typed<TYPE, EPI_STORE, true>(a, s) : launch_tc_typed<TYPE, EPI_STORE, false>(a, s); break;
+        case EPI_ADD: cs ? launch_tc_typed<TYPE, EPI_ADD, true>(a, s) : launch_tc_typed<TYPE, EPI_ADD, false>(a, s); break;
+        case EPI_SWIGLU: launch_tc_typed<TYPE, EPI_SWIGLU, false>(a, s); break;
+        case EPI_PARTIAL: launch_tc_typed<TYPE, EPI_PARTIAL, false>(a, s); break;
         default: throw Error(JV_ERR_ARG, "gemm: bad epilogue");
     }
 }
