@@ -481,18 +481,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     }
 }
 
-int gemm_bn_for(int T) {
-    // At least two token tiles from 128 tokens on, so that the 48-tile QKV and the split
-    // 24-tile projections still cover most SMs when T is a few hundred.
-    int tiles = (T + 255) / 256;
-    if (T >= 128 && tiles < 2) tiles = 2;
-    int per = (T + tiles - 1) / tiles;
-    int bn = (per + 15) / 16 * 16;
-    return bn < 16 ? 16 : bn;
-}
+// Token tiles of a pass of T tokens: ceil(T / 256) balanced tiles, multiples of 16. From 128 to
+// 256 tokens a product with few row tiles (the 48-tile QKV, the split 24-tile projections) takes
+// two tiles of T / 2 so that it still covers most SMs; one with many row tiles (gate/up, the
+// head) keeps one tile of T, which halves its MMA instructions and still fills the SMs. tpad is
+// a multiple of both.
 int gemm_tpad_for(int T) {
-    int bn = gemm_bn_for(T);
-    return (T + bn - 1) / bn * bn;
+    if (T >= 128 && T <= 256) return 2 * (((T + 1) / 2 + 15) / 16 * 16);
+    const int n = T > 0 ? (T + 255) / 256 : 1;
+    const int bn = ((T + n - 1) / n + 15) / 16 * 16;
+    return n * (bn < 16 ? 16 : bn);
+}
+// units_per_tile = row tiles x K splits of the product.
+int gemm_bn_for(int T, int units_per_tile, int sm_count) {
+    const int tpad = gemm_tpad_for(T);
+    if (T >= 128 && T <= 256) return units_per_tile * 4 >= sm_count * 3 ? tpad : tpad / 2;
+    const int n = T > 0 ? (T + 255) / 256 : 1;
+    return tpad / n;
 }
 
 static int g_sm_count = 0;

@@ -113,11 +113,12 @@ struct GemmArgs {
 };
 int gemm_splits_for(const QWeight& w);
 
-// Token tile for a GEMM over T tokens: balanced tiles of at most 256 (the MMA's N limit),
-// multiples of 16. Depends on T only, never on which tokens they are; the K order of the
-// MMA chain does not depend on it, so a token's result is independent of its batch.
-int gemm_bn_for(int T);
+// Token tiles for a GEMM over T tokens: balanced tiles of at most 256 (the MMA's N limit),
+// multiples of 32, halved for products that would leave SMs idle. Depends on T and the matrix
+// only, never on which tokens they are; the K order of the MMA chain does not depend on it,
+// so a token's result is independent of its batch.
 int gemm_tpad_for(int T);
+int gemm_bn_for(int T, int units_per_tile, int sm_count);
 
 // ------------------------------------------------------------ kernel API
 

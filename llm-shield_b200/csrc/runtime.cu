@@ -638,7 +638,7 @@ void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float*
     a.x = xs;
     a.T = T;
     a.tpad = tpad;
-    a.bn = gemm_bn_for(T);
+    a.bn = gemm_bn_for(T, w.tiles * ((epi == EPI_SWIGLU) ? 1 : gemm_splits_for(w)), x->m->sm_count);
     a.y = y;
     a.ldy = ldy;
     a.epilogue = epi;
@@ -671,7 +671,7 @@ const float* gemm_resid(jv_ctx* x, const QWeight& w, const __half* xs, int T, in
     a.x = xs;
     a.T = T;
     a.tpad = tpad;
-    a.bn = gemm_bn_for(T);
+    a.bn = gemm_bn_for(T, w.tiles * 2, x->m->sm_count);
     a.y = h;
     a.ldy = ldy;
     a.epilogue = EPI_PARTIAL;
