@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 {
                     const int x = (nbB == 0 || u >= 2 * nbA) ? (nbB == 0 ? 0 : 1) : (u & 1);
                     const int b = nbB == 0 ? u : u < 2 * nbA ? (u >> 1) : u - nbA;
-                    if (ns[x] > b && mbar_test(p_full, (uint32_t)(u & 1)) &&
+                    if ((x ? ns[1] : ns[0]) > b && mbar_test(p_full, (uint32_t)(u & 1)) &&
                         mbar_test(v_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) {
                         tc_fence_after();
                         const uint32_t p = s_addr(Ps), v = s_addr(Vs + (b & 1) * AT_TILE);
