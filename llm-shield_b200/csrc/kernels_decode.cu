@@ -497,10 +497,13 @@ void launch_dec_mode(int type, const DecGemvArgs& a, int splits, cudaStream_t s)
 }  // namespace
 
 int dec_splits_for(const QWeight& w, int sm_count) {
-    // about three CTAs per SM, and a weight slice of at most 64 KB so that three fit
-    int splits = gemv_splits_for(w, sm_count);
+    // About four CTAs per SM and weight slices of at most 40 KB: the next kernel's CTAs then
+    // find room to become resident and stage their own slices while this one runs (measured on
+    // C4 against three CTAs / 64 KB: 1.47 vs 1.55 ms per step). Never fewer than 4 k steps.
+    int splits = std::max(1, (4 * sm_count + w.tiles - 1) / w.tiles);
+    splits = std::min(splits, std::max(1, (w.ksteps + 3) / 4));
     const int cb = chunk_bytes(w.type);
-    const int max_per = std::max(1, (64 * 1024) / cb);
+    const int max_per = std::max(1, (40 * 1024) / cb);
     splits = std::max(splits, (w.ksteps + max_per - 1) / max_per);
     return std::min(splits, w.ksteps);
 }
