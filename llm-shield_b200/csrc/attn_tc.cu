@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 bool ok = true;
                 if (lane == 0) ok = mbar_wait(empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u);
                 if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
-                    if (lane == 0) atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+                    if (lane == 0) report_timeout(err, 16 + 1 + kv);
                     break;
                 }
                 const uint32_t tile = ring + (uint32_t)(s * AT_TILE);
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                     if (gtimer() - idle_since > WAIT_NS) ok = false;
                 }
             }
-            if (!ok) atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+            if (!ok) report_timeout(err, 16 + 3);
         }
     } else {
         // --------------------------------------------------- softmax and the output
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
         if (nbt > 0) {
             if (ok && !warp_wait(o_done + 8 * x, (uint32_t)((nbt - 1) & 1))) ok = false;
             if (!ok) {
-                atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+                report_timeout(err, 16 + 4 + x);
             } else {
                 tc_fence_after();
                 const float inv = 1.f / l;

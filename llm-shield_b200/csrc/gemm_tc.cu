@@ -320,12 +320,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                     issued++;
                 }
             }
-            if (!ok) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+            if (!ok) report_timeout(g_err, weights ? 1 : 2);
             // Never leave with copies in flight into this CTA's shared memory: wait for the
             // last min(issued, ring) copies.
             for (int i = 0; i < issued && i < depth; i++) {
                 r.prev();
-                if (!mbar_wait(full + 8 * r.idx, r.phase)) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+                if (!mbar_wait(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
             }
         }
     } else if (warp == 1) {
@@ -354,10 +354,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 }
                 if (ok) umma_commit(acc_full + 8 * ab);
             }
-            if (!ok) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+            if (!ok) report_timeout(g_err, 4);
             // Wait until every MMA this lane issued has completed before teardown.
             umma_commit(drained);
-            if (!mbar_wait(drained, 0)) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+            if (!mbar_wait(drained, 0)) report_timeout(g_err, 5);
         }
     } else if (warp >= DEC_WARP0) {  // --------------------------------------- decode
         // Two groups of four warps take alternate k steps (group g the steps k = g mod 2 of
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 rs.next();
             }
         }
-        if (!ok) atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+        if (!ok) report_timeout(g_err, 6);
     } else if (warp >= 4) {  // ------------------------------------------------- epilogue
         // Warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows of the unit's tile. The CTA's
         // last unit is drained by these warps and the (then idle) decoder warps together,
@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             const bool ready = mbar_wait(acc_full + 8 * ab, (uint32_t)((i >> 1) & 1));
             tc_fence_after();
             if (!ready) {
-                atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+                report_timeout(g_err, 7);
                 break;
             }
             const uint32_t tacc = tmem + (uint32_t)(ab * ncols) + ((uint32_t)(q * 32) << 16);
@@ -470,7 +470,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                        t0, min(bn, T - t0), tpad, ldy, epi == EPI_PARTIAL ? g_ws + (int64_t)sp * T * ldy : g_y, nullptr,
                        g_xs_out);
         } else {
-            atomicExch(g_err, JV_ERR_DEVICE_TIMEOUT);
+            report_timeout(g_err, 8);
         }
     }
     tc_fence_before();

@@ -581,16 +581,36 @@ void check_cancel(jv_ctx* x) {
     if (x->cancel && *x->cancel) throw Error(JV_ERR_CANCELLED, "The operation was canceled.");
 }
 
+// Sites of a device-side timeout (report_timeout in tc_common.cuh): kernel x 16 + role.
+const char* timeout_site(int site) {
+    switch (site) {
+        case 1: return "tensor-core GEMM, weight producer";
+        case 2: return "tensor-core GEMM, activation producer";
+        case 3: return "tensor-core GEMM, producer teardown";
+        case 4: return "tensor-core GEMM, MMA issuer";
+        case 5: return "tensor-core GEMM, MMA teardown";
+        case 6: return "tensor-core GEMM, decoders";
+        case 7: return "tensor-core GEMM, epilogue";
+        case 8: return "tensor-core GEMM, decoders draining the last tile";
+        case 17: return "tensor-core attention, K loader";
+        case 18: return "tensor-core attention, V loader";
+        case 19: return "tensor-core attention, MMA issuer";
+        case 20: return "tensor-core attention, softmax of query tile A";
+        case 21: return "tensor-core attention, softmax of query tile B";
+        default: return "a device kernel";
+    }
+}
+
 void sync_check(jv_ctx* x) {
-    JV_CUDA(cudaMemcpyAsync(x->h_err.get(1), x->d_err, sizeof(int), cudaMemcpyDeviceToHost, x->stream));
+    JV_CUDA(cudaMemcpyAsync(x->h_err.get(2), x->d_err, 2 * sizeof(int), cudaMemcpyDeviceToHost, x->stream));
     JV_CUDA(cudaStreamSynchronize(x->stream));
-    int e = *x->h_err.p;
+    const int e = x->h_err.p[0], site = x->h_err.p[1];
     if (e != 0) {
-        JV_CUDA(cudaMemsetAsync(x->d_err, 0, sizeof(int), x->stream));
+        JV_CUDA(cudaMemsetAsync(x->d_err, 0, 2 * sizeof(int), x->stream));
         if (x->gemm_ctr.p) JV_CUDA(cudaMemsetAsync(x->gemm_ctr.p, 0, x->gemm_ctr.cap * sizeof(int), x->stream));
         JV_CUDA(cudaStreamSynchronize(x->stream));
         if (e == JV_ERR_DEVICE_TIMEOUT)
-            throw Error(JV_ERR_DEVICE_TIMEOUT, "a device-side wait timed out in a tensor-core GEMM");
+            throw Error(JV_ERR_DEVICE_TIMEOUT, std::string("a device-side wait timed out (") + timeout_site(site) + ")");
         throw Error(e, "a kernel reported an out-of-range index");
     }
 }
@@ -1351,8 +1371,8 @@ int jv_ctx_create(jv_model* m, int32_t initial_capacity, jv_ctx** out) {
     int rc = guarded([&] {
         set_device(m);
         JV_CUDA(cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking));
-        x->d_err = dalloc<int>(1);
-        JV_CUDA(cudaMemset(x->d_err, 0, sizeof(int)));
+        x->d_err = dalloc<int>(2);  // error code, then the site of a timeout
+        JV_CUDA(cudaMemset(x->d_err, 0, 2 * sizeof(int)));
         x->capacity = std::max(1, initial_capacity > 0 ? initial_capacity : 512);
         ctx_ensure_capacity(x, 1);
     });

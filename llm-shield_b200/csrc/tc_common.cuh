@@ -44,6 +44,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         if (gtimer() - t0 > WAIT_NS) return false;
     return true;
 }
+// A bounded wait gave up: the error word takes JV_ERR_DEVICE_TIMEOUT and the word after it
+// the first site that gave up (kernel x 16 + role), which the host names in its message.
+__device__ __forceinline__ void report_timeout(int* err, int site) {
+    atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+    atomicCAS(err + 1, 0, site);
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
