@@ -113,6 +113,14 @@ int jv_ctx_profile(jv_ctx* ctx, int32_t enable);
 int jv_ctx_profile_read(jv_ctx* ctx, int32_t kind, double* total_ms, int64_t* launches, double* flops, double* bytes);
 int jv_ctx_profile_reset(jv_ctx* ctx);
 
+/* Check of the device-timeout path (no counterpart in the reference, which has no device
+ * waits): runs one kernel whose bounded wait nothing completes. The wait gives up after
+ * bound_cycles SM clock cycles (0 < bound_cycles <= 4e9; the tensor-core kernels use 4e9,
+ * about 2 s), and the call returns JV_ERR_DEVICE_TIMEOUT with the wait named in
+ * jv_last_error(). The context stays usable: its error word is cleared and later calls run
+ * normally. Nothing faults or hangs. */
+int jv_ctx_check_wait_timeout(jv_ctx* ctx, int64_t bound_cycles);
+
 /* ---- forward passes ------------------------------------------------------------------- */
 
 /* MinistralModel.ForwardAsync(tokens, options) (MinistralModel.cs:139) — appends tokens and

@@ -23,7 +23,7 @@
 // a different position modulo 8 in the page than in the tile (a branch segment starting off a
 // multiple of 8) goes chunk by chunk through cp.async instead. Warp 10 owns TMEM and issues the
 // MMAs from an event loop: the next P V as soon as its P and V are in place, S_X(b) as soon as
-// K(b) is and the softmax has read S_X(b - 1). Every wait is bounded (2 s of %globaltimer); on
+// K(b) is and the softmax has read S_X(b - 1). Every wait is bounded (WAIT_CYCLES of the SM clock); on
 // expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
 #include "tc_common.cuh"
 
@@ -100,9 +100,10 @@ __device__ __forceinline__ float ex2(float x) {
 
 // Bounded wait taken by a whole warp: every lane gets the same verdict, so the warp stays
 // converged for the .sync.aligned tcgen05 instructions after it.
-__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
-    return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+__device__ __forceinline__ bool warp_wait_bounded(uint32_t bar, uint32_t parity, long long bound) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, bound));
 }
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) { return warp_wait_bounded(bar, parity, WAIT_CYCLES); }
 
 __device__ __forceinline__ void mbar_add_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             const int nbx[2] = {nbA, nbB};
             const int nuses = nbA + nbB;
             int u = 0;  // next P V
-            uint64_t idle_since = gtimer();
+            long long idle_since = clock64();
             while (ok && u < nuses) {
                 bool did = false;
                 {
@@ -312,10 +313,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                     }
                 }
                 if (did) {
-                    idle_since = gtimer();
+                    idle_since = clock64();
                 } else {
                     __nanosleep(20);
-                    if (gtimer() - idle_since > WAIT_NS) ok = false;
+                    if (clock64() - idle_since > WAIT_CYCLES) ok = false;
                 }
             }
             if (!ok) report_timeout(err, 16 + 3);
@@ -474,6 +475,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     }
 }
 
+// One warp waits, with the bounded wait every tensor-core kernel uses, on an mbarrier that
+// nothing arrives at; the wait gives up after `bound` cycles and reports site 33. This checks
+// the device-timeout path (error word, site, host message, a context that stays usable)
+// without faulting or hanging the GPU.
+__global__ void k_wait_check(int* err, long long bound) {
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t b = s_addr(&bar);
+    if (threadIdx.x == 0) {
+        mbar_init(b, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (!warp_wait_bounded(b, 0u, bound) && threadIdx.x == 0) report_timeout(err, 33);
+}
+
 }  // namespace
 
 constexpr size_t AT_SMEM = (size_t)7 * AT_TILE + AT_PAGES * 4 + 160 + 1024;
@@ -491,6 +507,12 @@ void launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
         configured = true;
     }
     launch_pdl(k_attn_tc, dim3(a.n_items), dim3(AT_THREADS), AT_SMEM, s, a);
+    note_launch();
+}
+
+void launch_wait_check(int* err, long long bound_cycles, cudaStream_t s) {
+    k_wait_check<<<1, 32, 0, s>>>(err, bound_cycles);
+    JV_CUDA(cudaGetLastError());
     note_launch();
 }
 

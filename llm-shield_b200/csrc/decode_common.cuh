@@ -149,17 +149,14 @@ __device__ __forceinline__ bool dg_try(uint32_t bar, uint32_t parity) {
                  : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ uint64_t dg_timer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
-    return t;
-}
-// Bounded wait (2 s) for phase `parity` of an mbarrier; false if it never completed.
+// Bounded wait for phase `parity` of an mbarrier; false if it never completed within 4e9 SM
+// clock cycles (about 2 s at the maximum clock). The SM's cycle counter only moves forward,
+// unlike %globaltimer, which the driver may step.
 __device__ __forceinline__ bool dg_wait(uint32_t bar, uint32_t parity) {
     if (dg_try(bar, parity)) return true;
-    const uint64_t t0 = dg_timer();
+    const long long t0 = clock64();
     while (!dg_try(bar, parity))
-        if (dg_timer() - t0 > 2000000000ull) return false;
+        if (clock64() - t0 > 4000000000ll) return false;
     return true;
 }
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {

@@ -597,6 +597,7 @@ const char* timeout_site(int site) {
         case 19: return "tensor-core attention, MMA issuer";
         case 20: return "tensor-core attention, softmax of query tile A";
         case 21: return "tensor-core attention, softmax of query tile B";
+        case 33: return "the wait check, which nothing completes";
         default: return "a device kernel";
     }
 }
@@ -1459,6 +1460,17 @@ int jv_ctx_profile_reset(jv_ctx* x) {
         x->prof_launches[k] = 0;
     }
     return JV_OK;
+}
+
+int jv_ctx_check_wait_timeout(jv_ctx* x, int64_t bound_cycles) {
+    if (!x) return set_error(JV_ERR_ARG, "NULL context");
+    if (bound_cycles <= 0 || bound_cycles > 4000000000ll)
+        return set_error(JV_ERR_RANGE, "bound_cycles must be in (0, 4e9]");
+    return guarded([&] {
+        set_device(x->m);
+        launch_wait_check(x->d_err, (long long)bound_cycles, x->stream);
+        sync_check(x);
+    });
 }
 
 int jv_forward(jv_ctx* x, const int32_t* tokens, int32_t n, float* logits) {

@@ -7,7 +7,12 @@
 namespace jv {
 namespace {
 
-constexpr uint64_t WAIT_NS = 2000000000ull;
+// Bound of every wait, in SM clock cycles (%clock64): about 2 s at the 1.965 GHz maximum,
+// longer at lower clocks. The cycle counter of the SM running the thread only moves forward;
+// %globaltimer is not used for bounds, since a step of it (the driver may re-synchronise it
+// with the host clock) would end a wait early, and a backward step would underflow the
+// elapsed-time difference.
+constexpr long long WAIT_CYCLES = 4000000000ll;
 
 __device__ __forceinline__ uint32_t s_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -31,17 +36,12 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ uint64_t gtimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
-    return t;
-}
-// Bounded wait: false after ~2 s without the phase completing.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait: false after `bound` cycles without the phase completing.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long bound = WAIT_CYCLES) {
     if (mbar_try(bar, parity)) return true;
-    uint64_t t0 = gtimer();
+    const long long t0 = clock64();
     while (!mbar_try(bar, parity))
-        if (gtimer() - t0 > WAIT_NS) return false;
+        if (clock64() - t0 > bound) return false;
     return true;
 }
 // A bounded wait gave up: the error word takes JV_ERR_DEVICE_TIMEOUT and the word after it

@@ -53,6 +53,7 @@ SIGNATURES = [
     ("jv_ctx_profile_read", C.c_int, [vp, i32, C.POINTER(C.c_double), C.POINTER(i64), C.POINTER(C.c_double),
                                       C.POINTER(C.c_double)]),
     ("jv_ctx_profile_reset", C.c_int, [vp]),
+    ("jv_ctx_check_wait_timeout", C.c_int, [vp, i64]),
     ("jv_forward", C.c_int, [vp, i32p, i32, f32p]),
     ("jv_forward_selected", C.c_int, [vp, i32p, i32, i32p, i32, f32p]),
     ("jv_forward_tree", C.c_int, [vp, i32p, i32, i32p, i32p, i32, i32p, i32, f32p]),

@@ -207,6 +207,11 @@ class MinistralModel:
     def profile_reset(self) -> None:
         check(lib.jv_ctx_profile_reset(self._h))
 
+    def check_wait_timeout(self, bound_cycles: int = 20_000_000) -> None:
+        """Run one device wait that nothing completes; raises DeviceTimeoutError once its bound
+        (SM clock cycles) runs out, after which the context is usable again."""
+        check(lib.jv_ctx_check_wait_timeout(self._h, int(bound_cycles)))
+
     def profile_read(self, kind: str) -> dict:
         ms, n, fl, by = C.c_double(), C.c_int64(), C.c_double(), C.c_double()
         check(lib.jv_ctx_profile_read(self._h, self.PROFILE_KINDS[kind], C.byref(ms), C.byref(n), C.byref(fl),

@@ -257,6 +257,22 @@ def test_errors_map_to_the_reference_exceptions(small, tmp_path):
         jv.Model(short)
 
 
+def test_a_device_wait_that_runs_out_reports_and_leaves_the_context_usable(small):
+    """The bounded-wait path of the tensor-core kernels: a wait that nothing completes gives
+    up after its bound, the call raises the device-timeout error naming the wait, and the
+    next forward on the same context is bit-identical to one before it."""
+    prompt = [1] + toks(90, 8)
+    with ctx(small) as c:
+        before = c.forward(prompt)
+        c.kv_cache.reset()
+        with pytest.raises(jv.DeviceTimeoutError, match="wait check"):
+            c.check_wait_timeout(20_000_000)  # ~10 ms of SM clock
+        with pytest.raises(jv.ArgumentOutOfRangeError):
+            c.check_wait_timeout(0)
+        after = c.forward(prompt)
+        assert before.tobytes() == after.tobytes()
+
+
 def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
     """The tcgen05 GEMM against a CUDA-core product over the same fp16 operands, at every real
     matrix shape: only the accumulation order differs."""
