@@ -117,6 +117,23 @@ struct TcParams {
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+// The four epilogue warps' joint verdict (named barrier 1 with an AND reduction), so that on a
+// timeout all of them leave the unit loop together and none waits at epi_bar for the others.
+__device__ __forceinline__ bool epi_all(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n.reg .pred q, o;\nsetp.ne.u32 q, %1, 0;\nbar.red.and.pred o, 1, 128, q;\nselp.u32 %0, 1, 0, o;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)p)
+        : "memory");
+    return r != 0;
+}
+// A bounded wait taken by a whole warp: every lane gets the same verdict, so on a timeout the
+// warp leaves together and never reaches a .sync.aligned tcgen05 instruction or a __syncwarp
+// with lanes missing.
+__device__ __forceinline__ bool warp_wait_all(uint32_t bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
 
 // Position in a ring of n mbarrier-guarded slots: slot index and the parity of its current use.
 struct Ring {
@@ -375,7 +392,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
             for (int ks = 0; ks < nks; ks++, k++) {
                 if ((k & 1) != grp) continue;
-                if (!mbar_wait(raw_full + 8 * rr.idx, rr.phase)) { ok = false; break; }
+                if (!warp_wait_all(raw_full + 8 * rr.idx, rr.phase)) { ok = false; break; }
                 const uint8_t* raw = Rs + rr.idx * cb;
                 uint4 v[8];
 #pragma unroll
@@ -384,7 +401,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 if (lane == 0) mbar_arrive(raw_empty + 8 * rr.idx);
                 rr.next();
                 rr.next();
-                if (!mbar_wait(st_empty + 8 * rs.idx, rs.phase ^ 1u)) { ok = false; break; }
+                if (!warp_wait_all(st_empty + 8 * rs.idx, rs.phase ^ 1u)) { ok = false; break; }
                 uint8_t* A = As + rs.idx * 16384 + a_off;
 #pragma unroll
                 for (int it = 0; it < 8; it++) *(uint4*)(A + it * 16 * 128) = v[it];
@@ -408,10 +425,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             int tile, tt, sp;
             unit_coords(u, splits, ttiles, tile, tt, sp);
             const int t0 = tt * bn, ab = i & 1;
-            const bool ready = mbar_wait(acc_full + 8 * ab, (uint32_t)((i >> 1) & 1));
+            const bool w = warp_wait_all(acc_full + 8 * ab, (uint32_t)((i >> 1) & 1));
+            const bool ready = counter_split ? epi_all(w) : w;
             tc_fence_after();
             if (!ready) {
-                report_timeout(g_err, 7);
+                if (lane == 0) report_timeout(g_err, 7);
                 break;
             }
             const uint32_t tacc = tmem + (uint32_t)(ab * ncols) + ((uint32_t)(q * 32) << 16);
@@ -460,7 +478,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         unit_coords(ul, splits, ttiles, tile, tt, sp);
         const int ab = il & 1, q = warp & 3, grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
         pdl_wait();
-        const bool ready = mbar_wait(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
+        const bool ready = warp_wait_all(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
         tc_fence_after();
         if (ready) {
             const int t0 = tt * bn;

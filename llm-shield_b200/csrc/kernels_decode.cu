@@ -121,11 +121,14 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
             for (int i = 0; i < 32; i++) s = __fadd_rn(s, p[i]);
             sx[e] = s;
         }
-    __syncthreads();
-
-    if (nk > 0 && !dg_wait(bar, 0)) {
+    // x staged for every warp, and one verdict on the copy for the whole CTA (the warps' mma.sync
+    // below needs all lanes)
+    if (!__syncthreads_and(nk == 0 || dg_wait(bar, 0))) {
         // the copy never landed: report, and do not leave while it may still be writing
-        if (threadIdx.x == 0) atomicExch(a.err, JV_ERR_DEVICE_TIMEOUT);
+        if (threadIdx.x == 0) {
+            atomicExch(a.err, JV_ERR_DEVICE_TIMEOUT);
+            atomicCAS(a.err + 1, 0, 49);
+        }
         dg_wait(bar, 0);
         return;
     }

@@ -598,6 +598,7 @@ const char* timeout_site(int site) {
         case 20: return "tensor-core attention, softmax of query tile A";
         case 21: return "tensor-core attention, softmax of query tile B";
         case 33: return "the wait check, which nothing completes";
+        case 49: return "decode matvec, weight-slice copy";
         default: return "a device kernel";
     }
 }
