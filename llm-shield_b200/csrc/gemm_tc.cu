@@ -27,8 +27,8 @@
 // therefore does not depend on BN, its column in the tile, or the other tokens of the call
 // (the property of PanelGemmTests.cs:61-74).
 //
-// Every mbarrier wait is bounded (WAIT_CYCLES of the SM clock, about 2 s). On expiry the thread
-// sets the error word and its role stops; the others then time out in turn; the producer
+// Every mbarrier wait is bounded (WAIT_CYCLES of the SM clock, about 2 s), with one verdict per
+// warp. On expiry the warp sets the error word and its role stops; the others then time out in turn; the producer
 // waits (bounded) for its copies in flight, the MMA lane drains its own MMAs, and the CTA
 // frees its TMEM and returns. No cluster launch and no multicast: nothing here reads another
 // GPU's memory.
