@@ -57,6 +57,12 @@ def test_error_paths_return_statuses():
     else:
         with pytest.raises(jv.GgufIOError):
             jv.Model("/nonexistent.gguf")
+    # context entry points check their handle before touching a device
+    from jevstral_b200._lib import JV_ERR_ARG, lib
+
+    assert lib.jv_ctx_check_wait_timeout(None, 1000) == JV_ERR_ARG
+    assert lib.jv_ctx_profile(None, 1) == JV_ERR_ARG
+    assert b"NULL" in lib.jv_last_error()
 
 
 def test_token_layout_restatement_matches_the_reference_rules():
