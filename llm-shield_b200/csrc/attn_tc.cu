@@ -494,9 +494,6 @@ __global__ void k_wait_check(int* err, long long bound) {
 
 constexpr size_t AT_SMEM = (size_t)7 * AT_TILE + AT_PAGES * 4 + 160 + 1024;
 
-// Any pass: the page table is staged in shared memory when it fits, else read by the loaders.
-bool attention_tc_fits(int, int) { return true; }
-
 void launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
     if (a.n_items <= 0) return;
     if (a.page_slots % 8 != 0 || a.page_slots > 256) throw Error(JV_ERR_UNSUPPORTED, "attention: page slots");

@@ -187,7 +187,6 @@ struct AttnArgs {
 };
 void launch_attention(const AttnArgs& a, cudaStream_t s);
 void launch_attention_tc(const AttnArgs& a, cudaStream_t s);
-bool attention_tc_fits(int max_keys, int page_slots);  // the tensor-core kernel takes this pass
 // One bounded wait that nothing completes: gives up after bound_cycles and reports site 33.
 void launch_wait_check(int* err, long long bound_cycles, cudaStream_t s);
 

@@ -913,9 +913,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     // a run per item (they share every K/V block); pairing halves the K/V traffic but doubles the
     // item's time, so a pass that fits one wave of single tiles pairs none, one that fits a wave
     // only when paired pairs its shortest tiles until it does, and a longer pass pairs them all.
-    int pass_keys = 0;
-    for (int t = 0; t < T; t++) pass_keys = std::max(pass_keys, sh[t] + (L->slot[t] - L->seg[t] + 1));
-    const bool attn_tc = !attention_on_mma_sync() && attention_tc_fits(pass_keys + 64, m->page_slots);
+    const bool attn_tc = !attention_on_mma_sync();
     std::vector<AttnItem> items;
     if (!decode) {
         struct Tile { int t0, n, lim; bool cont; };  // cont: full, and the run goes on in the next tile
