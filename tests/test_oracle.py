@@ -221,6 +221,39 @@ def test_cached_and_uncached_produce_identical_logits(small_gguf):
     assert whole.tobytes() == cached.tobytes()
 
 
+def test_a_row_after_the_prefix_is_a_causal_continuation(small_gguf):
+    """TokenLayout.Rows (MinistralModel.cs:758-780): a row whose region starts right after the
+    shared prefix sees exactly the causal context, so its last logits equal ForwardAsync's on the
+    prompt plus the row (tolerance: the reference takes its sparse per-key attention for rows of
+    fewer than 16 tokens)."""
+    prefix = [1] + _tokens(30, 5)
+    row = _tokens(4, 6)
+    with ob.OracleModel(small_gguf) as m:
+        whole = m.forward(prefix + row)
+        m.kv_reset()
+        m.forward(prefix, logits=False)
+        rows = m.forward_rows(len(prefix), [len(prefix)], [0], [row])
+    close(whole, rows[0], 1e-5, "row vs causal")
+
+
+def test_rows_do_not_see_each_other(small_gguf):
+    """Each row attends to the shared prefix and its own region only: a row's logits do not
+    depend on which other rows share the pass (bit-identical while the head stays a GEMM, i.e.
+    at least two rows: one output takes RunRowsFloat, QuantMatMul.cs:90-95,140-176)."""
+    prefix = [1] + _tokens(30, 7)
+    p = len(prefix)
+    rows = [_tokens(n, 8 + i) for i, n in enumerate((3, 5, 2))]
+    bases = [p + 32 * i for i in range(3)]
+    with ob.OracleModel(small_gguf) as m:
+        m.forward(prefix, logits=False)
+        together = m.forward_rows(p, bases, [0, 0, 0], rows)
+        m.kv_reset()
+        m.forward(prefix, logits=False)
+        pair = m.forward_rows(p, [bases[2], bases[1]], [0, 0], [rows[2], rows[1]])
+    assert pair[0].tobytes() == together[2].tobytes()
+    assert pair[1].tobytes() == together[1].tobytes()
+
+
 def test_snapshot_rejects_more_than_is_cached(small_gguf):
     with ob.OracleModel(small_gguf) as m:
         m.forward([1, 2000], logits=False)
