@@ -351,6 +351,55 @@ def test_tensor_core_attention_matches_the_mma_sync_attention(model_factory):
     assert np.abs(tc["z"] - mma["z"]).max() < 2e-2
 
 
+def test_batched_rows_match_the_oracle(small):
+    """ForwardRowsAsync (MinistralModel.cs:282-294, TokenLayout.Rows :758-780): rows that each
+    append to their own KV region after a shared prefix, stepped together as ReasoningDecider's
+    batched decode does. Full-vocabulary logits of every row's last token against the oracle for
+    a first multi-token step and a one-token-per-row step; a row gives bit-identical logits in a
+    four-row and a two-row pass (the head stays a GEMM from two rows up)."""
+    prefix = [1] + toks(40, 21)
+    p = len(prefix)
+    bases = [p + 64 * r for r in range(4)]
+    first = [toks(n, 30 + r) for r, n in enumerate((3, 1, 6, 2))]
+    lengths = [len(f) for f in first]
+    with ctx(small) as c, ctx(small) as d, ob.OracleModel(small.path) as o:
+        c.prefill(prefix)
+        o.forward(prefix, logits=False)
+        got = c.forward_rows(p, bases, [0] * 4, first)
+        want = o.forward_rows(p, bases, [0] * 4, first)
+        assert got.shape == want.shape == (4, SMALL_CFG.vocab)
+        for r in range(4):
+            assert rel_l2(got[r], want[r]) < HIDDEN_TOL, r
+            assert int(np.argmax(got[r])) == int(np.argmax(want[r])), r
+        nxt = [[int(np.argmax(want[r]))] for r in range(4)]
+        got2 = c.forward_rows(p, bases, lengths, nxt)
+        want2 = o.forward_rows(p, bases, lengths, nxt)
+        for r in range(4):
+            assert rel_l2(got2[r], want2[r]) < HIDDEN_TOL, r
+            assert int(np.argmax(got2[r])) == int(np.argmax(want2[r])), r
+        # rows 2 and 0 in a pass of their own: the same bits as in the four-row pass
+        d.prefill(prefix)
+        two = d.forward_rows(p, [bases[2], bases[0]], [0, 0], [first[2], first[0]])
+        assert two[0].tobytes() == got[2].tobytes()
+        assert two[1].tobytes() == got[0].tobytes()
+
+
+def test_tree_logits_match_the_oracle(small):
+    """ForwardTreeLogitsAsync (MinistralModel.cs:227-255): full-vocabulary logits at every branch
+    token, each against the oracle's logits for the trunk followed by that branch prefix."""
+    trunk = [1] + toks(30, 23)
+    branches = [toks(n, 40 + i) for i, n in enumerate((3, 1, 4))]
+    with ctx(small) as c, ob.OracleModel(small.path) as o:
+        got = c.forward_tree_logits(trunk, branches)
+        assert [len(g) for g in got] == [len(b) for b in branches]
+        for b, br in enumerate(branches):
+            for i in range(len(br)):
+                o.kv_reset()
+                want = o.forward_tree(trunk, [br[: i + 1]], None)[0]
+                assert rel_l2(got[b][i], want) < HIDDEN_TOL, (b, i)
+                assert int(np.argmax(got[b][i])) == int(np.argmax(want)), (b, i)
+
+
 def test_decision_batch_is_bit_identical_to_single_decisions(small):
     """jv_decide_batch: each decision of a batch (trunks of different lengths, branches of odd
     lengths so segments start off multiples of 8, one decision without a trunk) gives exactly the
