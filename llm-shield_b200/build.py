@@ -3,6 +3,7 @@
 libjv.so     CUDA kernels for sm_100a + the host runtime behind include/jv.h
              (nvcc -gencode arch=compute_100a,code=sm_100a, static CUDA runtime).
 libjvsynth.so  the random-weight GGUF filler used by the tests and the benchmark.
+jvsynth        the same filler as a stand-alone program (the benchmark's reference arm).
 
 Usage: python llm-shield_b200/build.py [--verbose] [--ptxas]
 """
@@ -20,6 +21,7 @@ CSRC = PKG / "csrc"
 OUT = PKG / "_build"
 LIB = PKG / "libjv.so"
 SYNTH = PKG / "libjvsynth.so"
+SYNTH_EXE = PKG / "jvsynth"
 
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -73,6 +75,9 @@ def build(verbose: bool = False, ptxas: bool = False, force: bool = False) -> Pa
     synth_src = CSRC / "synth" / "gguf_synth.cpp"
     if force or _stale(SYNTH, [synth_src]):
         _run(["g++", "-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math", "-shared", "-o", str(SYNTH),
+              str(synth_src), "-lpthread"], verbose)
+    if force or _stale(SYNTH_EXE, [synth_src]):
+        _run(["g++", "-O3", "-std=c++17", "-DJVS_MAIN", "-ffp-contract=off", "-fno-fast-math", "-o", str(SYNTH_EXE),
               str(synth_src), "-lpthread"], verbose)
     return LIB
 

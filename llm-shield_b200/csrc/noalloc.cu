@@ -20,8 +20,15 @@
 //  * The first call on a device does a one-time set-up on that device: it looks up the
 //    array's device address with cudaGetSymbolAddress while that device is current. Make the
 //    first call on each device before any stream capture begins.
+//  * The address is remembered per CUDA context (the context current at the call), so a
+//    device reset, after which the device gets a new context, is followed by a fresh look-up
+//    on the next call instead of a stale address.
+#include <cuda.h>
+
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "jv_internal.h"
 
@@ -33,26 +40,48 @@ static __device__ __align__(256) float g_qmatvec_scratch[JV_QMATVEC_SCRATCH_FLOA
 
 namespace {
 
-constexpr int kMaxDevices = 64;
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The CUDA context current on this thread, or nullptr before the runtime has set one up, read
+// through the driver entry point the runtime hands out (no link against libcuda is needed).
+CUcontext current_context() {
+    static CtxGetCurrentFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        cudaGetLastError();
+        return (CtxGetCurrentFn)f;
+    }();
+    if (!fn) throw Error(JV_ERR_DEVICE, "cuCtxGetCurrent is not available from the CUDA driver");
+    CUcontext c = nullptr;
+    if (fn(&c) != CUDA_SUCCESS) throw Error(JV_ERR_DEVICE, "cuCtxGetCurrent failed");
+    return c;
+}
 
 struct ScratchAddress {
     std::mutex mu;
-    float* ptr[kMaxDevices] = {};
-    // The device address of g_qmatvec_scratch on `dev`, which must be the current device.
-    float* get(int dev) {
-        if (dev < 0 || dev >= kMaxDevices) throw Error(JV_ERR_ARG, "device index out of range");
+    std::vector<std::pair<CUcontext, float*>> known;
+    // The device address of g_qmatvec_scratch in the current context. The first call in a
+    // context looks it up (cudaGetSymbolAddress, which also sets up the current device's
+    // context if nothing has yet) and remembers it for that context.
+    float* get() {
         std::lock_guard<std::mutex> g(mu);
-        if (!ptr[dev]) {
-            void* p = nullptr;
-            cudaError_t e = cudaGetSymbolAddress(&p, g_qmatvec_scratch);
-            if (e != cudaSuccess || !p) {
-                cudaGetLastError();
-                throw Error(JV_ERR_DEVICE, std::string("cudaGetSymbolAddress of the matvec scratch: ") +
-                                               cudaGetErrorString(e));
-            }
-            ptr[dev] = (float*)p;
+        if (CUcontext c = current_context())
+            for (auto& k : known)
+                if (k.first == c) return k.second;
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_qmatvec_scratch);
+        if (e != cudaSuccess || !p) {
+            cudaGetLastError();
+            throw Error(JV_ERR_DEVICE, std::string("cudaGetSymbolAddress of the matvec scratch: ") +
+                                           cudaGetErrorString(e));
         }
-        return ptr[dev];
+        CUcontext c = current_context();
+        if (!c) throw Error(JV_ERR_DEVICE, "no CUDA context is current after the scratch look-up");
+        known.emplace_back(c, (float*)p);
+        return (float*)p;
     }
 };
 ScratchAddress g_scratch;
@@ -74,7 +103,7 @@ extern "C" int jv_qmatvec_noalloc(int32_t type, const void* tiled, int32_t rows,
                                           std::to_string(splits) + " k-splits need " + std::to_string(need) +
                                           " scratch floats; the fixed scratch holds " +
                                           std::to_string(JV_QMATVEC_SCRATCH_FLOATS));
-        float* part = g_scratch.get(dev);
+        float* part = g_scratch.get();
         launch_gemv(w, x, part, splits, (cudaStream_t)stream);
         launch_gemv_reduce(part, splits, rows, y, EPI_STORE, (cudaStream_t)stream);
         JV_CUDA(cudaGetLastError());

@@ -8,6 +8,7 @@
 // forward() = the private ForwardAsync (MinistralModel.cs:301-435) as a fixed sequence of
 //             kernel launches on the context's stream.
 #include <algorithm>
+#include <cstddef>
 #include <atomic>
 #include <cmath>
 #include <cstring>
@@ -21,6 +22,15 @@
 #include "jv_internal.h"
 
 using namespace jv;
+
+// The structs of the ABI as the C# binding mirrors them (LayoutKind.Sequential, default packing):
+// a change here is a breaking change of the binding.
+static_assert(sizeof(jv_config) == 68, "jv_config: 12 int32 then 5 float");
+static_assert(offsetof(jv_config, weight_type) == 44 && offsetof(jv_config, eps) == 48, "jv_config field offsets");
+static_assert(offsetof(jv_config, temperature_scale) == 64, "jv_config field offsets");
+static_assert(sizeof(jv_layout) == 56, "jv_layout: 5 pointers then 3 int32 (+4 padding)");
+static_assert(offsetof(jv_layout, outputs) == 32 && offsetof(jv_layout, n_outputs) == 40, "jv_layout field offsets");
+static_assert(offsetof(jv_layout, end) == 44 && offsetof(jv_layout, sparse) == 48, "jv_layout field offsets");
 
 namespace {
 

@@ -6,6 +6,10 @@
 // (gguf/quants.py 0.19.0, Q8_0/Q4_0/Q5_1 quantize_blocks), which the reference's converter
 // uses (tools/convert_shieldstral_to_gguf.py:285-292): the same fp32 input gives the same
 // bytes, checked by tests/test_synth.py against the package itself.
+//
+// Built twice: as libjvsynth.so (called in-process through ctypes) and, with -DJVS_MAIN, as the
+// stand-alone `jvsynth` program, which fills a file whose header is already written. The
+// benchmark's reference arm uses the program, so that process loads no library of this package.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -164,3 +168,60 @@ int64_t jvs_fill(uint8_t* dst, int type, int64_t rows, int64_t cols, uint64_t se
     return rows * rb;
 }
 }
+
+#ifdef JVS_MAIN
+#include <cstdio>
+#include <cstdlib>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+// jvsynth FILE TYPE SEED STD THREADS, then one line per matrix on stdin: "TID OFFSET ROWS COLS"
+// (OFFSET = the tensor's absolute byte offset in FILE). Exit status 0 when every matrix was filled.
+int main(int argc, char** argv) {
+    if (argc != 6) {
+        std::fprintf(stderr, "usage: jvsynth FILE TYPE SEED STD THREADS < 'TID OFFSET ROWS COLS' lines\n");
+        return 2;
+    }
+    const int type = std::atoi(argv[2]);
+    const uint64_t seed = std::strtoull(argv[3], nullptr, 10);
+    const float stdev = std::strtof(argv[4], nullptr);
+    const int threads = std::atoi(argv[5]);
+    int fd = open(argv[1], O_RDWR);
+    if (fd < 0) {
+        std::perror(argv[1]);
+        return 1;
+    }
+    struct stat st;
+    if (fstat(fd, &st) != 0) {
+        std::perror("fstat");
+        return 1;
+    }
+    void* base = mmap(nullptr, (size_t)st.st_size, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    if (base == MAP_FAILED) {
+        std::perror("mmap");
+        return 1;
+    }
+    unsigned tid;
+    long long off, rows, cols;
+    int rc = 0;
+    while (std::scanf("%u %lld %lld %lld", &tid, &off, &rows, &cols) == 4) {
+        const int64_t rb = type == 0 ? cols * 4 : cols / 32 * block_bytes(type);
+        if (off < 0 || rows <= 0 || off + rows * rb > (long long)st.st_size) {
+            std::fprintf(stderr, "jvsynth: tensor %u does not fit the file\n", tid);
+            rc = 1;
+            break;
+        }
+        if (jvs_fill((uint8_t*)base + off, type, rows, cols, seed, tid, stdev, threads) != rows * rb) {
+            std::fprintf(stderr, "jvsynth: tensor %u: bad type or shape\n", tid);
+            rc = 1;
+            break;
+        }
+    }
+    if (msync(base, (size_t)st.st_size, MS_SYNC) != 0) rc = 1;
+    munmap(base, (size_t)st.st_size);
+    close(fd);
+    return rc;
+}
+#endif

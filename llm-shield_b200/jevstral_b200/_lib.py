@@ -97,7 +97,9 @@ class JvError(Exception):
         self.code = code
 
 
-# The reference's exception types (see the C# mapping in INTEGRATION.md).
+# The reference's exception types: ArgumentException, ArgumentOutOfRangeException,
+# InvalidDataException, IOException, NotSupportedException, OperationCanceledException, and a
+# device failure, which has no counterpart in the managed reference.
 class ArgumentError(JvError, ValueError): ...
 class ArgumentOutOfRangeError(JvError, IndexError): ...
 class InvalidDataError(JvError): ...

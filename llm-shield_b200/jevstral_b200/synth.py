@@ -8,7 +8,10 @@ quantization rules (gguf.quants, the converter's quantizer):
     the small test models;
   * backend="fast": weights from libjvsynth's counter-based generator, quantized by its
     restatement of the same rules, written straight into a memory-mapped file — seconds
-    for the full 3B model instead of minutes.
+    for the full 3B model instead of minutes;
+  * backend="exe": the same bytes as "fast", filled by the stand-alone `jvsynth` program in a
+    child process, so the calling process loads no library of this package (the benchmark's
+    reference arm imports this file on its own, outside the package).
 Norm gains are 1.0 in F32, the LM head is tied to token_embd, and the vocabulary is a
 placeholder token list with "yes" at 13059 and "no" at 2649 (the real ids) when it fits.
 """
@@ -17,6 +20,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 import struct
+import subprocess
 from dataclasses import dataclass
 from pathlib import Path
 from typing import Dict, List, Tuple
@@ -25,6 +29,7 @@ import numpy as np
 
 PKG = Path(__file__).resolve().parent.parent
 SYNTH_LIB = PKG / "libjvsynth.so"
+SYNTH_EXE = PKG / "jvsynth"
 
 QTYPES = {"F32": 0, "Q4_0": 2, "Q5_1": 7, "Q8_0": 8}
 BLOCK_BYTES = {0: 4, 2: 18, 7: 24, 8: 34}
@@ -179,20 +184,32 @@ def write_random_gguf(path, cfg: SynthConfig = MINISTRAL_3B, qtype: str = "Q8_0"
         f.write(header)
         f.truncate(total)
     mm = np.memmap(tmp, dtype=np.uint8, mode="r+")
-    lib = _synth_lib()
     threads = os.cpu_count() or 1
+    jobs = []
     for tid, ((name, shape, is_mat), o) in enumerate(zip(plan, offsets)):
         base = data_start + o
         if not is_mat:
             mm[base:base + 4 * shape[0]] = np.ones(shape[0], dtype=np.float32).view(np.uint8)
             continue
-        rows, cols = shape
-        ptr = mm.ctypes.data + base
-        n = lib.jvs_fill(C.c_void_p(ptr), t, rows, cols, seed, tid, std, threads)
-        if n != _row_bytes(t, cols) * rows:
-            raise RuntimeError(f"jvs_fill failed for {name}")
-    mm.flush()
-    del mm
+        jobs.append((tid, base, shape[0], shape[1], name))
+    if backend == "exe":
+        mm.flush()
+        del mm
+        if not SYNTH_EXE.exists():
+            raise FileNotFoundError(f"{SYNTH_EXE} is not built; run `python llm-shield_b200/build.py`")
+        plan_text = "".join(f"{tid} {base} {rows} {cols}\n" for tid, base, rows, cols, _ in jobs)
+        r = subprocess.run([str(SYNTH_EXE), str(tmp), str(t), str(seed), repr(float(std)), str(threads)],
+                           input=plan_text, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"jvsynth failed ({r.returncode}): {r.stderr.strip()}")
+    else:
+        lib = _synth_lib()
+        for tid, base, rows, cols, name in jobs:
+            n = lib.jvs_fill(C.c_void_p(mm.ctypes.data + base), t, rows, cols, seed, tid, std, threads)
+            if n != _row_bytes(t, cols) * rows:
+                raise RuntimeError(f"jvs_fill failed for {name}")
+        mm.flush()
+        del mm
     os.replace(tmp, path)
     return path
 

@@ -90,3 +90,34 @@ def test_decider_tail_matches_the_reference_formulas():
     p = decision_probs(z, 2.0)
     e = np.exp(z / 2 - (z / 2).max())
     assert np.allclose(p, e / e.sum(), rtol=1e-6)
+
+
+def test_struct_layouts_match_the_binding(tmp_path):
+    """jv_config and jv_layout as a C compiler lays them out (the layout the C# structs mirror
+    with LayoutKind.Sequential) against the ctypes mirror and the fixed sizes the library
+    asserts at compile time (runtime.cu)."""
+    import ctypes
+    import subprocess
+
+    from jevstral_b200._lib import JvConfig, JvLayout
+
+    fields = {"jv_config": [f for f, _ in JvConfig._fields_], "jv_layout": [f for f, _ in JvLayout._fields_]}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "jv.h"', "int main(void) {"]
+    for st, names in fields.items():
+        lines.append(f'    printf("{st} sizeof %zu\\n", sizeof({st}));')
+        for n in names:
+            lines.append(f'    printf("{st} {n} %zu\\n", offsetof({st}, {n}));')
+    lines += ["    return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        st, name, val = line.split()
+        got[(st, name)] = int(val)
+    for st, cls in (("jv_config", JvConfig), ("jv_layout", JvLayout)):
+        assert got[(st, "sizeof")] == ctypes.sizeof(cls), st
+        for n in fields[st]:
+            assert got[(st, n)] == getattr(cls, n).offset, (st, n)
+    assert got[("jv_config", "sizeof")] == 68 and got[("jv_layout", "sizeof")] == 56
