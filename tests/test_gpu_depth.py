@@ -91,7 +91,7 @@ def test_c1_prefill_every_layer_matches_the_oracle(full_model, qtype):
     gpu, cpu = {}, {}
     with jv.Model(path, kv_pool_mb=1024) as m, jv.MinistralModel(m) as c:
         c.set_activation_sink(keep_layer_outputs(gpu))
-        c.prefill(prompt)
+        logits_gpu = c.forward(prompt)
         c.set_activation_sink(None)
         c.kv_cache.reset()
         v_gpu = c.forward_selected(prompt, ROWS)
@@ -99,8 +99,11 @@ def test_c1_prefill_every_layer_matches_the_oracle(full_model, qtype):
         logits = o.forward(prompt, sink=keep_layer_outputs(cpu))
     worst = check_layers(gpu, cpu)
     assert rel_l2(gpu["final_norm"][-1], cpu["final_norm"][-1]) < HIDDEN_TOL
+    assert rel_l2(logits_gpu, logits) < HIDDEN_TOL
     v_cpu = logits[ROWS]
     assert np.abs(v_gpu - v_cpu).max() < Z_TOL, (v_gpu, v_cpu, worst)
+    print(f"C1 {qtype}: worst layer rel-L2 {worst:.2e}, logits rel-L2 {rel_l2(logits_gpu, logits):.2e}, "
+          f"verdict |d| {np.abs(v_gpu - v_cpu).max():.2e}")
 
 
 def test_c2_tree_decision_matches_the_oracle(full_model):
@@ -119,8 +122,9 @@ def test_c2_tree_decision_matches_the_oracle(full_model):
         v_gpu = c.forward_tree(trunk, branches, ROWS)
     with ob.OracleModel(path) as o:
         v_cpu = o.forward_tree(trunk, branches, ROWS, sink=keep_layer_outputs(cpu))
-    check_layers(gpu, cpu)
-    check_margins(v_gpu, v_cpu)
+    worst = check_layers(gpu, cpu)
+    err = check_margins(v_gpu, v_cpu)
+    print(f"C2: worst layer rel-L2 {worst:.2e}, max |dz| {err:.2e}")
 
 
 def test_c3_long_trunk_and_reused_trunk_match_the_oracle(full_model):
@@ -147,6 +151,7 @@ def test_c3_long_trunk_and_reused_trunk_match_the_oracle(full_model):
         err = float(np.abs(got.margins - z_cpu).max())
         assert err < Z_TOL, (err, got.margins, z_cpu)
         assert int(np.argmax(got.margins)) == int(np.argmax(z_cpu))
+        print(f"C3 decision (cached {got.cached_tokens}): max |dz| {err:.2e}")
 
 
 def test_c4_greedy_decode_matches_the_oracle(full_model):
@@ -164,11 +169,14 @@ def test_c4_greedy_decode_matches_the_oracle(full_model):
         c.kv_cache.truncate(len(prompt))
         fed = [first] + chosen[:-1]
         logits_gpu = [c.forward([t]) for t in fed]
+    worst = 0.0
     with ob.OracleModel(path, 1280) as o:
         o.forward(prompt, logits=False)
         for step, (t, want_tok, lg) in enumerate(zip(fed, chosen, logits_gpu)):
             lo = o.forward([t])
+            worst = max(worst, rel_l2(lg, lo))
             assert rel_l2(lg, lo) < HIDDEN_TOL, step
             top = int(np.argmax(lo))
             assert top == want_tok or lo[top] - lo[want_tok] < Z_TOL, (step, top, want_tok, lo[top] - lo[want_tok])
             assert int(np.argmax(lg)) == want_tok, step  # the loop and the single-token call agree
+    print(f"C4: {steps} greedy steps, worst logits rel-L2 {worst:.2e}, tokens {chosen}")
