@@ -159,6 +159,21 @@ __device__ __forceinline__ bool dg_wait(uint32_t bar, uint32_t parity) {
         if (clock64() - t0 > 4000000000ll) return false;
     return true;
 }
+// This CTA's share of an L2 prefetch of [pf, pf + bytes) (bytes a multiple of 16) split evenly
+// over the grid's CTAs: pieces of at most 64 KB, issued by the calling thread; nothing waits for
+// them. A later kernel of the step then finds its weights in L2 instead of HBM, while HBM keeps
+// streaming across the boundaries between launches.
+__device__ __forceinline__ void dg_prefetch_share(const uint8_t* pf, int64_t bytes) {
+    if (!pf || bytes <= 0) return;
+    const int64_t ncta = (int64_t)gridDim.x * gridDim.y;
+    const int64_t cta = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+    const int64_t share = ((bytes + ncta - 1) / ncta + 15) & ~(int64_t)15;
+    const int64_t b1 = min(bytes, (cta + 1) * share);
+    for (int64_t o = cta * share; o < b1; o += 65536) {
+        const uint32_t n = (uint32_t)min((int64_t)65536, b1 - o);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(pf + o), "r"(n) : "memory");
+    }
+}
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }

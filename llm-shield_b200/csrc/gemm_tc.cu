@@ -499,26 +499,388 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     }
 }
 
-// Token tiles of a pass of T tokens: ceil(T / 256) balanced tiles, multiples of 16. From 128 to
-// 256 tokens a product with few row tiles (the 48-tile QKV, the split 24-tile projections) takes
-// two tiles of T / 2 so that it still covers most SMs; one with many row tiles (gate/up, the
-// head) keeps one tile of T, which halves its MMA instructions and still fills the SMs. tpad is
-// a multiple of both.
+// ------------------------------------------------------------------------------------------------
+// k_gemm_tm: the same product with the decoded weights (the MMA's A operand) in tensor memory.
+//
+// In k_gemm_tc every k step moves ~113 KB through shared memory at N = 256 (raw chunk in and
+// out, decoded weights in and out, the activation tile in and the tensor core's reads of both
+// operands), which at ~128 B per clock is ~880 clocks against the 512 the four MMAs need; the
+// tensor pipe idles half the time. Here:
+//   * the decoder warps read each weight row straight from global memory (L2, kept ahead by a
+//     bulk L2 prefetch) into registers — no raw chunk in shared memory;
+//   * they write the decoded fp16 row into TMEM (tcgen05.st, one row per lane, fp16 pairs (2j,
+//     2j + 1) in column j) and the MMA reads A from there (tcgen05.mma ... [d], [a], b_desc);
+//   * shared memory holds only the activation ring (7 stages at N = 224).
+// TMEM (512 columns): accumulator 0 in [0, bn), A stage 0 in [224, 256), accumulator 1 in
+// [256, 256 + bn), A stage 1 in [480, 512); so bn <= 224. Decoder group g (warps 8 + 4g ..
+// 11 + 4g, one TMEM lane quarter each) decodes the k steps g, g + 2, ... of the CTA's sequence
+// into A stage g. Everything else (units, epilogues, bounded waits, batch invariance) is k_gemm_tc's.
+constexpr int TM_MAX_BN = 224;
+constexpr int TM_PREFETCH = 24;  // own k steps whose weight chunks a decoder group keeps in flight to L2
+
+__device__ __forceinline__ uint32_t tm_a_col(int g) { return 224u + 256u * (uint32_t)g; }
+
+// D (TMEM) (+)= A (TMEM, fp16 pairs two to a column) x B (shared-memory descriptor).
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "r"(tmem_a), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// 32 consecutive TMEM columns of this warp's 32 lanes, one row of 64 fp16 weights per lane.
+__device__ __forceinline__ void tm_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,"
+        "%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tm_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+// The raw bytes of one weight row (64 weights = two 32-wide blocks) of one chunk, in registers.
+template <int TYPE>
+struct RowRaw {
+    uint4 q[TYPE == T_Q8_0 ? 4 : 2];  // Q8_0: 64 int8; Q4_0 / Q5_1: two blocks of 16 nibble-pair bytes
+    uint32_t d;                       // fp16 d of blocks 0 and 1
+    uint32_t m;                       // Q5_1: fp16 m of blocks 0 and 1
+    uint2 qh;                         // Q5_1: the fifth bits of blocks 0 and 1
+};
+
+template <int TYPE>
+__device__ __forceinline__ void row_load(RowRaw<TYPE>& r, const uint8_t* __restrict__ chunk, int row) {
+    if (TYPE == T_Q8_0) {
+        const uint4* q = (const uint4*)(chunk + row * 64);
+#pragma unroll
+        for (int i = 0; i < 4; i++) r.q[i] = __ldg(q + i);
+        r.d = __ldg((const uint32_t*)(chunk + 8192 + row * 4));
+    } else {
+        const uint4* q = (const uint4*)(chunk + row * 32);
+        r.q[0] = __ldg(q);
+        r.q[1] = __ldg(q + 1);
+        if (TYPE == T_Q4_0) {
+            r.d = __ldg((const uint32_t*)(chunk + 4096 + row * 4));
+        } else {
+            r.qh = __ldg((const uint2*)(chunk + 4096 + row * 8));
+            r.d = __ldg((const uint32_t*)(chunk + 5120 + row * 4));
+            r.m = __ldg((const uint32_t*)(chunk + 5632 + row * 4));
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t w_at(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// The row's 64 weights decoded to fp16 with exactly decode8's arithmetic: column j of the
+// result holds weights (2j, 2j + 1).
+template <int TYPE>
+__device__ __forceinline__ void row_decode(const RowRaw<TYPE>& r, uint32_t (&v)[32]) {
+    const __half2 d0 = __half2half2(__ushort_as_half((unsigned short)(r.d & 0xFFFFu)));
+    const __half2 d1 = __half2half2(__ushort_as_half((unsigned short)(r.d >> 16)));
+    if (TYPE == T_Q8_0) {
+        const __half2 bias = __floats2half2_rn(1152.f, 1152.f);  // 1024 + 128
+#pragma unroll
+        for (int i = 0; i < 16; i++) {  // word i = weights 4i .. 4i + 3
+            const uint32_t x = w_at(r.q[i >> 2], i & 3) ^ 0x80808080u;
+            const __half2 d = i < 8 ? d0 : d1;
+            v[2 * i] = hu(__hmul2(__hsub2(byte_pair(x, 0x4140u), bias), d));
+            v[2 * i + 1] = hu(__hmul2(__hsub2(byte_pair(x, 0x4342u), bias), d));
+        }
+        return;
+    }
+    // Q4_0 / Q5_1: block b's byte j holds weight j (low nibble) and j + 16 (high nibble).
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        const __half2 d = b ? d1 : d0;
+        __half2 m2 = __float2half2_rn(0.f);
+        uint32_t qh = 0;
+        if (TYPE == T_Q5_1) {
+            m2 = __half2half2(__ushort_as_half((unsigned short)(b ? (r.m >> 16) : (r.m & 0xFFFFu))));
+            qh = b ? r.qh.y : r.qh.x;
+        }
+#pragma unroll
+        for (int half = 0; half < 2; half++) {  // weights 16 * half .. 16 * half + 15 of the block
+#pragma unroll
+            for (int i = 0; i < 4; i++) {       // word i of the block: bytes 4i .. 4i + 3
+                uint32_t x = w_at(r.q[b], i);
+                x = half ? (x >> 4) & 0x0F0F0F0Fu : x & 0x0F0F0F0Fu;
+                const int e = 16 * half + 4 * i;  // first weight of these four within the block
+                const int col = 16 * b + e / 2;
+                if (TYPE == T_Q4_0) {
+                    const __half2 bias = __floats2half2_rn(1032.f, 1032.f);  // 1024 + 8
+                    v[col] = hu(__hmul2(__hsub2(byte_pair(x, 0x4140u), bias), d));
+                    v[col + 1] = hu(__hmul2(__hsub2(byte_pair(x, 0x4342u), bias), d));
+                } else {
+                    const uint32_t h4 = (qh >> e) & 0xFu;
+                    x |= ((h4 & 1u) << 4) | ((h4 & 2u) << 11) | ((h4 & 4u) << 18) | ((h4 & 8u) << 25);
+                    const __half2 bias = __floats2half2_rn(1024.f, 1024.f);
+                    v[col] = hu(__hfma2(__hsub2(byte_pair(x, 0x4140u), bias), d, m2));
+                    v[col + 1] = hu(__hfma2(__hsub2(byte_pair(x, 0x4342u), bias), d, m2));
+                }
+            }
+        }
+    }
+}
+
+template <int TYPE, int EPI, bool CSPLIT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tm(TcParams p) {
+    const uint8_t* __restrict__ g_w = p.w;
+    const __half* __restrict__ g_x = p.x;
+    float* __restrict__ g_y = p.y;
+    int* __restrict__ g_err = p.err;
+    __half* __restrict__ g_xs_out = p.xs_out;
+    float* g_ws = p.ws;
+    int* __restrict__ g_ctr = p.counters;
+    constexpr int epi = EPI;
+    const int ksteps = p.ksteps, T = p.T, tpad = p.tpad, bn = p.bn, ldy = p.ldy;
+    const int splits = p.splits, ttiles = p.ttiles, units = p.units, NB = p.ns;
+    const int bar_off = p.bar_off;
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t* sm = gsm_raw + ((1024u - (s_addr(gsm_raw) & 1023u)) & 1023u);
+    const int cb = chunk_bytes(TYPE);
+    uint8_t* Bs = sm;  // NB x bn*128 activation tiles
+    uint64_t* bars = (uint64_t*)(sm + bar_off);
+    // b_full (activation tile landed), b_empty (the MMA that read it completed), a_full (four
+    // decoder warps wrote the A stage), a_empty (the MMA that read the A stage completed)
+    const uint32_t b_full = s_addr(bars), b_empty = b_full + 8 * NB;
+    const uint32_t a_full = b_empty + 8 * NB, a_empty = a_full + 16;
+    const uint32_t acc_full = a_empty + 16, acc_empty = acc_full + 16, drained = acc_empty + 16;
+    uint32_t* tslot = (uint32_t*)(bars + 2 * NB + 9);
+    volatile int* last_flag = (volatile int*)(tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nks = ksteps / splits;
+    const uint32_t bbytes = (uint32_t)bn * 128u;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NB; i++) { mbar_init(b_full + 8 * i, 1); mbar_init(b_empty + 8 * i, 1); }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(a_full + 8 * i, DEC_WARPS_PER_GROUP);
+            mbar_init(a_empty + 8 * i, 1);
+            mbar_init(acc_full + 8 * i, 1);
+            mbar_init(acc_empty + 8 * i, 4);
+        }
+        mbar_init(drained, 1);
+        fence_barrier_init();
+    }
+    if (warp == 2) tmem_alloc(s_addr(tslot), 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    pdl_launch_dependents();
+
+    if (warp == 3) {
+        if (lane == 0) {  // ------------------------------------------ activation producer
+            Ring r(NB);
+            bool ok = true;
+            int issued = 0;
+            pdl_wait();
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                int tile, tt, sp;
+                unit_coords(u, splits, ttiles, tile, tt, sp);
+                const int kb = sp * nks, t0 = tt * bn;
+                const uint8_t* src = (const uint8_t*)(g_x + ((int64_t)kb * tpad + t0) * 64);
+                for (int ks = 0; ks < nks; ks++) {
+                    if (!mbar_wait(b_empty + 8 * r.idx, r.phase ^ 1u)) { ok = false; break; }
+                    mbar_expect_tx(b_full + 8 * r.idx, bbytes);
+                    bulk_g2s(s_addr(Bs + (size_t)r.idx * bbytes), src + (int64_t)ks * tpad * 128, bbytes, b_full + 8 * r.idx);
+                    r.next();
+                    issued++;
+                }
+            }
+            if (!ok) report_timeout(g_err, 2);
+            for (int i = 0; i < issued && i < NB; i++) {
+                r.prev();
+                if (!mbar_wait(b_full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // --------------------------------------------- MMA issue
+            const uint32_t idesc = idesc_f16(bn, 128);
+            Ring rb(NB);
+            bool ok = true;
+            int i = 0, k = 0;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
+                const int ab = i & 1;
+                if (!mbar_wait(acc_empty + 8 * ab, (uint32_t)((i >> 1) & 1) ^ 1u)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(ab * 256);
+                for (int ks = 0; ks < nks; ks++, k++) {
+                    const int sa = k & 1;
+                    if (!mbar_wait(a_full + 8 * sa, (uint32_t)((k >> 1) & 1)) || !mbar_wait(b_full + 8 * rb.idx, rb.phase)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_t = tmem + tm_a_col(sa), b_base = s_addr(Bs + (size_t)rb.idx * bbytes);
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        umma_ts(acc, a_t + 8u * j, sdesc(b_base + 32 * j), idesc, (ks > 0 || j > 0) ? 1u : 0u);
+                    umma_commit(b_empty + 8 * rb.idx);
+                    umma_commit(a_empty + 8 * sa);
+                    rb.next();
+                }
+                if (ok) umma_commit(acc_full + 8 * ab);
+            }
+            if (!ok) report_timeout(g_err, 4);
+            umma_commit(drained);
+            if (!mbar_wait(drained, 0)) report_timeout(g_err, 5);
+        }
+    } else if (warp >= DEC_WARP0) {  // --------------------------------------- decode
+        // Group g decodes the CTA's k steps g, g + 2, ... into A stage g; warp quarter q owns
+        // TMEM lanes (rows) 32q .. 32q + 31, one row per lane. Each own step's weight rows are
+        // loaded into registers one own step ahead (and their chunks prefetched into L2
+        // TM_PREFETCH own steps ahead), so the loads fly while the previous step is decoded.
+        const int grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP, q = warp & 3;
+        const int row = 32 * q + lane;
+        const uint32_t a_dst = tmem + ((uint32_t)(32 * q) << 16) + tm_a_col(grp);
+        const int my_units = (int)blockIdx.x < units ? (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+        const int total = my_units * nks;  // k steps in the CTA's sequence
+        auto chunk_of = [&](int k) -> const uint8_t* {
+            const int i = k / nks, ks = k - i * nks;
+            int tile, tt, sp;
+            unit_coords((int)blockIdx.x + i * (int)gridDim.x, splits, ttiles, tile, tt, sp);
+            return g_w + ((int64_t)tile * ksteps + sp * nks + ks) * cb;
+        };
+        if (q == 0 && lane == 0)
+            for (int k = grp; k < total && k < grp + 2 * TM_PREFETCH; k += 2) bulk_prefetch_l2(chunk_of(k), (uint32_t)cb);
+        RowRaw<TYPE> nxt;
+        if (grp < total) row_load<TYPE>(nxt, chunk_of(grp), row);
+        bool ok = true;
+        int n = 0;
+        for (int k = grp; k < total; k += 2, n++) {
+            const RowRaw<TYPE> cur = nxt;
+            if (k + 2 < total) row_load<TYPE>(nxt, chunk_of(k + 2), row);
+            if (q == 0 && lane == 0 && k + 2 * TM_PREFETCH < total) bulk_prefetch_l2(chunk_of(k + 2 * TM_PREFETCH), (uint32_t)cb);
+            uint32_t v[32];
+            row_decode<TYPE>(cur, v);
+            if (!warp_wait_all(a_empty + 8 * grp, (uint32_t)(n & 1) ^ 1u)) { ok = false; break; }
+            tc_fence_after();
+            tm_st32(a_dst, v);
+            tm_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(a_full + 8 * grp);
+        }
+        if (!ok) report_timeout(g_err, 6);
+    } else if (warp >= 4) {  // ------------------------------------------------- epilogue
+        const int q = warp & 3;
+        constexpr bool counter_split = CSPLIT;
+        pdl_wait();
+        int i = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, i++) {
+            int tile, tt, sp;
+            unit_coords(u, splits, ttiles, tile, tt, sp);
+            const int t0 = tt * bn, ab = i & 1;
+            const bool w = warp_wait_all(acc_full + 8 * ab, (uint32_t)((i >> 1) & 1));
+            const bool ready = counter_split ? epi_all(w) : w;
+            tc_fence_after();
+            if (!ready) {
+                if (lane == 0) report_timeout(g_err, 7);
+                break;
+            }
+            const uint32_t tacc = tmem + (uint32_t)(ab * 256) + ((uint32_t)(q * 32) << 16);
+            const int nrow = tile * 128 + q * 32 + lane;
+            const int tn = min(bn, T - t0);
+            float* mine = splits > 1 ? g_ws + (int64_t)sp * T * ldy : nullptr;
+            if (counter_split) {
+                drain_cols(tacc, 0, bn, DR_RAW, lane, q, nrow, tile, t0, tn, tpad, ldy, mine, nullptr, g_xs_out);
+                __threadfence();
+                epi_bar();
+                if (warp == 4 && lane == 0) {
+                    int* ctr = g_ctr + tile * ttiles + tt;
+                    int old = atomicAdd(ctr, 1);
+                    int is_last = old == splits - 1;
+                    if (is_last) atomicExch(ctr, 0);
+                    *last_flag = is_last;
+                }
+                epi_bar();
+                const bool last = *last_flag != 0;
+                epi_bar();
+                if (last) {
+                    __threadfence();
+                    drain_cols(tacc, 0, bn, epi == EPI_ADD ? DR_ADD : DR_STORE, lane, q, nrow, tile, t0, tn, tpad, ldy, g_y,
+                               g_ws + (int64_t)(1 - sp) * T * ldy, g_xs_out);
+                }
+            } else {
+                const int cend = u + (int)gridDim.x >= units ? drain_share(bn, 1) : bn;
+                const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
+                drain_cols(tacc, 0, cend, kind, lane, q, nrow, tile, t0, tn, tpad, ldy, epi == EPI_PARTIAL ? mine : g_y, nullptr,
+                           g_xs_out);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+        }
+    }
+    // The decoder warps, done with the main loop, drain two thirds of the last unit's columns.
+    if (warp >= DEC_WARP0 && !CSPLIT && (int)blockIdx.x < units) {
+        const int my_units = (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+        const int il = my_units - 1, ul = (int)blockIdx.x + il * (int)gridDim.x;
+        int tile, tt, sp;
+        unit_coords(ul, splits, ttiles, tile, tt, sp);
+        const int ab = il & 1, q = warp & 3, grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
+        pdl_wait();
+        const bool ready = warp_wait_all(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
+        tc_fence_after();
+        if (ready) {
+            const int t0 = tt * bn;
+            const uint32_t tacc = tmem + (uint32_t)(ab * 256) + ((uint32_t)(q * 32) << 16);
+            const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
+            drain_cols(tacc, drain_share(bn, grp + 1), drain_share(bn, grp + 2), kind, lane, q, tile * 128 + q * 32 + lane, tile,
+                       t0, min(bn, T - t0), tpad, ldy, epi == EPI_PARTIAL ? g_ws + (int64_t)sp * T * ldy : g_y, nullptr,
+                       g_xs_out);
+        } else {
+            report_timeout(g_err, 8);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// Token tiles of a pass of T tokens: ceil(T / max) balanced tiles, multiples of 16, max = 256 (the
+// MMA's N limit) for k_gemm_tc and 224 for k_gemm_tm (the widest accumulator that leaves room for
+// two A stages in TMEM). From 128 to max tokens a
+// product with few row tiles (the 48-tile QKV, the split 24-tile projections) takes two tiles of
+// T / 2 so that it still covers most SMs; one with many row tiles (gate/up, the head) keeps one
+// tile of T, which halves its MMA instructions and still fills the SMs. tpad is a multiple of both.
+static bool gemm_on_smem_a();
+static int gemm_max_bn() { return gemm_on_smem_a() ? 256 : TM_MAX_BN; }
 int gemm_tpad_for(int T) {
-    if (T >= 128 && T <= 256) return 2 * (((T + 1) / 2 + 15) / 16 * 16);
-    const int n = T > 0 ? (T + 255) / 256 : 1;
+    const int mx = gemm_max_bn();
+    if (T >= 128 && T <= mx) return 2 * (((T + 1) / 2 + 15) / 16 * 16);
+    const int n = T > 0 ? (T + mx - 1) / mx : 1;
     const int bn = ((T + n - 1) / n + 15) / 16 * 16;
     return n * (bn < 16 ? 16 : bn);
 }
 // units_per_tile = row tiles x K splits of the product.
 int gemm_bn_for(int T, int units_per_tile, int sm_count) {
     const int tpad = gemm_tpad_for(T);
-    if (T >= 128 && T <= 256) return units_per_tile * 4 >= sm_count * 3 ? tpad : tpad / 2;
-    const int n = T > 0 ? (T + 255) / 256 : 1;
+    const int mx = gemm_max_bn();
+    if (T >= 128 && T <= mx) return units_per_tile * 4 >= sm_count * 3 ? tpad : tpad / 2;
+    const int n = T > 0 ? (T + mx - 1) / mx : 1;
     return tpad / n;
 }
 
 static int g_sm_count = 0;
+
+// JV_GEMM_KERNEL=tmem selects k_gemm_tm (decoded weights in TMEM, token tiles of at most 224)
+// instead of k_gemm_tc (decoded weights staged in shared memory, tiles of at most 256). Both give
+// the same bits (test_tmem_operand_gemm_is_bit_identical_to_the_shared_memory_gemm).
+static bool gemm_on_smem_a() {
+    static const bool v = [] {
+        const char* e = getenv("JV_GEMM_KERNEL");
+        return !(e != nullptr && strcmp(e, "tmem") == 0);
+    }();
+    return v;
+}
 
 template <int TYPE, int EPI, bool CSPLIT>
 static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
@@ -545,6 +907,27 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     int nc = 32;
     while (nc < a.bn) nc <<= 1;
     p.ncols = nc;
+    if (!gemm_on_smem_a()) {
+        // k_gemm_tm: shared memory holds only the activation ring (up to 8 stages in ~222 KB).
+        if (a.bn > TM_MAX_BN) throw Error(JV_ERR_ARG, "gemm: token tile above 224 for the TMEM-operand kernel");
+        const size_t budget = 222 * 1024, stage = (size_t)a.bn * 128;
+        p.ns = (int)std::min<size_t>(8, budget / stage);
+        p.nr = 0;
+        p.b_off = 0;
+        p.raw_off = 0;
+        p.bar_off = (int)(stage * p.ns);
+        // at least ~120 KB so that one CTA holds the SM (TMEM is allocated whole)
+        size_t smem = std::max<size_t>((size_t)p.bar_off + 8 * (2 * p.ns + 9) + 16 + 1024, 120 * 1024);
+        JV_CUDA(cudaFuncSetAttribute(k_gemm_tm<TYPE, EPI, CSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (g_sm_count == 0) {
+            int dev = 0;
+            JV_CUDA(cudaGetDevice(&dev));
+            JV_CUDA(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
+        }
+        launch_pdl(k_gemm_tm<TYPE, EPI, CSPLIT>, dim3(std::min(p.units, g_sm_count)), dim3(GEMM_THREADS), smem, s, p);
+        note_launch();
+        return;
+    }
     // Ring depths within ~222 KB: 4 stages (activation tile + decoded weights) if at least 4
     // raw chunks still fit, else 3; the raw ring takes the rest (up to 12 chunks).
     const size_t budget = 222 * 1024, stage = 16384 + (size_t)a.bn * 128;

@@ -245,6 +245,10 @@ struct DecGemvArgs {
     int advance = 0;             // advance *step to the next token after the argmax
     int32_t* tokens_out = nullptr;  // [steps], written at step->index when advancing
     DecodeStep* step_rw = nullptr;
+    // L2 prefetch of bytes a later kernel of the step reads (pf_bytes a multiple of 16, split
+    // evenly over the CTAs; nothing waits for it)
+    const uint8_t* pf = nullptr;
+    int64_t pf_bytes = 0;
 };
 void launch_dec_gemv(int mode, bool norm, int type, const DecGemvArgs& a, int splits, cudaStream_t s);
 int dec_splits_for(const QWeight& w, int sm_count);
@@ -261,6 +265,8 @@ struct DecAttnArgs {
     float* partial;   // [heads][splits][DEC_ATTN_PSTRIDE]
     int* counters;    // [kv_heads], zero between launches
     float* ctx32;     // [heads * 128]
+    const uint8_t* pf = nullptr;  // L2 prefetch of a later kernel's weights (as in DecGemvArgs)
+    int64_t pf_bytes = 0;
 };
 constexpr int DEC_ATTN_KEYS = 64;      // logical keys per attention split
 constexpr int DEC_ATTN_PSTRIDE = 132;  // floats per (head, split) partial, 16-byte multiple

@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
             dg_expect_tx(bar, (uint32_t)(nk * cb));
             for (int i = 0; i < nk; i++) dg_bulk(smem_u32(raw + (size_t)i * cb), src + (size_t)i * cb, (uint32_t)cb, bar);
         }
+        dg_prefetch_share(a.pf, a.pf_bytes);
     }
     pdl_launch_dependents();
     pdl_wait();
@@ -343,6 +344,7 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
     __shared__ const char* krow[DA_KEYS];  // K and V planes of each key's page, and its row there
     __shared__ const char* vrow[DA_KEYS];
     __shared__ int krowi[DA_KEYS];
+    if (threadIdx.x == 0) dg_prefetch_share(a.pf, a.pf_bytes);
     pdl_launch_dependents();
     pdl_wait();
     const DecodeStep st = *a.step;

@@ -729,6 +729,15 @@ void gemv(jv_ctx* x, const QWeight& w, const float* v, float* y, int epi) {
 // step varies by (token, slot, position, visible keys) is read from *d_step on the device.
 // attn_splits bounds the visible keys (64 per split) for every step this sequence serves.
 constexpr int DEC_ATTN_CTR = 4096;  // attention counters start here in dec_ctr
+// JV_DECODE_PREFETCH=0 turns the decode step's L2 weight prefetch off (for measuring what it gives).
+bool dec_prefetch_enabled() {
+    static const bool v = [] {
+        const char* e = getenv("JV_DECODE_PREFETCH");
+        return !(e != nullptr && strcmp(e, "0") == 0);
+    }();
+    return v;
+}
+
 void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool advance, int32_t* tokens_out) {
     jv_model* m = x->m;
     const jv_config& c = m->cfg;
@@ -751,8 +760,28 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
     if (m->layers.size() && m->head.tiles + 1 > DEC_ATTN_CTR) throw Error(JV_ERR_UNSUPPORTED, "decode: vocabulary too large");
 
     launch_embed(m->embd, &d_step->token, 1, h, hidden, x->d_err, s);
+    // Weight prefetch into L2, one matrix ahead (a Q4_0 layer is 65.5 MB, about half the 126 MB
+    // L2): QKV fetches O; the attention the first half of gate/up and O the second; gate/up
+    // fetches down; down fetches the next layer's QKV, or the head's first 32 MB after the last
+    // layer. The first QKV of a step is read from HBM.
+    auto pf_of = [](const QWeight& w, int64_t from, int64_t upto) {
+        const int64_t b = (int64_t)w.bytes();
+        from = std::min(from, b) & ~(int64_t)15;
+        upto = std::min(upto, b) & ~(int64_t)15;
+        return std::make_pair((const uint8_t*)w.data + from, std::max<int64_t>(0, upto - from));
+    };
+    const bool prefetch = dec_prefetch_enabled();
     for (int l = 0; l < c.layers; l++) {
         const LayerW& W = m->layers[l];
+        const int64_t gu_half = ((int64_t)W.gu.bytes() / 2) & ~(int64_t)15;
+        std::pair<const uint8_t*, int64_t> none{nullptr, 0};
+        auto pf_qkv = prefetch ? pf_of(W.o, 0, INT64_MAX) : none;
+        auto pf_attn = prefetch ? pf_of(W.gu, 0, gu_half) : none;
+        auto pf_o = prefetch ? pf_of(W.gu, gu_half, INT64_MAX) : none;
+        auto pf_gu = prefetch ? pf_of(W.down, 0, INT64_MAX) : none;
+        auto pf_down = !prefetch ? none
+                       : l + 1 < c.layers ? pf_of(m->layers[l + 1].qkv, 0, INT64_MAX)
+                       : head ? pf_of(m->head, 0, 32ll << 20) : none;
         DecGemvArgs a;
         a.partial = part;
         a.counters = ctr;
@@ -777,7 +806,11 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         a.page_table = x->d_pages.p;
         a.page_bytes = m->page_bytes;
         a.page_slots = m->page_slots;
+        a.pf = pf_qkv.first;
+        a.pf_bytes = pf_qkv.second;
         launch_dec_gemv(DEC_QKV, true, W.qkv.type, a, dec_splits_for(W.qkv, sms), s);
+        a.pf = nullptr;
+        a.pf_bytes = 0;
         // 2. attention
         DecAttnArgs da;
         da.q32 = q32;
@@ -793,6 +826,8 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         da.partial = apart;
         da.counters = ctr + DEC_ATTN_CTR;
         da.ctx32 = ctx;
+        da.pf = pf_attn.first;
+        da.pf_bytes = pf_attn.second;
         launch_dec_attn(da, attn_splits, s);
         // 3. O + residual
         DecGemvArgs o = a;
@@ -803,6 +838,8 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         o.n_in = qdim;
         o.norm_w = nullptr;
         o.y = h;
+        o.pf = pf_o.first;
+        o.pf_bytes = pf_o.second;
         launch_dec_gemv(DEC_ADD, false, W.o.type, o, dec_splits_for(W.o, sms), s);
         // 4. ffn_norm + gate/up + SwiGLU
         DecGemvArgs g = a;
@@ -813,6 +850,8 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         g.n_in = hidden;
         g.norm_w = W.ffn_norm;
         g.y = act;
+        g.pf = pf_gu.first;
+        g.pf_bytes = pf_gu.second;
         launch_dec_gemv(DEC_SWIGLU, true, W.gu.type, g, dec_splits_for(W.gu, sms), s);
         // 5. down + residual
         DecGemvArgs d = a;
@@ -823,6 +862,8 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         d.n_in = ff;
         d.norm_w = nullptr;
         d.y = h;
+        d.pf = pf_down.first;
+        d.pf_bytes = pf_down.second;
         launch_dec_gemv(DEC_ADD, false, W.down.type, d, dec_splits_for(W.down, sms), s);
     }
     if (head) {

@@ -311,6 +311,45 @@ def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
         assert e < 2e-3, (k, errs)
 
 
+@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
+def test_tmem_operand_gemm_is_bit_identical_to_the_shared_memory_gemm(model_factory, qtype):
+    """k_gemm_tm (decoded weights in TMEM, read straight from L2) against k_gemm_tc (decoded weights
+    staged in shared memory): the same fp16 operands and the same K order, so every captured
+    activation (the capture path's counter-combined K split) and the product path's verdict
+    logits (split-K halves folded by the next RMSNorm) are the same bits, for a causal prefill of
+    300 tokens and a tree after it."""
+    path = model_factory(WIDE_CFG, qtype, seed=12)
+    code = (
+        "import sys, numpy as np; sys.path[:0] = sys.argv[2:];"
+        "import jevstral_b200 as jv;"
+        "m = jv.Model(sys.argv[1], kv_pool_mb=512); c = jv.MinistralModel(m); caps = {};"
+        "c.set_activation_sink(lambda n, a: caps.__setitem__(n, a));"
+        "c.forward([1] + [(11 * i) % 16000 + 100 for i in range(299)]);"
+        "c.set_activation_sink(None); c.kv_cache.reset();"
+        "v = c.forward_tree([1] + list(range(2000, 2150)), [[5, 6, 7] * 10, [8] * 37, [9, 10]], [13059, 2649, 40]);"
+        "caps['verdicts'] = np.asarray(v, dtype=np.float32);"
+        "np.savez(sys.stdout.buffer, **caps)"
+    )
+    import io
+
+    from conftest import REPO
+
+    paths = [str(REPO / "llm-shield_b200"), str(REPO)]
+    outs = []
+    for kernel in ("tmem", "smem"):
+        env = dict(os.environ)
+        env.pop("JV_GEMM_KERNEL", None)
+        if kernel == "tmem":
+            env["JV_GEMM_KERNEL"] = "tmem"
+        r = subprocess.run([sys.executable, "-c", code, str(path)] + paths, env=env, capture_output=True, timeout=900)
+        assert r.returncode == 0, r.stderr.decode()[-2000:]
+        outs.append(np.load(io.BytesIO(r.stdout)))
+    tm, sm = outs
+    assert set(tm.files) == set(sm.files) and len(tm.files) > 20
+    diff = [k for k in sm.files if tm[k].tobytes() != sm[k].tobytes()]
+    assert not diff, {k: rel_l2(tm[k], sm[k]) for k in diff}
+
+
 def test_tensor_core_attention_matches_the_mma_sync_attention(model_factory):
     """The tcgen05 prefill attention against the mma.sync one on the same cache: a 1100-token
     causal trunk (nine 128-key blocks, ragged last block) and then a tree over it, per layer."""
