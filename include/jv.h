@@ -35,7 +35,10 @@ enum jv_status {
     JV_ERR_CANCELLED = 6,      /* OperationCanceledException                         */
     JV_ERR_DEVICE = 7,         /* a CUDA call failed                                 */
     JV_ERR_DEVICE_TIMEOUT = 8, /* a bounded device-side wait gave up                 */
-    JV_ERR_OOM = 9             /* device memory exhausted                            */
+    JV_ERR_OOM = 9,            /* device memory exhausted                            */
+    JV_ERR_NUMERIC = 10        /* an activation left the fp16 range of the device path
+                                  (|x| >= 65520 or not a number): ArithmeticException.
+                                  The reference's fp32 path has no such limit.        */
 };
 
 typedef struct jv_model jv_model;       /* weights resident on one device            */

@@ -175,8 +175,9 @@ __device__ __forceinline__ int drain_share(int bn, int s) {
 // t0 + column for columns below tn.
 __device__ __forceinline__ void drain_cols(uint32_t tacc, int c0, int c1, int kind, int lane, int q, int n, int tile,
                                            int t0, int tn, int tpad, int ldy, float* __restrict__ y,
-                                           const float* __restrict__ other, __half* __restrict__ xs_out) {
+                                           const float* __restrict__ other, __half* __restrict__ xs_out, int* err) {
     if (c0 >= c1) return;
+    bool bad = false;
     uint32_t cur[16], nxt[16];
     tmem_ld16_issue(tacc + (uint32_t)c0, cur);
     tmem_wait16(cur);
@@ -203,7 +204,11 @@ __device__ __forceinline__ void drain_cols(uint32_t tacc, int c0, int c1, int ki
                 const float uu = hi ? mv : ov;
                 const float up = __fmul_rn(gg, uu);
                 const float sg = __frcp_rn(__fadd_rn(1.0f, __expf(-gg)));
-                if (jj < lim) xs_out[kslab_offset(t0 + col + jj, jf, tpad)] = __float2half_rn(__fmul_rn(sg, up));
+                const float act = __fmul_rn(sg, up);
+                if (jj < lim) {
+                    bad |= f16_out_of_range(act);
+                    xs_out[kslab_offset(t0 + col + jj, jf, tpad)] = __float2half_rn(act);
+                }
             }
         } else {
             // Row pointers step by ldy per token.
@@ -241,6 +246,7 @@ __device__ __forceinline__ void drain_cols(uint32_t tacc, int c0, int c1, int ki
             for (int j = 0; j < 16; j++) cur[j] = nxt[j];
         }
     }
+    if (bad) report_numeric(err, NS_SWIGLU);
 }
 
 template <int TYPE, int EPI, bool CSPLIT>
@@ -440,7 +446,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 // Both K halves publish their partial; the unit that finishes last adds the
                 // other half to its own (still in TMEM): p0 + p1, the same value whichever
                 // unit that is (IEEE addition commutes).
-                drain_cols(tacc, 0, bn, DR_RAW, lane, q, n, tile, t0, tn, tpad, ldy, mine, nullptr, g_xs_out);
+                drain_cols(tacc, 0, bn, DR_RAW, lane, q, n, tile, t0, tn, tpad, ldy, mine, nullptr, g_xs_out, g_err);
                 __threadfence();
                 epi_bar();
                 if (warp == 4 && lane == 0) {
@@ -456,13 +462,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 if (last) {
                     __threadfence();
                     drain_cols(tacc, 0, bn, epi == EPI_ADD ? DR_ADD : DR_STORE, lane, q, n, tile, t0, tn, tpad, ldy, g_y,
-                               g_ws + (int64_t)(1 - sp) * T * ldy, g_xs_out);
+                               g_ws + (int64_t)(1 - sp) * T * ldy, g_xs_out, g_err);
                 }
             } else {
                 const int cend = u + (int)gridDim.x >= units ? drain_share(bn, 1) : bn;  // last unit: share 0
                 const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
                 drain_cols(tacc, 0, cend, kind, lane, q, n, tile, t0, tn, tpad, ldy, epi == EPI_PARTIAL ? mine : g_y, nullptr,
-                           g_xs_out);
+                           g_xs_out, g_err);
             }
             tc_fence_before();
             __syncwarp();
@@ -486,7 +492,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
             drain_cols(tacc, drain_share(bn, grp + 1), drain_share(bn, grp + 2), kind, lane, q, tile * 128 + q * 32 + lane, tile,
                        t0, min(bn, T - t0), tpad, ldy, epi == EPI_PARTIAL ? g_ws + (int64_t)sp * T * ldy : g_y, nullptr,
-                       g_xs_out);
+                       g_xs_out, g_err);
         } else {
             report_timeout(g_err, 8);
         }
@@ -787,7 +793,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tm(TcParams p) {
             const int tn = min(bn, T - t0);
             float* mine = splits > 1 ? g_ws + (int64_t)sp * T * ldy : nullptr;
             if (counter_split) {
-                drain_cols(tacc, 0, bn, DR_RAW, lane, q, nrow, tile, t0, tn, tpad, ldy, mine, nullptr, g_xs_out);
+                drain_cols(tacc, 0, bn, DR_RAW, lane, q, nrow, tile, t0, tn, tpad, ldy, mine, nullptr, g_xs_out, g_err);
                 __threadfence();
                 epi_bar();
                 if (warp == 4 && lane == 0) {
@@ -803,13 +809,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tm(TcParams p) {
                 if (last) {
                     __threadfence();
                     drain_cols(tacc, 0, bn, epi == EPI_ADD ? DR_ADD : DR_STORE, lane, q, nrow, tile, t0, tn, tpad, ldy, g_y,
-                               g_ws + (int64_t)(1 - sp) * T * ldy, g_xs_out);
+                               g_ws + (int64_t)(1 - sp) * T * ldy, g_xs_out, g_err);
                 }
             } else {
                 const int cend = u + (int)gridDim.x >= units ? drain_share(bn, 1) : bn;
                 const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
                 drain_cols(tacc, 0, cend, kind, lane, q, nrow, tile, t0, tn, tpad, ldy, epi == EPI_PARTIAL ? mine : g_y, nullptr,
-                           g_xs_out);
+                           g_xs_out, g_err);
             }
             tc_fence_before();
             __syncwarp();
@@ -832,7 +838,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tm(TcParams p) {
             const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
             drain_cols(tacc, drain_share(bn, grp + 1), drain_share(bn, grp + 2), kind, lane, q, tile * 128 + q * 32 + lane, tile,
                        t0, min(bn, T - t0), tpad, ldy, epi == EPI_PARTIAL ? g_ws + (int64_t)sp * T * ldy : g_y, nullptr,
-                       g_xs_out);
+                       g_xs_out, g_err);
         } else {
             report_timeout(g_err, 8);
         }

@@ -126,16 +126,28 @@ void launch_repack(const uint8_t* raw, int type, int rows, int cols, int64_t raw
                    int dst_tiles, int ksteps, int row_in_tile_base, int tile_offset, int interleave,
                    cudaStream_t s);
 void launch_embed(const QWeight& table, const int32_t* ids, int T, float* h, int hidden, int* err, cudaStream_t s);
+// fp16 operands: a value that rounds to infinity in fp16 (|v| >= 65520) or is not a number.
+// Kernels that pack fp16 record it in the context's error word (JV_ERR_NUMERIC and the site).
+enum NumericSite : int { NS_RMSNORM = 65, NS_ROPE_KV = 66, NS_SWIGLU = 67, NS_DEC_INPUT = 68, NS_DEC_KV = 69, NS_KV_RESTORE = 70 };
+#ifdef __CUDACC__
+__device__ __forceinline__ bool f16_out_of_range(float v) { return !(fabsf(v) < 65520.f); }
+__device__ __forceinline__ void report_numeric(int* err, int site) {
+    if (!err) return;
+    atomicCAS(err, 0, JV_ERR_NUMERIC);  // a timeout, if any, keeps priority
+    atomicCAS(err + 1, 0, site);
+}
+#endif
+
 void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __half* xs, int tpad, float* out32,
-                    cudaStream_t s);
+                    int* err, cudaStream_t s);
 // Prefill RMSNorm into the fp16 K-slab, first folding a pending split-K residual into h
 // (h += resid[0] + resid[1] when resid != nullptr, resid = [2][T][n]).
 void launch_rmsnorm_resid(float* h, const float* resid, const float* w, int T, int n, float eps, __half* xs, int tpad,
-                          cudaStream_t s);
+                          int* err, cudaStream_t s);
 // h += resid[0] + resid[1] (resid = [2][T][n]).
 void launch_resid_add(float* h, const float* resid, int64_t count, cudaStream_t s);
 void launch_rmsnorm_rows(const float* h, const int32_t* rows, int n_rows, const float* w, int n, float eps,
-                         float* out32, __half* xs, int tpad, cudaStream_t s);
+                         float* out32, __half* xs, int tpad, int* err, cudaStream_t s);
 void launch_gemm(const GemmArgs& a, cudaStream_t s);
 void launch_gemm_reference(const GemmArgs& a, cudaStream_t s);
 void launch_gemv(const QWeight& w, const float* x, float* partial, int splits, cudaStream_t s);
@@ -157,6 +169,7 @@ struct RopeArgs {
     int64_t page_bytes;     // bytes per page
     int page_slots;         // slots per page
     float* k32;             // optional capture of rotated keys [T][kvdim]
+    int* err = nullptr;     // error word (JV_ERR_NUMERIC when a value leaves the fp16 range)
 };
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s);
 void launch_rope_table(float2* table, const float* freqs, int half, int pos0, int npos, float mscale, cudaStream_t s);
@@ -272,7 +285,7 @@ constexpr int DEC_ATTN_KEYS = 64;      // logical keys per attention split
 constexpr int DEC_ATTN_PSTRIDE = 132;  // floats per (head, split) partial, 16-byte multiple
 void launch_dec_attn(const DecAttnArgs& a, int splits, cudaStream_t s);
 
-void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, cudaStream_t s);
+void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, int* err, cudaStream_t s);
 void launch_add(float* h, const float* x, int64_t n, cudaStream_t s);
 void launch_head_rows(const QWeight& table, const float* normed, int n_out, const int32_t* rows, int n_rows,
                       float* out, int* err, cudaStream_t s);
@@ -282,7 +295,7 @@ void launch_kslab_to_f32(const __half* xs, int T, int K, int tpad, float* out, c
 void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
                       int kv_heads, int len, float* out, cudaStream_t s);
 void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, const float* in, cudaStream_t s);
+                      int kv_heads, int len, const float* in, int* err, cudaStream_t s);
 int64_t launches_total();
 
 void note_launch(int n = 1);

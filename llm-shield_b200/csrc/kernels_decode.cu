@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
     }
     __syncthreads();
     // B fragments: column 0 = fp16(x), column 1 = fp16(x - column 0); lanes 0-3 / 4-7.
+    bool bad = false;
     for (int e = threadIdx.x; e < nk * 32; e += DG_THREADS) {
         const int ks = e >> 5, rest = e & 31, b = rest >> 4, sub = (rest >> 3) & 1, l = rest & 7;
         const int kq = l & 3, n = l >> 2;
@@ -106,6 +107,7 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
         uint32_t w[2];
 #pragma unroll
         for (int j = 0; j < 2; j++) {
+            bad |= f16_out_of_range(p[2 * j]) | f16_out_of_range(p[2 * j + 1]);
             __half h0 = __float2half_rn(p[2 * j]), h1 = __float2half_rn(p[2 * j + 1]);
             if (n == 1) {
                 h0 = __float2half_rn(__fsub_rn(p[2 * j], __half2float(h0)));
@@ -122,6 +124,7 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
             for (int i = 0; i < 32; i++) s = __fadd_rn(s, p[i]);
             sx[e] = s;
         }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) report_numeric(a.err, NS_DEC_INPUT);
     // x staged for every warp, and one verdict on the copy for the whole CTA (the warps' mma.sync
     // below needs all lanes)
     if (!__syncthreads_and(nk == 0 || dg_wait(bar, 0))) {
@@ -251,10 +254,12 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
                     a.q32[tile * 128 + 2 * t + 1] = r1;
                 } else {
                     char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq, 0, st.slot);
+                    if (f16_out_of_range(r0) || f16_out_of_range(r1)) report_numeric(a.err, NS_DEC_KV);
                     *(__half2*)(dst + kv_elem_offset(st.slot % a.page_slots, 2 * t, a.page_slots)) = __floats2half2_rn(r0, r1);
                 }
             } else {
                 char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq - hk, 1, st.slot);
+                if (f16_out_of_range(x0) || f16_out_of_range(x1)) report_numeric(a.err, NS_DEC_KV);
                 *(__half2*)(dst + kv_elem_offset(st.slot % a.page_slots, 2 * t, a.page_slots)) = __floats2half2_rn(x0, x1);
             }
         }

@@ -30,7 +30,7 @@ __device__ __forceinline__ double block_sum_double(double v, double* red) {
 }
 
 __device__ __forceinline__ void rmsnorm_row(const float* __restrict__ x, const float* __restrict__ w, int n, float eps,
-                                            int t, __half* __restrict__ xs, int tpad, float* __restrict__ out32) {
+                                            int t, __half* __restrict__ xs, int tpad, float* __restrict__ out32, int* err) {
     __shared__ double red[33];
     double s = 0;
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
@@ -39,23 +39,28 @@ __device__ __forceinline__ void rmsnorm_row(const float* __restrict__ x, const f
     }
     s = block_sum_double(s, red);
     float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / n), eps)));
+    bool bad = false;
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
         float y = __fmul_rn(__fmul_rn(x[k], scale), w[k]);
-        if (xs) xs[kslab_offset(t, k, tpad)] = __float2half_rn(y);
+        if (xs) {
+            bad |= f16_out_of_range(y);
+            xs[kslab_offset(t, k, tpad)] = __float2half_rn(y);
+        }
         if (out32) out32[k] = y;
     }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) report_numeric(err, NS_RMSNORM);
 }
 
 __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm(const float* __restrict__ h, const float* __restrict__ w,
                                                            int n, float eps, __half* __restrict__ xs, int tpad,
-                                                           float* __restrict__ out32) {
+                                                           float* __restrict__ out32, int* err) {
     int t = blockIdx.x;
-    rmsnorm_row(h + (int64_t)t * n, w, n, eps, t, xs, tpad, out32 ? out32 + (int64_t)t * n : nullptr);
+    rmsnorm_row(h + (int64_t)t * n, w, n, eps, t, xs, tpad, out32 ? out32 + (int64_t)t * n : nullptr, err);
 }
 
 void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __half* xs, int tpad, float* out32,
-                    cudaStream_t s) {
-    k_rmsnorm<<<T, NORM_THREADS, 0, s>>>(h, w, n, eps, xs, tpad, out32);
+                    int* err, cudaStream_t s) {
+    k_rmsnorm<<<T, NORM_THREADS, 0, s>>>(h, w, n, eps, xs, tpad, out32, err);
     note_launch();
 }
 
@@ -67,7 +72,8 @@ void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __h
 constexpr int RN_VEC = 4;
 __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_resid(float* __restrict__ h, const float* __restrict__ resid,
                                                                  const float* __restrict__ w, int n, float eps,
-                                                                 __half* __restrict__ xs, int tpad, int64_t plane) {
+                                                                 __half* __restrict__ xs, int tpad, int64_t plane,
+                                                                 int* err) {
     __shared__ double red[33];
     pdl_launch_dependents();
     pdl_wait();
@@ -96,25 +102,30 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_resid(float* __restric
     s = block_sum_double(s, red);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / n), eps)));
     const float4* w4 = (const float4*)w;
+    bool bad = false;
 #pragma unroll
     for (int j = 0; j < RN_VEC; j++) {
         const int i = threadIdx.x + j * NORM_THREADS;
         if (i < n4) {
             const float4 g = w4[i];
-            __half2 lo = __floats2half2_rn(__fmul_rn(__fmul_rn(v[j].x, scale), g.x), __fmul_rn(__fmul_rn(v[j].y, scale), g.y));
-            __half2 hi = __floats2half2_rn(__fmul_rn(__fmul_rn(v[j].z, scale), g.z), __fmul_rn(__fmul_rn(v[j].w, scale), g.w));
+            const float y0 = __fmul_rn(__fmul_rn(v[j].x, scale), g.x), y1 = __fmul_rn(__fmul_rn(v[j].y, scale), g.y);
+            const float y2 = __fmul_rn(__fmul_rn(v[j].z, scale), g.z), y3 = __fmul_rn(__fmul_rn(v[j].w, scale), g.w);
+            bad |= f16_out_of_range(y0) | f16_out_of_range(y1) | f16_out_of_range(y2) | f16_out_of_range(y3);
+            __half2 lo = __floats2half2_rn(y0, y1);
+            __half2 hi = __floats2half2_rn(y2, y3);
             uint2 pk;
             pk.x = *reinterpret_cast<uint32_t*>(&lo);
             pk.y = *reinterpret_cast<uint32_t*>(&hi);
             *(uint2*)(xs + kslab_offset(t, 4 * i, tpad)) = pk;
         }
     }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) report_numeric(err, NS_RMSNORM);
 }
 
 void launch_rmsnorm_resid(float* h, const float* resid, const float* w, int T, int n, float eps, __half* xs, int tpad,
-                          cudaStream_t s) {
+                          int* err, cudaStream_t s) {
     if (n % 4 != 0 || n > 4 * RN_VEC * NORM_THREADS) throw Error(JV_ERR_UNSUPPORTED, "rmsnorm: row width");
-    launch_pdl(k_rmsnorm_resid, dim3(T), dim3(NORM_THREADS), 0, s, h, resid, w, n, eps, xs, tpad, (int64_t)T * n);
+    launch_pdl(k_rmsnorm_resid, dim3(T), dim3(NORM_THREADS), 0, s, h, resid, w, n, eps, xs, tpad, (int64_t)T * n, err);
     note_launch();
 }
 
@@ -131,14 +142,15 @@ void launch_resid_add(float* h, const float* resid, int64_t count, cudaStream_t 
 // RMSNorm of selected rows (the output rows of a tree/rows pass, MinistralModel.cs:371-373,396).
 __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_rows(const float* __restrict__ h, const int32_t* __restrict__ rows,
                                                                 const float* __restrict__ w, int n, float eps,
-                                                                float* __restrict__ out32, __half* __restrict__ xs, int tpad) {
+                                                                float* __restrict__ out32, __half* __restrict__ xs, int tpad,
+                                                                int* err) {
     int b = blockIdx.x;
-    rmsnorm_row(h + (int64_t)rows[b] * n, w, n, eps, b, xs, tpad, out32 ? out32 + (int64_t)b * n : nullptr);
+    rmsnorm_row(h + (int64_t)rows[b] * n, w, n, eps, b, xs, tpad, out32 ? out32 + (int64_t)b * n : nullptr, err);
 }
 
 void launch_rmsnorm_rows(const float* h, const int32_t* rows, int n_rows, const float* w, int n, float eps,
-                         float* out32, __half* xs, int tpad, cudaStream_t s) {
-    k_rmsnorm_rows<<<n_rows, NORM_THREADS, 0, s>>>(h, rows, w, n, eps, out32, xs, tpad);
+                         float* out32, __half* xs, int tpad, int* err, cudaStream_t s) {
+    k_rmsnorm_rows<<<n_rows, NORM_THREADS, 0, s>>>(h, rows, w, n, eps, out32, xs, tpad, err);
     note_launch();
 }
 
@@ -200,6 +212,7 @@ __global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
     char* kv0 = (char*)a.kv_pool + (int64_t)page * a.page_bytes + kv_plane_offset(a.layer, a.kv_heads, 0, 0, a.page_slots);
     const int64_t head_stride = (int64_t)2 * a.page_slots * 256, v_off = (int64_t)a.page_slots * 256;
     const int nq4 = qdim / 4, nk4 = kvdim / 4;
+    bool bad = false;
     for (int i = threadIdx.x; i < nq4 + 2 * nk4; i += blockDim.x) {
         const float4 x = *(const float4*)(row + 4 * i);
         if (i < nq4 + nk4) {
@@ -208,6 +221,8 @@ __global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
             const float4 cs = tab4[d / 4];
             float r[4];
             rope_pair2(x, cs, i < nq4 ? temp : 1.0f, r);
+            if (i >= nq4 || a.q16)
+                bad |= f16_out_of_range(r[0]) | f16_out_of_range(r[1]) | f16_out_of_range(r[2]) | f16_out_of_range(r[3]);
             if (i < nq4) {
                 if (a.q16) {
                     __half2 lo = __floats2half2_rn(r[0], r[1]), hi = __floats2half2_rn(r[2], r[3]);
@@ -226,11 +241,13 @@ __global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
             }
         } else {  // v: straight copy to its slot
             const int ve = 4 * i - qdim - kvdim, head = ve / hd, d = ve % hd;
+            bad |= f16_out_of_range(x.x) | f16_out_of_range(x.y) | f16_out_of_range(x.z) | f16_out_of_range(x.w);
             __half2* dst = (__half2*)(kv0 + head * head_stride + v_off + kv_elem_offset(row_in_page, d, a.page_slots));
             dst[0] = __floats2half2_rn(x.x, x.y);
             dst[1] = __floats2half2_rn(x.z, x.w);
         }
     }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) report_numeric(a.err, NS_ROPE_KV);
 }
 
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
@@ -244,9 +261,11 @@ void launch_rope_kv(const RopeArgs& a, cudaStream_t s) {
 // Kernels.SwiGlu (Kernels.cs:82-89): up <- g*u; dst <- 1/(1+exp(-g)); dst <- dst*up.
 // gu holds the fused gate/up product: feature j = 64i + w sits in row tile i, gate at
 // column 128i + 32*(w/16) + w%16 and up 16 columns further.
-__global__ void k_swiglu(const float* __restrict__ gu, int ff, __half* __restrict__ xs, int tpad, float* __restrict__ out32) {
+__global__ void k_swiglu(const float* __restrict__ gu, int ff, __half* __restrict__ xs, int tpad, float* __restrict__ out32,
+                         int* err) {
     int t = blockIdx.x;
     const float* row = gu + (int64_t)t * 2 * ff;
+    bool bad = false;
     for (int j = threadIdx.x; j < ff; j += blockDim.x) {
         int w = j & 63;
         int col = (j >> 6) * 128 + (w >> 4) * 32 + (w & 15);
@@ -254,13 +273,17 @@ __global__ void k_swiglu(const float* __restrict__ gu, int ff, __half* __restric
         float up = __fmul_rn(g, u);
         float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
         float y = __fmul_rn(sg, up);
-        if (xs) xs[kslab_offset(t, j, tpad)] = __float2half_rn(y);
+        if (xs) {
+            bad |= f16_out_of_range(y);
+            xs[kslab_offset(t, j, tpad)] = __float2half_rn(y);
+        }
         if (out32) out32[(int64_t)t * ff + j] = y;
     }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) report_numeric(err, NS_SWIGLU);
 }
 
-void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, cudaStream_t s) {
-    k_swiglu<<<T, 256, 0, s>>>(gu, ff, xs, tpad, out32);
+void launch_swiglu(const float* gu, int T, int ff, __half* xs, int tpad, float* out32, int* err, cudaStream_t s) {
+    k_swiglu<<<T, 256, 0, s>>>(gu, ff, xs, tpad, out32, err);
     note_launch();
 }
 
@@ -315,7 +338,7 @@ __global__ void k_kv_export(const __half* __restrict__ pool, const int32_t* __re
 }
 
 __global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict__ page_table, int64_t page_bytes,
-                            int page_slots, int layers, int kv_heads, int len, const float* __restrict__ in) {
+                            int page_slots, int layers, int kv_heads, int len, const float* __restrict__ in, int* err) {
     int64_t total = (int64_t)2 * layers * kv_heads * len * 128;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int d = (int)(i % 128);
@@ -329,7 +352,9 @@ __global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict
         int page = page_table[p / page_slots];
         __half* dst = (__half*)((char*)pool + (int64_t)page * page_bytes + kv_plane_offset(l, kv_heads, h, kv, page_slots) +
                                 kv_elem_offset(p % page_slots, d, page_slots));
-        *dst = __float2half_rn(in[i]);
+        const float v = in[i];
+        if (f16_out_of_range(v)) report_numeric(err, NS_KV_RESTORE);
+        *dst = __float2half_rn(v);
     }
 }
 
@@ -340,9 +365,9 @@ void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t pag
     note_launch();
 }
 void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, const float* in, cudaStream_t s) {
+                      int kv_heads, int len, const float* in, int* err, cudaStream_t s) {
     if (len <= 0) return;
-    k_kv_import<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, in);
+    k_kv_import<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, in, err);
     note_launch();
 }
 

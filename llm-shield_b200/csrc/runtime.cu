@@ -613,6 +613,18 @@ const char* timeout_site(int site) {
     }
 }
 
+const char* numeric_site(int site) {
+    switch (site) {
+        case NS_RMSNORM: return "an RMSNorm (the fp16 operand of the next projection)";
+        case NS_ROPE_KV: return "the RoPE / K-V page write";
+        case NS_SWIGLU: return "the SwiGLU activation (the fp16 operand of the down projection)";
+        case NS_DEC_INPUT: return "the input of a single-token matvec";
+        case NS_DEC_KV: return "the single-token K-V page write";
+        case NS_KV_RESTORE: return "a KV snapshot restore";
+        default: return "a device kernel";
+    }
+}
+
 void sync_check(jv_ctx* x) {
     JV_CUDA(cudaMemcpyAsync(x->h_err.get(2), x->d_err, 2 * sizeof(int), cudaMemcpyDeviceToHost, x->stream));
     JV_CUDA(cudaStreamSynchronize(x->stream));
@@ -623,6 +635,10 @@ void sync_check(jv_ctx* x) {
         JV_CUDA(cudaStreamSynchronize(x->stream));
         if (e == JV_ERR_DEVICE_TIMEOUT)
             throw Error(JV_ERR_DEVICE_TIMEOUT, std::string("a device-side wait timed out (") + timeout_site(site) + ")");
+        if (e == JV_ERR_NUMERIC)
+            throw Error(JV_ERR_NUMERIC, std::string("an activation left the fp16 range the device path computes in "
+                                                    "(|x| >= 65520, or not a number) at ") + numeric_site(site) +
+                                            "; the reference's fp32 path has no such limit");
         throw Error(e, "a kernel reported an out-of-range index");
     }
 }
@@ -661,7 +677,7 @@ void gemm(jv_ctx* x, const QWeight& w, const __half* xs, int T, int tpad, float*
     if (epi == EPI_SWIGLU && use_ref) {  // the CUDA-core check product has no fused epilogue
         float* gu = x->gu32.get((size_t)T * w.rows);
         gemm(x, w, xs, T, tpad, gu, w.rows, EPI_STORE);
-        launch_swiglu(gu, T, w.rows / 2, xs_out, tpad, nullptr, x->stream);
+        launch_swiglu(gu, T, w.rows / 2, xs_out, tpad, nullptr, x->d_err, x->stream);
         return;
     }
     GemmArgs a;
@@ -1101,9 +1117,10 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         ra.page_bytes = m->page_bytes;
         ra.page_slots = m->page_slots;
         ra.k32 = capture ? x->k32.get((size_t)T * kvdim) : nullptr;
+        ra.err = x->d_err;
         if (decode) {
             float* xn = x->x32.get(hidden);
-            launch_rmsnorm(h, W.attn_norm, 1, hidden, c.eps, nullptr, 0, xn, s);
+            launch_rmsnorm(h, W.attn_norm, 1, hidden, c.eps, nullptr, 0, xn, x->d_err, s);
             observe(x, p + "attn_norm", xn, 1, hidden);
             gemv(x, W.qkv, xn, qkv32, EPI_STORE);
             ra.q16 = nullptr;
@@ -1143,12 +1160,12 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
                 gemv(x, W.o, da.ctx32, h, EPI_ADD);
             }
             observe(x, p + "post_attn", h, 1, hidden);
-            launch_rmsnorm(h, W.ffn_norm, 1, hidden, c.eps, nullptr, 0, xn, s);
+            launch_rmsnorm(h, W.ffn_norm, 1, hidden, c.eps, nullptr, 0, xn, x->d_err, s);
             observe(x, p + "ffn_norm", xn, 1, hidden);
             float* gu = x->gu32.get(2 * (size_t)ff);
             gemv(x, W.gu, xn, gu, EPI_STORE);
             float* act = x->act32.get(ff);
-            launch_swiglu(gu, 1, ff, nullptr, 0, act, s);
+            launch_swiglu(gu, 1, ff, nullptr, 0, act, x->d_err, s);
             if (capture) {
                 float* fo = x->out32.get(hidden);
                 gemv(x, W.down, act, fo, EPI_STORE);
@@ -1162,9 +1179,9 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         }
         __half* xs = x->xs.get((size_t)tpad * hidden);
         if (capture)
-            launch_rmsnorm(h, W.attn_norm, T, hidden, c.eps, xs, tpad, nullptr, s);
+            launch_rmsnorm(h, W.attn_norm, T, hidden, c.eps, xs, tpad, nullptr, x->d_err, s);
         else
-            launch_rmsnorm_resid(h, resid, W.attn_norm, T, hidden, c.eps, xs, tpad, s);
+            launch_rmsnorm_resid(h, resid, W.attn_norm, T, hidden, c.eps, xs, tpad, x->d_err, s);
         observe_kslab(x, p + "attn_norm", xs, T, hidden, tpad);
         ra.q16 = x->q16.get((size_t)T * qdim);
         ra.q32 = capture ? x->q32.get((size_t)T * qdim) : nullptr;
@@ -1210,9 +1227,9 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         }
         observe(x, p + "post_attn", h, T, hidden);
         if (capture)
-            launch_rmsnorm(h, W.ffn_norm, T, hidden, c.eps, xs, tpad, nullptr, s);
+            launch_rmsnorm(h, W.ffn_norm, T, hidden, c.eps, xs, tpad, nullptr, x->d_err, s);
         else
-            launch_rmsnorm_resid(h, resid, W.ffn_norm, T, hidden, c.eps, xs, tpad, s);
+            launch_rmsnorm_resid(h, resid, W.ffn_norm, T, hidden, c.eps, xs, tpad, x->d_err, s);
         resid = nullptr;
         observe_kslab(x, p + "ffn_norm", xs, T, hidden, tpad);
         __half* xf = x->xs_ff.get((size_t)tpad * ff);
@@ -1235,7 +1252,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     // Heads (MinistralModel.cs:362-424).
     if (rows && out) {
         float* normed = x->x32.get((size_t)n_out * hidden);
-        launch_rmsnorm_rows(h, d_outs, n_out, m->out_norm, hidden, c.eps, normed, nullptr, 0, s);
+        launch_rmsnorm_rows(h, d_outs, n_out, m->out_norm, hidden, c.eps, normed, nullptr, 0, x->d_err, s);
         float* d_res = x->out32.get((size_t)n_out * n_rows);
         launch_head_rows(m->head, normed, n_out, d_rows, n_rows, d_res, x->d_err, s);
         float* hres = x->h_out.get((size_t)n_out * n_rows);
@@ -1248,11 +1265,11 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         if (n_out >= 2) {
             int tp = gemm_tpad_for(n_out);
             __half* xo = x->xs.get((size_t)std::max(tp, tpad) * hidden);
-            launch_rmsnorm_rows(h, d_outs, n_out, m->out_norm, hidden, c.eps, nullptr, xo, tp, s);
+            launch_rmsnorm_rows(h, d_outs, n_out, m->out_norm, hidden, c.eps, nullptr, xo, tp, x->d_err, s);
             gemm(x, m->head, xo, n_out, tp, d_res, V, EPI_STORE);
         } else {
             float* normed = x->x32.get(hidden);
-            launch_rmsnorm_rows(h, d_outs, 1, m->out_norm, hidden, c.eps, normed, nullptr, 0, s);
+            launch_rmsnorm_rows(h, d_outs, 1, m->out_norm, hidden, c.eps, normed, nullptr, 0, x->d_err, s);
             gemv(x, m->head, normed, d_res, EPI_STORE);
         }
         float* hres = x->h_out.get((size_t)n_out * V);
@@ -1270,7 +1287,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         if (!fused) {  // the fused decode step already wrote the logits
             int32_t* d_last = x->out_i32.get(1);
             JV_CUDA(cudaMemcpyAsync(d_last, &last, sizeof(int32_t), cudaMemcpyHostToDevice, s));
-            launch_rmsnorm_rows(h, d_last, 1, m->out_norm, hidden, c.eps, normed, nullptr, 0, s);
+            launch_rmsnorm_rows(h, d_last, 1, m->out_norm, hidden, c.eps, normed, nullptr, 0, x->d_err, s);
             observe(x, "final_norm", normed, 1, hidden);
             gemv(x, m->head, normed, d_logits, EPI_STORE);
         }
@@ -1758,7 +1775,7 @@ int jv_kv_restore(jv_ctx* x, const float* snap, int64_t n_floats, int32_t length
         float* d = x->cap32.get((size_t)std::max<int64_t>(1, need));
         JV_CUDA(cudaMemcpyAsync(d, snap, sizeof(float) * need, cudaMemcpyHostToDevice, x->stream));
         const jv_config& c = x->m->cfg;
-        launch_kv_import(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, length, d, x->stream);
+        launch_kv_import(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, length, d, x->d_err, x->stream);
         JV_CUDA(cudaStreamSynchronize(x->stream));
         x->length = length;
     });

@@ -5,7 +5,7 @@ package mirrors the reference's MinistralModel / KvCache / JevstralDecider membe
 tests and the benchmark drive the same entry points a .NET host binds over P/Invoke.
 """
 from ._lib import (ArgumentError, ArgumentOutOfRangeError, DeviceError, DeviceOutOfMemoryError,  # noqa: F401
-                   DeviceTimeoutError, GgufIOError, InvalidDataError, JvError, NotSupportedError,
+                   DeviceTimeoutError, GgufIOError, InvalidDataError, JvError, NotSupportedError, NumericError,
                    OperationCanceledError, SIGNATURES, LIB_PATH)
 from .decider import (DecisionResult, TokenDecider, decision_probs, margins_from_verdicts,  # noqa: F401
                       softmax)

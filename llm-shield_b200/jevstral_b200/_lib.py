@@ -86,7 +86,7 @@ for _name, _res, _args in SIGNATURES:
 
 # Status codes (enum jv_status).
 JV_OK, JV_ERR_ARG, JV_ERR_RANGE, JV_ERR_FORMAT, JV_ERR_IO, JV_ERR_UNSUPPORTED, JV_ERR_CANCELLED, JV_ERR_DEVICE, \
-    JV_ERR_DEVICE_TIMEOUT, JV_ERR_OOM = range(10)
+    JV_ERR_DEVICE_TIMEOUT, JV_ERR_OOM, JV_ERR_NUMERIC = range(11)
 
 
 class JvError(Exception):
@@ -98,8 +98,9 @@ class JvError(Exception):
 
 
 # The reference's exception types: ArgumentException, ArgumentOutOfRangeException,
-# InvalidDataException, IOException, NotSupportedException, OperationCanceledException, and a
-# device failure, which has no counterpart in the managed reference.
+# InvalidDataException, IOException, NotSupportedException, OperationCanceledException; a device
+# failure, which has no counterpart in the managed reference; and ArithmeticException for an
+# activation outside the fp16 range the device path computes in.
 class ArgumentError(JvError, ValueError): ...
 class ArgumentOutOfRangeError(JvError, IndexError): ...
 class InvalidDataError(JvError): ...
@@ -109,11 +110,13 @@ class OperationCanceledError(JvError): ...
 class DeviceError(JvError, RuntimeError): ...
 class DeviceTimeoutError(DeviceError): ...
 class DeviceOutOfMemoryError(DeviceError, MemoryError): ...
+class NumericError(JvError, ArithmeticError): ...
 
 
 _BY_CODE = {JV_ERR_ARG: ArgumentError, JV_ERR_RANGE: ArgumentOutOfRangeError, JV_ERR_FORMAT: InvalidDataError,
             JV_ERR_IO: GgufIOError, JV_ERR_UNSUPPORTED: NotSupportedError, JV_ERR_CANCELLED: OperationCanceledError,
-            JV_ERR_DEVICE: DeviceError, JV_ERR_DEVICE_TIMEOUT: DeviceTimeoutError, JV_ERR_OOM: DeviceOutOfMemoryError}
+            JV_ERR_DEVICE: DeviceError, JV_ERR_DEVICE_TIMEOUT: DeviceTimeoutError, JV_ERR_OOM: DeviceOutOfMemoryError,
+            JV_ERR_NUMERIC: NumericError}
 
 
 def check(rc: int) -> None:

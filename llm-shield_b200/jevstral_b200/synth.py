@@ -48,9 +48,32 @@ class SynthConfig:
     rope_theta: float = 1e6
     eps: float = 1e-5
     context_length: int = 262144
+    # Further `mistral3.*` metadata as (key after the architecture prefix, kind, value); kind is
+    # "str", "u32" or "f32". yarn_metadata() gives the real checkpoint's RoPE scaling keys.
+    extra: Tuple[Tuple[str, str, object], ...] = ()
+    norm_gain: float = 1.0  # every RMSNorm gain (1.0 in the benchmark model)
 
 
 MINISTRAL_3B = SynthConfig()
+
+
+def yarn_metadata(factor: float = 16.0, original_context: int = 16384, beta_fast: float = 32.0,
+                  beta_slow: float = 1.0, temperature_scale: float = 0.1) -> Tuple[Tuple[str, str, object], ...]:
+    """The RoPE-scaling and attention-temperature keys the reference's converter writes for a
+    Mistral-format checkpoint with YaRN and llama-4 scaling (tools/convert_shieldstral_to_gguf.py:
+    337-354): YaRN factor over an original window, beta fast/slow, "apply_scale": false (the
+    magnitude terms cancel to 1), and the query temperature beta past the window."""
+    return (("rope.scaling.type", "str", "yarn"),
+            ("rope.scaling.factor", "f32", float(factor)),
+            ("rope.scaling.original_context_length", "u32", int(original_context)),
+            ("rope.scaling.yarn_beta_fast", "f32", float(beta_fast)),
+            ("rope.scaling.yarn_beta_slow", "f32", float(beta_slow)),
+            ("rope.scaling.yarn_ext_factor", "f32", 1.0),
+            ("rope.scaling.mscale", "f32", 1.0),
+            ("rope.scaling.yarn_log_multiplier", "f32", 1.0),
+            ("rope.scaling.attn_factor", "f32", 1.0),
+            ("attention.temperature_scale", "f32", float(temperature_scale)),
+            ("attention.temperature_length", "u32", int(original_context)))
 
 
 def tensor_plan(cfg: SynthConfig) -> List[Tuple[str, Tuple[int, ...], bool]]:
@@ -102,6 +125,7 @@ def _metadata(cfg: SynthConfig, qtype: int) -> Dict[str, tuple]:
         "tokenizer.ggml.tokens": ("strs", _token_list(cfg.vocab)),
         "tokenizer.ggml.bos_token_id": ("u32", 1),
         "tokenizer.ggml.eos_token_id": ("u32", 2),
+        **{f"{a}.{k}": (kind, v) for k, kind, v in cfg.extra},
     }
 
 
@@ -189,7 +213,7 @@ def write_random_gguf(path, cfg: SynthConfig = MINISTRAL_3B, qtype: str = "Q8_0"
     for tid, ((name, shape, is_mat), o) in enumerate(zip(plan, offsets)):
         base = data_start + o
         if not is_mat:
-            mm[base:base + 4 * shape[0]] = np.ones(shape[0], dtype=np.float32).view(np.uint8)
+            mm[base:base + 4 * shape[0]] = np.full(shape[0], cfg.norm_gain, dtype=np.float32).view(np.uint8)
             continue
         jobs.append((tid, base, shape[0], shape[1], name))
     if backend == "exe":
@@ -234,7 +258,7 @@ def _write_numpy(path: Path, cfg: SynthConfig, qtype: str, seed: int, std: float
             w.add_array(k, v)
     for name, shape, is_mat in tensor_plan(cfg):
         if not is_mat:
-            w.add_tensor(name, np.ones(shape, dtype=np.float32))
+            w.add_tensor(name, np.full(shape, cfg.norm_gain, dtype=np.float32))
             continue
         vals = (rng.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
         w.add_tensor(name, gguf.quants.quantize(vals, qt), raw_dtype=qt)

@@ -121,3 +121,20 @@ def test_struct_layouts_match_the_binding(tmp_path):
         for n in fields[st]:
             assert got[(st, n)] == getattr(cls, n).offset, (st, n)
     assert got[("jv_config", "sizeof")] == 68 and got[("jv_layout", "sizeof")] == 56
+
+
+def test_status_codes_match_the_header():
+    """Every JV_* status in include/jv.h has the same value in the Python binding (and so in the
+    C# enum that INTEGRATION.md lists)."""
+    import re as _re
+
+    from jevstral_b200 import _lib
+
+    text = HEADER.read_text()
+    body = text[text.index("enum jv_status"):text.index("};", text.index("enum jv_status"))]
+    body = _re.sub(r"/\*.*?\*/", "", body, flags=_re.S)
+    codes = dict((n, int(v)) for n, v in _re.findall(r"(JV_[A-Z_]+)\s*=\s*(\d+)", body))
+    assert codes["JV_ERR_NUMERIC"] == 10 and len(codes) == 11
+    for name, value in codes.items():
+        assert getattr(_lib, name) == value, name
+    assert issubclass(_lib._BY_CODE[_lib.JV_ERR_NUMERIC], ArithmeticError)

@@ -122,6 +122,50 @@ def test_full_width_tree_matches_the_oracle(model_factory, qtype):
     assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
 
 
+@pytest.mark.parametrize("window", [16384, 64])
+def test_yarn_rope_and_query_temperature_match_the_oracle(model_factory, window):
+    """The real checkpoint's RoPE scaling (YaRN factor 16, beta 32/1, magnitude scale 1) and the
+    llama-4 query temperature q *= 1 + 0.1 ln(1 + floor(pos / window)) (Rope.cs:33-106,
+    MinistralModel.cs:676-682). With the 16384 window the prompt stays inside it (the YaRN table
+    alone); with a 64-token window a 300-token prompt crosses four interval boundaries, and the tree
+    branches and single-token steps after it run at positions 300-330. Every layer's rotated q and
+    k and output, the logits, the branch verdicts and the decode logits against the oracle."""
+    from jevstral_b200.synth import SynthConfig, yarn_metadata
+
+    cfg = SynthConfig(layers=2, hidden=256, heads=8, kv_heads=2, head_dim=128, ff=512, vocab=16384,
+                      extra=yarn_metadata(original_context=window))
+    path = model_factory(cfg, "Q8_0", seed=14)
+    prompt = [1] + toks(299, 61)
+    branches = [toks(n, 62 + i) for i, n in enumerate((9, 4, 17))]
+    gpu, cpu = {}, {}
+    with jv.Model(path, kv_pool_mb=128) as m, ctx(m) as c, ob.OracleModel(path) as o:
+        assert m.config.yarn_active and m.config.rope_mscale == 1.0
+        assert abs(m.config.temperature_scale - 0.1) < 1e-7 and m.config.rope_orig_ctx == window
+        c.set_activation_sink(capture_into(gpu))
+        lg = c.forward(prompt)
+        lo = o.forward(prompt, sink=capture_into(cpu))
+        for l in range(cfg.layers):
+            for n in ("q_rope", "k_rope", "output"):
+                key = f"blk.{l}.{n}"
+                assert rel_l2(gpu[key], cpu[key]) < HIDDEN_TOL, key
+        assert rel_l2(lg, lo) < HIDDEN_TOL
+        c.set_activation_sink(None)
+        c.kv_cache.truncate(len(prompt) - 1)
+        o.kv_truncate(len(prompt) - 1)
+        v_gpu = c.forward_tree([prompt[-1]], branches, VERDICT_ROWS)
+        o_v = o.forward_tree([prompt[-1]], branches, VERDICT_ROWS)
+        z_gpu, z_cpu = margins_from_verdicts(v_gpu, 1), margins_from_verdicts(o_v, 1)
+        assert np.abs(z_gpu - z_cpu).max() < Z_TOL
+        c.kv_cache.truncate(len(prompt))
+        o.kv_truncate(len(prompt))
+        nxt = int(np.argmax(lo))
+        for step in range(3):  # the fused single-token kernels apply the temperature on the device
+            lg = c.forward([nxt])
+            lo = o.forward([nxt])
+            assert rel_l2(lg, lo) < HIDDEN_TOL, step
+            nxt = int(np.argmax(lo))
+
+
 def test_decode_steps_match_the_oracle(small):
     """Single-token forwards (the decode GEMV path) with the full LM head."""
     prompt = [1] + toks(40, 9)
@@ -255,6 +299,35 @@ def test_errors_map_to_the_reference_exceptions(small, tmp_path):
     short.write_bytes(data[: len(data) // 3])
     with pytest.raises(jv.GgufIOError):
         jv.Model(short)
+
+
+def test_activations_beyond_the_fp16_range_raise_a_numeric_error(model_factory):
+    """Norm gains of 1e5 put the RMSNorm output far outside fp16 (|x| >= 65520). The reference
+    computes this in fp32; the device path packs its GEMM operands in fp16, so every fp16 writer
+    checks its values and the call raises NumericError (ArithmeticException), naming where, instead
+    of returning logits built from infinities. Prefill, tree and single-token paths; the context
+    stays usable (a second call raises the same way)."""
+    from jevstral_b200.synth import SynthConfig
+
+    cfg = SynthConfig(layers=2, hidden=256, heads=8, kv_heads=2, head_dim=128, ff=512, vocab=16384,
+                      norm_gain=1e5)
+    path = model_factory(cfg, "Q8_0", seed=15)
+    prompt = [1] + toks(40, 71)
+    with jv.Model(path, kv_pool_mb=128) as m, ctx(m) as c:
+        for _ in range(2):
+            c.kv_cache.reset()
+            with pytest.raises(jv.NumericError, match="RMSNorm"):
+                c.forward(prompt)
+        c.kv_cache.reset()
+        with pytest.raises(jv.NumericError):
+            c.forward_tree(prompt, [[2000, 3000], [4000]], VERDICT_ROWS)
+        c.kv_cache.reset()
+        with pytest.raises(jv.NumericError):
+            c.forward([1])  # the fused single-token kernels
+    # a model inside the range is unaffected
+    ok = model_factory(SMALL_CFG, "Q8_0", seed=15)
+    with jv.Model(ok, kv_pool_mb=128) as m, ctx(m) as c:
+        assert np.isfinite(c.forward(prompt)).all()
 
 
 def test_a_device_wait_that_runs_out_reports_and_leaves_the_context_usable(small):

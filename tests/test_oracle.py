@@ -284,3 +284,51 @@ def test_truncated_gguf_is_rejected(small_gguf, tmp_path):
     with pytest.raises(ob.OracleError) as e:
         ob.OracleModel(bad)
     assert e.value.code == 3
+
+
+def _rope_cs_freqs(base, dims, factor, orig, beta_fast, beta_slow, ext=1.0):
+    """Rope() of the reference (src/Jevstral/Model/Rope.cs:33-66, YarnCorrectionDims :91-106) in
+    float32, as MathF computes it: the frequency of every rotated pair with the YaRN ramp."""
+    f32 = np.float32
+    half = dims // 2
+    base, factor, ext = f32(base), f32(factor), f32(ext)
+    freq_scale = f32(1) / factor
+
+    def corr(rot):
+        return f32(dims) * np.log(f32(orig) / (f32(rot) * f32(2) * f32(np.pi)), dtype=f32) / (f32(2) * np.log(base, dtype=f32))
+
+    low = max(f32(0), np.floor(corr(beta_fast)))
+    high = min(f32(dims) / f32(2) - f32(1), np.ceil(corr(beta_slow)))
+    out = np.empty(half, dtype=f32)
+    for i in range(half):
+        extrap = f32(1) / np.power(base, f32(2) * f32(i) / f32(dims), dtype=f32)
+        interp = freq_scale * extrap
+        y = (f32(i) - low) / max(f32(0.001), high - low)
+        mix = (f32(1) - np.clip(y, f32(0), f32(1))) * ext
+        out[i] = interp * (f32(1) - mix) + extrap * mix
+    return out
+
+
+def test_yarn_frequencies_follow_the_reference_formula(tmp_path):
+    """The oracle's YaRN table (the real checkpoint's keys: factor 16 over 16384, beta 32/1,
+    "apply_scale": false) against Rope.cs restated in float32, within float32 pow/log rounding; the
+    magnitude scale cancels to exactly 1 and the query temperature is read (RopeAndCacheTests
+    MagnitudeScaleIsOneWhenApplyScaleIsOff / YarnRampInterpolatesTheSlowBandsOnly)."""
+    from jevstral_b200.synth import SynthConfig, write_random_gguf, yarn_metadata
+
+    cfg = SynthConfig(layers=1, hidden=256, heads=8, kv_heads=2, head_dim=128, ff=512, vocab=2048,
+                      extra=yarn_metadata())
+    path = write_random_gguf(tmp_path / "yarn.gguf", cfg, "Q8_0", seed=1, backend="fast")
+    with ob.OracleModel(path) as o:
+        assert o.config["yarn_active"] == 1
+        assert o.config["rope_mscale"] == 1.0
+        assert abs(o.config["temperature_scale"] - 0.1) < 1e-7
+        assert o.config["rope_orig_ctx"] == 16384
+        got = np.empty(64, dtype=np.float32)
+        assert ob.lib.orc_rope_freqs(o._h, got.ctypes.data_as(ob.f32p)) == 64
+    want = _rope_cs_freqs(1e6, 128, 16.0, 16384, 32.0, 1.0)
+    assert np.allclose(got, want, rtol=4e-7, atol=0), np.abs(got / want - 1).max()
+    base = np.float32(1) / np.power(np.float32(1e6), np.arange(64, dtype=np.float32) * 2 / 128, dtype=np.float32)
+    # the fast bands keep the base frequency, the slow bands are divided by the factor
+    assert np.allclose(got[:8], base[:8], rtol=1e-6)
+    assert np.allclose(got[-4:], base[-4:] / 16, rtol=1e-6)
