@@ -73,3 +73,114 @@ def gather_results(dist: Any, rank: int, world: int, mine: Sequence[Tuple[int, A
     merged = [p for part in box for p in part]
     merged.sort(key=lambda p: p[0])
     return [r for _, r in merged]
+
+
+# ------------------------------------------------------------------ failure handling
+#
+# A rank that dies (raises, exits, or never starts) must not lose its decisions. run_requeued
+# keeps the same longest-first shard plan, but every decision is claimed in a shared key-value
+# store before it runs and its result is published there; ranks beat a heartbeat after every
+# decision (and from a background thread). A rank that finishes its own shard takes over any
+# decision whose owner is marked failed or whose heartbeat is older than `timeout_s`, stealing
+# the claim of a dead rank atomically (compare-and-set), so each decision's published result
+# comes from one completed run. Rank 0 hosts the store and collects the results in decision
+# order; its own failure ends the job. Nothing here touches a GPU: the store is
+# torch.distributed's TCPStore (or any object with set/get/check/compare_set).
+
+import pickle
+import threading
+import time
+
+
+def _key(kind: str, i: int) -> str:
+    return f"jvdp/{kind}/{i}"
+
+
+class RankFailed(RuntimeError):
+    """Raised by run_requeued on the rank whose own run_one raised, after it has marked itself
+    failed in the store (so the survivors take its decisions at once)."""
+
+
+def _alive(store, rank: int, now: float, timeout_s: float, started: float, startup_s: float) -> bool:
+    if store.check([_key("failed", rank)]):
+        return False
+    if store.check([_key("hb", rank)]):
+        return now - float(store.get(_key("hb", rank)).decode()) <= timeout_s
+    return now - started <= startup_s  # never started: dead once the start-up grace has passed
+
+
+def run_requeued(store, rank: int, world: int, costs: Sequence[float], run_one, timeout_s: float = 10.0,
+                 poll_s: float = 0.05, startup_s: float = 60.0) -> Optional[List[Any]]:
+    """Run decision i (run_one(i) -> picklable result) for every i, sharded longest-first over
+    `world` ranks, surviving the failure of any rank but 0. Returns the results in decision order
+    on rank 0 and None elsewhere. A rank is dead once it has marked itself failed, once its
+    heartbeat is older than `timeout_s`, or, if it never beat, once `startup_s` have passed since
+    rank 0 opened the job (the time rank 0 publishes in the store, which every rank reads)."""
+    if rank == 0:
+        store.set("jvdp/start", repr(time.time()))
+    started = float(store.get("jvdp/start").decode())
+    n = len(costs)
+    plan = shard_decisions(costs, world)
+    owner = {i: r for r, s in enumerate(plan) for i in s}
+    me = str(rank).encode()
+    stop = threading.Event()
+
+    def beat():
+        while not stop.is_set():
+            store.set(_key("hb", rank), repr(time.time()))
+            stop.wait(timeout_s / 4)
+
+    hb = threading.Thread(target=beat, daemon=True)
+    store.set(_key("hb", rank), repr(time.time()))
+    hb.start()
+
+    def run(i: int) -> None:
+        try:
+            res = run_one(i)
+        except BaseException as e:
+            store.set(_key("failed", rank), repr(e))
+            stop.set()
+            raise RankFailed(f"rank {rank} failed on decision {i}") from e
+        store.set(_key("res", i), pickle.dumps(res))
+        store.set(_key("hb", rank), repr(time.time()))
+
+    def claim(i: int, holder: bytes) -> bool:
+        got = store.compare_set(_key("claim", i), holder, me)
+        return got == me
+
+    try:
+        for i in plan[rank]:
+            if not store.check([_key("res", i)]) and claim(i, b""):
+                run(i)
+        while True:
+            missing = [i for i in range(n) if not store.check([_key("res", i)])]
+            if not missing:
+                break
+            took = False
+            now = time.time()
+            for i in missing:
+                if store.check([_key("res", i)]):
+                    continue
+                held = store.get(_key("claim", i)) if store.check([_key("claim", i)]) else b""
+                holder = int(held.decode()) if held else owner[i]
+                if holder == rank or _alive(store, holder, now, timeout_s, started, startup_s):
+                    continue
+                if claim(i, held):
+                    run(i)
+                    took = True
+            if not took:
+                time.sleep(poll_s)
+    finally:
+        stop.set()
+    store.set(_key("done", rank), b"1")
+    if rank != 0:
+        return None
+    results = [pickle.loads(store.get(_key("res", i))) for i in range(n)]
+    # rank 0 hosts the store: stay until every rank still alive has left the loop above
+    while True:
+        now = time.time()
+        waiting = [r for r in range(1, world)
+                   if not store.check([_key("done", r)]) and _alive(store, r, now, timeout_s, started, startup_s)]
+        if not waiting:
+            return results
+        time.sleep(poll_s)

@@ -93,3 +93,70 @@ def test_two_gloo_ranks_shard_and_gather(tmp_path):
 
 def test_single_rank_gather_needs_no_process_group():
     assert dp.gather_results(None, 0, 1, [(2, "c"), (0, "a"), (1, "b")]) == ["a", "b", "c"]
+
+
+# ------------------------------------------------------------ failure handling (host side)
+
+
+def _requeue_main(rank, world, port, out_dir, scenario):
+    import datetime
+    import time
+
+    from torch.distributed import TCPStore
+
+    ready = os.path.join(out_dir, "store_ready")
+    if rank != 0:  # connect once the store is listening (a client that starts first backs off for long)
+        t0 = time.time()
+        while not os.path.exists(ready) and time.time() - t0 < 60:
+            time.sleep(0.02)
+    store = TCPStore("127.0.0.1", port, None, rank == 0, datetime.timedelta(seconds=60), wait_for_workers=False)
+    if rank == 0:
+        open(ready, "w").close()
+    shapes = c5_shapes(30, seed=5)
+    costs = [dp.decision_cost(t, b) for t, b in shapes]
+    count = [0]
+
+    def run_one(i):
+        count[0] += 1
+        if scenario == "raise" and rank == 2 and count[0] == 2:
+            raise RuntimeError("injected failure")
+        if scenario == "exit" and rank == 1 and count[0] == 2:
+            os._exit(3)  # dies mid-decision, with its claim held and without marking itself failed
+        time.sleep(0.01)
+        return (i, float(shapes[i][0]) * len(shapes[i][1]), rank)
+
+    res = dp.run_requeued(store, rank, world, costs, run_one, timeout_s=1.0, poll_s=0.02, startup_s=6.0)
+    if rank == 0:
+        np.save(os.path.join(out_dir, "results.npy"), np.asarray(res, dtype=np.float64))
+
+
+@pytest.mark.parametrize("scenario", ["raise", "exit", "absent"])
+def test_a_failed_rank_s_decisions_are_requeued_onto_the_survivors(tmp_path, scenario):
+    """Three ranks share a 30-decision list over a TCPStore. One of them fails: rank 2 raises on its
+    second decision (and marks itself failed), or rank 1 exits mid-decision holding its claim (found
+    by its stale heartbeat), or rank 2 never starts (found once the start-up grace passes). The survivors
+    run every orphaned decision and rank 0 returns all 30 results, correct and in order."""
+    import multiprocessing as mpx
+
+    world, port = 3, _free_port()
+    ctx = mpx.get_context("spawn")
+    ranks = [0, 1] if scenario == "absent" else [0, 1, 2]
+    procs = [ctx.Process(target=_requeue_main, args=(r, world, port, str(tmp_path), scenario)) for r in ranks]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    codes = {r: p.exitcode for r, p in zip(ranks, procs)}
+    failed = {"raise": 2, "exit": 1, "absent": None}[scenario]
+    for r, c in codes.items():
+        assert (c != 0) if r == failed else (c == 0), codes
+    got = np.load(tmp_path / "results.npy")
+    shapes = c5_shapes(30, seed=5)
+    assert got[:, 0].tolist() == list(range(30))
+    assert got[:, 1].tolist() == [float(t) * len(b) for t, b in shapes]
+    costs = [dp.decision_cost(t, b) for t, b in shapes]
+    lost = dp.shard_decisions(costs, world)[failed if failed is not None else 2]
+    assert len(lost) > 0
+    # the decisions the failed rank never finished were run by a survivor
+    ran_by = {int(i): int(r) for i, _, r in got}
+    assert all(ran_by[i] != (failed if failed is not None else 2) for i in lost[1:])
