@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 tc_fence_after();
                 const uint32_t acc = tmem + (uint32_t)(ab * ncols);
                 for (int ks = 0; ks < nks; ks++) {
-                    if (!mbar_wait(a_full + 8 * rs.idx, rs.phase) || !mbar_wait(b_full + 8 * rs.idx, rs.phase)) {
+                    if (!mbar_poll(a_full + 8 * rs.idx, rs.phase) || !mbar_poll(b_full + 8 * rs.idx, rs.phase)) {
                         ok = false;
                         break;
                     }
@@ -716,7 +716,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tm(TcParams p) {
                 const uint32_t acc = tmem + (uint32_t)(ab * 256);
                 for (int ks = 0; ks < nks; ks++, k++) {
                     const int sa = k & 1;
-                    if (!mbar_wait(a_full + 8 * sa, (uint32_t)((k >> 1) & 1)) || !mbar_wait(b_full + 8 * rb.idx, rb.phase)) {
+                    if (!mbar_poll(a_full + 8 * sa, (uint32_t)((k >> 1) & 1)) || !mbar_poll(b_full + 8 * rb.idx, rb.phase)) {
                         ok = false;
                         break;
                     }

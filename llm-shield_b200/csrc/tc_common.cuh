@@ -44,6 +44,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long lo
         if (clock64() - t0 > bound) return false;
     return true;
 }
+// Bounded wait that polls with the non-blocking mbarrier.test_wait instead of sleeping in
+// try_wait: for the single thread that issues the MMAs, whose wake-up latency after a phase
+// completes would otherwise sit between the data landing and the next MMA.
+__device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, long long bound = WAIT_CYCLES) {
+    uint32_t ok;
+    const long long t0 = clock64();
+    for (;;) {
+        asm volatile(
+            "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (clock64() - t0 > bound) return false;
+    }
+}
 // A bounded wait gave up: the error word takes JV_ERR_DEVICE_TIMEOUT and the word after it
 // the first site that gave up (kernel x 16 + role), which the host names in its message.
 __device__ __forceinline__ void report_timeout(int* err, int site) {
