@@ -217,6 +217,24 @@ int jv_kv_snapshot(jv_ctx* ctx, int32_t length, float* out, int64_t n_floats);
 /* KvCache.Restore (:115-136). */
 int jv_kv_restore(jv_ctx* ctx, const float* snapshot, int64_t n_floats, int32_t length);
 
+/* SystemPromptCache.Save (src/Jevstral/SystemPromptCache.cs:110-127) straight from the device
+ * pages: writes the reference's "SHKV" file for the first n_tokens cached positions — uint32
+ * magic 0x53484B56, int32 version 1, the fingerprint string as .NET's BinaryWriter writes it
+ * (7-bit-encoded UTF-8 byte count, then the bytes), int32 token count, the tokens, int64 float
+ * count, then the KvCache.Snapshot floats (:94-112) — streamed one (K|V, layer) slice at a time
+ * through pinned memory, so the whole state never sits in host memory. The fingerprint is the
+ * host's (ComputeFingerprint, :91-106); n_tokens must not exceed the cached length. */
+int jv_kv_save_shkv(jv_ctx* ctx, const char* path, const char* fingerprint, const int32_t* tokens, int32_t n_tokens);
+/* SystemPromptCache.TryLoad + RestoreInto (SystemPromptCache.cs:65-74,133-164) into the device
+ * pages: reads an SHKV file, checks its magic, version, that its fingerprint equals `fingerprint`
+ * and that its float count fits its token count on this model, then streams the floats into the
+ * pages (the cache then holds exactly that prefix) and writes the tokens to tokens_out
+ * (max_tokens entries) and their count to *n_tokens. TryLoad's miss (null) is JV_ERR_IO for a file
+ * that cannot be opened and JV_ERR_FORMAT for one that is not a valid snapshot of this model and
+ * prefix; both leave the cache as it was. */
+int jv_kv_load_shkv(jv_ctx* ctx, const char* path, const char* fingerprint, int32_t* tokens_out, int32_t max_tokens,
+                    int32_t* n_tokens);
+
 /* Zero-copy prefix reuse (the question-snapshot LRU and system-prompt cache of
  * JevstralDecider.cs:131-137,262-280 without the memcpy): jv_kv_share pins the pages that
  * hold the first `length` positions; jv_kv_adopt makes a context's cache exactly that prefix

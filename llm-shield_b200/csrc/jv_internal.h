@@ -292,10 +292,13 @@ void launch_head_rows(const QWeight& table, const float* normed, int n_out, cons
 void launch_argmax(const float* x, int n, int32_t* out, cudaStream_t s);
 void launch_kslab_to_f32(const __half* xs, int T, int K, int tpad, float* out, cudaStream_t s);
 // KV pages <-> the reference's flat fp32 snapshot layout (keys of every layer/head, then values).
+// Elements [base, base + count) of the flat snapshot (count = 0: to the end), to or from a
+// buffer holding exactly those elements.
 void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, float* out, cudaStream_t s);
+                      int kv_heads, int len, float* out, cudaStream_t s, int64_t base = 0, int64_t count = 0);
 void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, const float* in, int* err, cudaStream_t s);
+                      int kv_heads, int len, const float* in, int* err, cudaStream_t s, int64_t base = 0,
+                      int64_t count = 0);
 int64_t launches_total();
 
 void note_launch(int n = 1);

@@ -318,9 +318,10 @@ namespace jv {
 // KvCache.Snapshot / Restore layout (reference src/Jevstral/Model/KvCache.cs:94-136):
 // [pass: K then V][layer][kv head][position < len][128] fp32.
 __global__ void k_kv_export(const __half* __restrict__ pool, const int32_t* __restrict__ page_table, int64_t page_bytes,
-                            int page_slots, int layers, int kv_heads, int len, float* __restrict__ out) {
-    int64_t total = (int64_t)2 * layers * kv_heads * len * 128;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+                            int page_slots, int layers, int kv_heads, int len, float* __restrict__ out, int64_t base,
+                            int64_t count) {
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < count; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = base + j;
         int d = (int)(i % 128);
         int64_t r = i / 128;
         int p = (int)(r % len);
@@ -333,14 +334,15 @@ __global__ void k_kv_export(const __half* __restrict__ pool, const int32_t* __re
         const __half* src = (const __half*)((const char*)pool + (int64_t)page * page_bytes +
                                              kv_plane_offset(l, kv_heads, h, kv, page_slots) +
                                              kv_elem_offset(p % page_slots, d, page_slots));
-        out[i] = __half2float(*src);
+        out[j] = __half2float(*src);
     }
 }
 
 __global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict__ page_table, int64_t page_bytes,
-                            int page_slots, int layers, int kv_heads, int len, const float* __restrict__ in, int* err) {
-    int64_t total = (int64_t)2 * layers * kv_heads * len * 128;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+                            int page_slots, int layers, int kv_heads, int len, const float* __restrict__ in, int* err,
+                            int64_t base, int64_t count) {
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < count; j += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = base + j;
         int d = (int)(i % 128);
         int64_t r = i / 128;
         int p = (int)(r % len);
@@ -352,22 +354,24 @@ __global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict
         int page = page_table[p / page_slots];
         __half* dst = (__half*)((char*)pool + (int64_t)page * page_bytes + kv_plane_offset(l, kv_heads, h, kv, page_slots) +
                                 kv_elem_offset(p % page_slots, d, page_slots));
-        const float v = in[i];
+        const float v = in[j];
         if (f16_out_of_range(v)) report_numeric(err, NS_KV_RESTORE);
         *dst = __float2half_rn(v);
     }
 }
 
 void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, float* out, cudaStream_t s) {
+                      int kv_heads, int len, float* out, cudaStream_t s, int64_t base, int64_t count) {
     if (len <= 0) return;
-    k_kv_export<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, out);
+    if (count <= 0) count = (int64_t)2 * layers * kv_heads * len * 128 - base;
+    k_kv_export<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, out, base, count);
     note_launch();
 }
 void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, const float* in, int* err, cudaStream_t s) {
+                      int kv_heads, int len, const float* in, int* err, cudaStream_t s, int64_t base, int64_t count) {
     if (len <= 0) return;
-    k_kv_import<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, in, err);
+    if (count <= 0) count = (int64_t)2 * layers * kv_heads * len * 128 - base;
+    k_kv_import<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, in, err, base, count);
     note_launch();
 }
 

@@ -11,6 +11,7 @@
 #include <cstddef>
 #include <atomic>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <limits>
 #include <memory>
@@ -1778,6 +1779,145 @@ int jv_kv_restore(jv_ctx* x, const float* snap, int64_t n_floats, int32_t length
         launch_kv_import(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, length, d, x->d_err, x->stream);
         JV_CUDA(cudaStreamSynchronize(x->stream));
         x->length = length;
+    });
+}
+
+// ---- SHKV persistence straight from / into the device pages (SystemPromptCache.Save / TryLoad)
+
+namespace {
+
+constexpr uint32_t SHKV_MAGIC = 0x53484B56u;  // "SHKV", SystemPromptCache.cs:25
+constexpr int32_t SHKV_VERSION = 1;           // SystemPromptCache.cs:26
+
+// BinaryWriter.Write(string): the UTF-8 byte count as a 7-bit encoded integer, then the bytes.
+void shkv_put_string(std::string& out, const std::string& v) {
+    uint32_t n = (uint32_t)v.size();
+    while (n >= 0x80) {
+        out.push_back((char)(n | 0x80));
+        n >>= 7;
+    }
+    out.push_back((char)n);
+    out += v;
+}
+void shkv_put32(std::string& out, uint32_t v) { out.append((const char*)&v, 4); }
+void shkv_put64(std::string& out, int64_t v) { out.append((const char*)&v, 8); }
+
+struct File {
+    std::FILE* f = nullptr;
+    ~File() {
+        if (f) std::fclose(f);
+    }
+};
+
+}  // namespace
+
+int jv_kv_save_shkv(jv_ctx* x, const char* path, const char* fingerprint, const int32_t* tokens, int32_t n_tokens) {
+    if (!x || !path || !fingerprint || (!tokens && n_tokens > 0)) return set_error(JV_ERR_ARG, "NULL argument");
+    return guarded([&] {
+        if (n_tokens < 0 || n_tokens > x->length)
+            throw Error(JV_ERR_RANGE, "Only " + std::to_string(x->length) + " positions are cached.");
+        set_device(x->m);
+        ctx_upload_pages(x);
+        const jv_config& c = x->m->cfg;
+        const int64_t total = jv_kv_snapshot_floats(x, n_tokens);
+        std::string head;
+        shkv_put32(head, SHKV_MAGIC);
+        shkv_put32(head, (uint32_t)SHKV_VERSION);
+        shkv_put_string(head, fingerprint);
+        shkv_put32(head, (uint32_t)n_tokens);
+        for (int i = 0; i < n_tokens; i++) shkv_put32(head, (uint32_t)tokens[i]);
+        shkv_put64(head, total);
+        File f;
+        f.f = std::fopen(path, "wb");
+        if (!f.f) throw Error(JV_ERR_IO, std::string("cannot create ") + path);
+        if (std::fwrite(head.data(), 1, head.size(), f.f) != head.size()) throw Error(JV_ERR_IO, std::string("write failed: ") + path);
+        // one (K|V, layer) slice of the flat layout at a time: gather from the pages on the
+        // device, one copy to pinned memory, one write
+        const int64_t slice = (int64_t)c.kv_heads * n_tokens * 128;
+        float* d = x->cap32.get((size_t)std::max<int64_t>(1, slice));
+        float* h = x->h_cap.get((size_t)std::max<int64_t>(1, slice));
+        for (int64_t base = 0; base < total; base += slice) {
+            launch_kv_export(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, n_tokens, d,
+                             x->stream, base, slice);
+            JV_CUDA(cudaMemcpyAsync(h, d, sizeof(float) * slice, cudaMemcpyDeviceToHost, x->stream));
+            JV_CUDA(cudaStreamSynchronize(x->stream));
+            if (std::fwrite(h, sizeof(float), (size_t)slice, f.f) != (size_t)slice)
+                throw Error(JV_ERR_IO, std::string("write failed: ") + path);
+        }
+        if (std::fflush(f.f) != 0) throw Error(JV_ERR_IO, std::string("write failed: ") + path);
+    });
+}
+
+int jv_kv_load_shkv(jv_ctx* x, const char* path, const char* fingerprint, int32_t* tokens_out, int32_t max_tokens,
+                    int32_t* n_tokens) {
+    if (!x || !path || !fingerprint || !n_tokens) return set_error(JV_ERR_ARG, "NULL argument");
+    *n_tokens = 0;
+    return guarded([&] {
+        File f;
+        f.f = std::fopen(path, "rb");
+        if (!f.f) throw Error(JV_ERR_IO, std::string("cannot open ") + path);
+        auto get = [&](void* dst, size_t n) {
+            if (std::fread(dst, 1, n, f.f) != n) throw Error(JV_ERR_FORMAT, std::string(path) + " is truncated");
+        };
+        uint32_t magic = 0;
+        int32_t version = 0;
+        get(&magic, 4);
+        get(&version, 4);
+        if (magic != SHKV_MAGIC || version != SHKV_VERSION) throw Error(JV_ERR_FORMAT, std::string(path) + " is not an SHKV v1 file");
+        uint32_t len = 0;
+        for (int shift = 0;; shift += 7) {
+            uint8_t b = 0;
+            get(&b, 1);
+            if (shift > 28) throw Error(JV_ERR_FORMAT, "bad fingerprint length");
+            len |= (uint32_t)(b & 0x7F) << shift;
+            if (!(b & 0x80)) break;
+        }
+        if (len > (1u << 20)) throw Error(JV_ERR_FORMAT, "bad fingerprint length");
+        std::string fp(len, '\0');
+        get(fp.data(), len);
+        if (fp != fingerprint) throw Error(JV_ERR_FORMAT, "the snapshot was captured for a different model or prefix");
+        int32_t count = 0;
+        get(&count, 4);
+        if (count < 0 || count > 1000000) throw Error(JV_ERR_FORMAT, "bad token count");
+        std::vector<int32_t> toks((size_t)count);
+        if (count) get(toks.data(), sizeof(int32_t) * (size_t)count);
+        int64_t state = 0;
+        get(&state, 8);
+        if (state != jv_kv_snapshot_floats(x, count))
+            throw Error(JV_ERR_FORMAT, "the snapshot holds " + std::to_string(state) + " floats; " + std::to_string(count) +
+                                           " positions of this model need " + std::to_string(jv_kv_snapshot_floats(x, count)));
+        const long here = std::ftell(f.f);
+        std::fseek(f.f, 0, SEEK_END);
+        const long end = std::ftell(f.f);
+        if (here < 0 || end - here < (long)(state * 4)) throw Error(JV_ERR_FORMAT, std::string(path) + " is truncated");
+        std::fseek(f.f, here, SEEK_SET);
+        if (count > max_tokens || (!tokens_out && count > 0))
+            throw Error(JV_ERR_RANGE, "the snapshot holds " + std::to_string(count) + " tokens; the buffer holds " +
+                                          std::to_string(max_tokens));
+        // the file is a valid snapshot of this model: now replace the cache with it
+        set_device(x->m);
+        const jv_config& c = x->m->cfg;
+        ctx_ensure_capacity(x, std::max(1, count));
+        std::vector<int> wp;
+        for (int p = 0; p * x->m->page_slots < count; p++) wp.push_back(p);
+        ctx_make_writable(x, wp);
+        ctx_upload_pages(x);
+        const int64_t slice = (int64_t)c.kv_heads * count * 128;
+        float* d = x->cap32.get((size_t)std::max<int64_t>(1, slice));
+        float* h = x->h_cap.get((size_t)std::max<int64_t>(1, slice));
+        x->length = 0;  // the pages hold a partial copy until the last slice is in
+        for (int64_t base = 0; base < state; base += slice) {
+            if (std::fread(h, sizeof(float), (size_t)slice, f.f) != (size_t)slice)
+                throw Error(JV_ERR_IO, std::string("read failed: ") + path);
+            JV_CUDA(cudaMemcpyAsync(d, h, sizeof(float) * slice, cudaMemcpyHostToDevice, x->stream));
+            launch_kv_import(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, count, d,
+                             x->d_err, x->stream, base, slice);
+            JV_CUDA(cudaStreamSynchronize(x->stream));
+        }
+        sync_check(x);
+        x->length = count;
+        if (count) std::memcpy(tokens_out, toks.data(), sizeof(int32_t) * (size_t)count);
+        *n_tokens = count;
     });
 }
 

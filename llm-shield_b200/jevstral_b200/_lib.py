@@ -73,6 +73,8 @@ SIGNATURES = [
     ("jv_kv_snapshot_floats", i64, [vp, i32]),
     ("jv_kv_snapshot", C.c_int, [vp, i32, f32p, i64]),
     ("jv_kv_restore", C.c_int, [vp, f32p, i64, i32]),
+    ("jv_kv_save_shkv", C.c_int, [vp, C.c_char_p, C.c_char_p, i32p, i32]),
+    ("jv_kv_load_shkv", C.c_int, [vp, C.c_char_p, C.c_char_p, i32p, i32, i32p]),
     ("jv_kv_share", C.c_int, [vp, i32, C.POINTER(vp)]),
     ("jv_kv_adopt", C.c_int, [vp, vp]),
     ("jv_snapshot_length", i32, [vp]),

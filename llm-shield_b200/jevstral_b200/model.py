@@ -150,6 +150,25 @@ class KvCache:
         s = np.ascontiguousarray(snapshot, dtype=np.float32)
         check(lib.jv_kv_restore(self._ctx._h, _p(s, C.c_float), s.size, int(length)))
 
+    def save_shkv(self, path, fingerprint: str, tokens: Sequence[int]) -> None:
+        """SystemPromptCache.Save (SystemPromptCache.cs:110-127) of the first len(tokens) cached
+        positions, written from the device pages in the reference's SHKV file format."""
+        t = _i32(tokens)
+        check(lib.jv_kv_save_shkv(self._ctx._h, str(path).encode(), fingerprint.encode(), _p(t), t.size))
+
+    def load_shkv(self, path, fingerprint: str, max_tokens: int = 1 << 20) -> Optional[List[int]]:
+        """SystemPromptCache.TryLoad + RestoreInto (SystemPromptCache.cs:65-74,133-164): the
+        cache becomes the file's prefix and its tokens are returned; None on a miss (a file that
+        is absent, unreadable, or not a snapshot of this model and prefix), cache untouched."""
+        out = np.empty(max_tokens, dtype=np.int32)
+        n = C.c_int32(0)
+        rc = lib.jv_kv_load_shkv(self._ctx._h, str(path).encode(), fingerprint.encode(), _p(out), max_tokens,
+                                 C.byref(n))
+        if rc in (_lib.JV_ERR_IO, _lib.JV_ERR_FORMAT):
+            return None
+        check(rc)
+        return out[: n.value].tolist()
+
     def share(self, length: int) -> Snapshot:
         h = C.c_void_p()
         check(lib.jv_kv_share(self._ctx._h, int(length), C.byref(h)))

@@ -138,3 +138,33 @@ def test_status_codes_match_the_header():
     for name, value in codes.items():
         assert getattr(_lib, name) == value, name
     assert issubclass(_lib._BY_CODE[_lib.JV_ERR_NUMERIC], ArithmeticError)
+
+
+def test_shkv_restatement_round_trips_and_encodes_lengths_like_binarywriter():
+    import numpy as _np
+
+    import shkv_format as shkv
+
+    # .NET's documented 7-bit encoding examples
+    assert shkv.encode_7bit(0) == b"\x00" and shkv.encode_7bit(127) == b"\x7f"
+    assert shkv.encode_7bit(128) == b"\x80\x01" and shkv.encode_7bit(300) == b"\xac\x02"
+    state = _np.arange(24, dtype=_np.float32) / 7
+    fp = "ab" * 100  # a 200-byte string needs the two-byte length prefix
+    blob = shkv.write(fp, [1, 5, 9], state)
+    assert blob[:4] == bytes.fromhex("564b4853")  # "SHKV" little-endian
+    got_fp, toks, st = shkv.read(blob)
+    assert got_fp == fp and toks == [1, 5, 9] and _np.array_equal(st, state)
+
+
+def test_shkv_entry_points_reject_bad_arguments_without_a_device():
+    from jevstral_b200._lib import JV_ERR_ARG, lib
+
+    n = ctypes_i32()
+    assert lib.jv_kv_save_shkv(None, b"/tmp/x", b"fp", None, 0) == JV_ERR_ARG
+    assert lib.jv_kv_load_shkv(None, b"/tmp/x", b"fp", None, 0, n) == JV_ERR_ARG
+
+
+def ctypes_i32():
+    import ctypes
+
+    return ctypes.byref(ctypes.c_int32(0))

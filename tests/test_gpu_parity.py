@@ -264,6 +264,49 @@ def test_reusing_the_trunk_for_a_second_decision_is_bit_identical(small):
         assert r2.margins.tobytes() == ref.margins.tobytes()
 
 
+def test_system_prompt_snapshot_file_and_the_verdict_scorer_flow(small, tmp_path):
+    """SystemPromptCache and VerdictScorer on device pages (SystemPromptCache.cs:51-164,
+    VerdictScorer.cs:231-254): capture the system prefix, Save it as an SHKV file straight from the
+    pages (byte for byte the reference's format of KvCache.Snapshot), TryLoad it into a fresh
+    context, and ForwardSelectedAsync the request: the same bits as an uncached forward of the whole
+    prompt. A wrong fingerprint, a missing file and a truncated file are misses that leave the cache
+    as it was; the loaded prefix shared zero-copy into another context gives the same bits again
+    (the per-request restore without a copy)."""
+    import shkv_format as shkv
+
+    system = [1] + toks(70, 81)
+    request = toks(25, 82)
+    fp = "model.gguf|123|456|mistral3|2x2x128|71:" + "x" * 150  # > 127 bytes: two-byte length prefix
+    path = tmp_path / "system.shkv"
+    with ctx(small) as a:
+        a.prefill(system)
+        a.kv_cache.save_shkv(path, fp, system)
+        snap = a.kv_cache.snapshot(len(system))
+    data = path.read_bytes()
+    assert data == shkv.write(fp, system, snap)
+    with ctx(small) as whole:
+        want = whole.forward_selected(system + request, VERDICT_ROWS)
+    with ctx(small) as b:
+        b.prefill([1, 2000, 3000])  # a cache the load replaces
+        assert b.kv_cache.load_shkv(path, fp) == system
+        assert b.kv_cache.length == len(system)
+        got = b.forward_selected(request, VERDICT_ROWS)
+        assert got.tobytes() == want.tobytes()
+        b.kv_cache.truncate(len(system))
+        assert b.kv_cache.load_shkv(path, fp + "?") is None
+        assert b.kv_cache.load_shkv(tmp_path / "absent.shkv", fp) is None
+        (tmp_path / "short.shkv").write_bytes(data[:-100])
+        assert b.kv_cache.load_shkv(tmp_path / "short.shkv", fp) is None
+        assert b.kv_cache.length == len(system)
+        assert np.array_equal(b.kv_cache.snapshot(len(system)), snap)
+        shared = b.kv_cache.share(len(system))
+        with ctx(small) as c2:
+            c2.kv_cache.adopt(shared)
+            again = c2.forward_selected(request, VERDICT_ROWS)
+        shared.release()
+        assert again.tobytes() == want.tobytes()
+
+
 def test_snapshot_round_trip_and_errors(small):
     with ctx(small) as c:
         c.prefill([1] + toks(70, 4))
