@@ -82,13 +82,17 @@ static void parallel_for(int n, const std::function<void(int)>& body) {
 // ------------------------------------------------------------ GGML types
 
 // ggml_type numbering, GgmlType.cs:9-44 (only what the hot path reads).
-enum GgmlType : uint32_t { F32 = 0, F16 = 1, Q4_0 = 2, Q5_1 = 7, Q8_0 = 8, BF16 = 30 };
+enum GgmlType : uint32_t {
+    F32 = 0, F16 = 1, Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, Q8_1 = 9,
+    Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, BF16 = 30
+};
 
 // GgmlTypeInfo.BlockSize / TypeSize, GgmlType.cs:55-106.
 static int block_size(uint32_t t) {
     switch (t) {
         case F32: case F16: case BF16: return 1;
-        case Q4_0: case Q5_1: case Q8_0: return 32;
+        case Q4_0: case Q4_1: case Q5_0: case Q5_1: case Q8_0: case Q8_1: return 32;
+        case Q2_K: case Q3_K: case Q4_K: case Q5_K: case Q6_K: return 256;
         default: throw Error(ERR_UNSUPPORTED, "GGML type " + std::to_string(t) + " is not on the hot path");
     }
 }
@@ -97,8 +101,16 @@ static int type_size(uint32_t t) {
         case F32: return 4;
         case F16: case BF16: return 2;
         case Q4_0: return 2 + 16;
+        case Q4_1: return 2 + 2 + 16;
+        case Q5_0: return 2 + 4 + 16;
         case Q5_1: return 2 + 2 + 4 + 16;
         case Q8_0: return 2 + 32;
+        case Q8_1: return 2 + 2 + 32;
+        case Q2_K: return 84;
+        case Q3_K: return 110;
+        case Q4_K: return 144;
+        case Q5_K: return 176;
+        case Q6_K: return 210;
         default: throw Error(ERR_UNSUPPORTED, "GGML type " + std::to_string(t) + " is not on the hot path");
     }
 }
@@ -188,6 +200,133 @@ static void dequantize(uint32_t type, const uint8_t* src, float* dst, int64_t co
                 float d = half_to_float(rd16(src));
                 const int8_t* qs = (const int8_t*)(src + 2);
                 for (int j = 0; j < 32; j++) dst[j] = d * (float)qs[j];
+            }
+            return;
+        // Q4_1 :184-209  v = d * nibble + m.
+        case Q4_1:
+            for (int64_t b = 0; b < count / 32; b++, src += 20, dst += 32) {
+                float d = half_to_float(rd16(src)), m = half_to_float(rd16(src + 2));
+                const uint8_t* qs = src + 4;
+                for (int j = 0; j < 16; j++) {
+                    float lo = d * (float)(qs[j] & 0x0F), hi = d * (float)(qs[j] >> 4);
+                    dst[j] = lo + m;
+                    dst[16 + j] = hi + m;
+                }
+            }
+            return;
+        // Q5_0 :211-238  v = d * (q5 - 16).
+        case Q5_0:
+            for (int64_t b = 0; b < count / 32; b++, src += 22, dst += 32) {
+                float d = half_to_float(rd16(src));
+                uint32_t qh = rd32(src + 2);
+                const uint8_t* qs = src + 6;
+                for (int j = 0; j < 16; j++) {
+                    int lo = (qs[j] & 0x0F) | (int)(((qh >> j) & 1) << 4);
+                    int hi = (qs[j] >> 4) | (int)(((qh >> (j + 16)) & 1) << 4);
+                    dst[j] = d * (float)(lo - 16);
+                    dst[16 + j] = d * (float)(hi - 16);
+                }
+            }
+            return;
+        // Q8_1 :307-318  v = d * q (the stored block sum plays no part).
+        case Q8_1:
+            for (int64_t b = 0; b < count / 32; b++, src += 36, dst += 32) {
+                float d = half_to_float(rd16(src));
+                const int8_t* qs = (const int8_t*)(src + 4);
+                for (int j = 0; j < 32; j++) dst[j] = d * (float)qs[j];
+            }
+            return;
+        // Q2_K :323-344  per 16: dl = d * (sc & 15), ml = dmin * (sc >> 4); v = dl * q - ml.
+        case Q2_K:
+            for (int64_t b = 0; b < count / 256; b++, src += 84, dst += 256) {
+                const uint8_t* scales = src;
+                const uint8_t* qs = src + 16;
+                float d = half_to_float(rd16(src + 80)), dmin = half_to_float(rd16(src + 82));
+                int o = 0;
+                for (int g = 0; g < 2; g++)
+                    for (int s = 0; s < 4; s++)
+                        for (int j = 0; j < 32; j++, o++) {
+                            int sb = o >> 4;
+                            float dl = d * (float)(scales[sb] & 0x0F), ml = dmin * (float)(scales[sb] >> 4);
+                            int q = (qs[g * 32 + j] >> (2 * s)) & 3;
+                            float p = dl * (float)q;
+                            dst[o] = p - ml;
+                        }
+            }
+            return;
+        // Q3_K :346-376  6-bit signed scales per 16; v = d * sc * (ql - 4 * (1 - hbit)).
+        case Q3_K:
+            for (int64_t b = 0; b < count / 256; b++, src += 110, dst += 256) {
+                const uint8_t* hmask = src;
+                const uint8_t* qs = src + 32;
+                const uint8_t* scales = src + 96;
+                float d = half_to_float(rd16(src + 108));
+                int sc[16];
+                for (int k = 0; k < 16; k++) {
+                    int low = scales[k & 7] >> (k < 8 ? 0 : 4);
+                    int high = scales[8 + (k & 3)] >> (2 * (k >> 2));
+                    sc[k] = (int)(int8_t)(((low & 0x0F) | ((high & 0x03) << 4)) - 32);
+                }
+                int o = 0;
+                for (int g = 0; g < 2; g++)
+                    for (int s = 0; s < 4; s++)
+                        for (int j = 0; j < 32; j++, o++) {
+                            int ql = (qs[g * 32 + j] >> (2 * s)) & 3;
+                            int qh = ((hmask[j] >> (g * 4 + s)) & 1) ^ 1;
+                            float t = d * (float)sc[o >> 4];
+                            dst[o] = t * (float)(ql - (qh << 2));
+                        }
+            }
+            return;
+        // Q4_K :396-419 / Q5_K :421-448  per 32: dl = d * sc, ml = dmin * mn; v = dl * q - ml,
+        // the 6-bit scale/min pairs unpacked as UnpackK4Scales (:385-394) does.
+        case Q4_K:
+        case Q5_K: {
+            const bool five = type == Q5_K;
+            const int bytes = five ? 176 : 144;
+            for (int64_t b = 0; b < count / 256; b++, src += bytes, dst += 256) {
+                float d = half_to_float(rd16(src)), dmin = half_to_float(rd16(src + 2));
+                const uint8_t* p = src + 4;
+                uint8_t sc[8], mn[8];
+                for (int i = 0; i < 4; i++) {
+                    sc[i] = p[i] & 0x3F;
+                    mn[i] = p[4 + i] & 0x3F;
+                    sc[4 + i] = (uint8_t)((p[8 + i] & 0x0F) | ((p[i] >> 2) & 0x30));
+                    mn[4 + i] = (uint8_t)((p[8 + i] >> 4) | ((p[4 + i] >> 2) & 0x30));
+                }
+                const uint8_t* qh = src + 16;
+                const uint8_t* qs = src + (five ? 48 : 16);
+                int o = 0;
+                for (int g = 0; g < 4; g++)
+                    for (int s = 0; s < 2; s++) {
+                        int sb = g * 2 + s;
+                        float dl = d * (float)sc[sb], ml = dmin * (float)mn[sb];
+                        for (int j = 0; j < 32; j++, o++) {
+                            int q = (qs[g * 32 + j] >> (4 * s)) & 0x0F;
+                            if (five) q |= ((qh[j] >> sb) & 1) << 4;
+                            float t = dl * (float)q;
+                            dst[o] = t - ml;
+                        }
+                    }
+            }
+            return;
+        }
+        // Q6_K :450-471  v = d * scales[o / 16] * (q6 - 32).
+        case Q6_K:
+            for (int64_t b = 0; b < count / 256; b++, src += 210, dst += 256) {
+                const uint8_t* ql = src;
+                const uint8_t* qh = src + 128;
+                const int8_t* scales = (const int8_t*)(src + 192);
+                float d = half_to_float(rd16(src + 208));
+                int o = 0;
+                for (int g = 0; g < 2; g++)
+                    for (int s = 0; s < 2; s++)
+                        for (int j = 0; j < 64; j++, o++) {
+                            int lo = (ql[g * 64 + j] >> (4 * s)) & 0x0F;
+                            int hi = (qh[g * 32 + (j & 31)] >> (2 * (s * 2 + (j >> 5)))) & 0x03;
+                            float t = d * (float)scales[o >> 4];
+                            dst[o] = t * (float)((lo | (hi << 4)) - 32);
+                        }
             }
             return;
         default:

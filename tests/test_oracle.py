@@ -16,8 +16,11 @@ from conftest import GOLDEN
 from oracle import binding as ob
 from small_model import SMALL_PROMPT, VERDICT_ROWS
 
-TYPE_IDS = {"F32": 0, "F16": 1, "Q4_0": 2, "Q5_1": 7, "Q8_0": 8}
-GEOMETRY = {"Q4_0": (32, 18), "Q5_1": (32, 24), "Q8_0": (32, 34), "F32": (1, 4), "F16": (1, 2)}
+TYPE_IDS = {"F32": 0, "F16": 1, "Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11,
+            "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+GEOMETRY = {"Q4_0": (32, 18), "Q4_1": (32, 20), "Q5_0": (32, 22), "Q5_1": (32, 24), "Q8_0": (32, 34), "F32": (1, 4),
+            "F16": (1, 2), "Q2_K": (256, 84), "Q3_K": (256, 110), "Q4_K": (256, 144), "Q5_K": (256, 176),
+            "Q6_K": (256, 210)}
 
 
 def close(expected, actual, rel, what=""):
