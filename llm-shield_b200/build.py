@@ -28,7 +28,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                      "-Xcompiler", "-Wall,-Wno-unused-function", "-I", str(PKG.parent / "include")]
 
-SOURCES = ["gguf.cpp", "runtime.cu", "kernels_quant.cu", "kernels_elem.cu", "kernels_attn.cu", "attn_tc.cu", "gemm_tc.cu",
+SOURCES = ["gguf.cpp", "qx.cpp", "runtime.cu", "kernels_quant.cu", "kernels_elem.cu", "kernels_attn.cu", "attn_tc.cu", "gemm_tc.cu",
            "quantmatmul.cu", "noalloc.cu", "kernels_decode.cu"]
 
 

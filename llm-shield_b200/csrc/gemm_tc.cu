@@ -55,6 +55,23 @@ __device__ __forceinline__ uint32_t hu(__half2 h) { return *reinterpret_cast<uin
 template <int TYPE>
 __device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r, int c) {
     uint4 o;
+    if (TYPE == T_QX) {
+        // v = (a * q) + c in fp32, then one rounding to fp16 (the others' rounding too)
+        const uint2 q = *(const uint2*)(raw + r * 64 + c * 8);
+        const float a = *(const float*)(raw + 8192 + (r * 4 + (c >> 1)) * 4);
+        const float cc = *(const float*)(raw + 10240 + (r * 4 + (c >> 1)) * 4);
+        const int8_t* qb = (const int8_t*)&q;
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            w[i] = hu(__floats2half2_rn(__fadd_rn(__fmul_rn(a, (float)qb[2 * i]), cc),
+                                        __fadd_rn(__fmul_rn(a, (float)qb[2 * i + 1]), cc)));
+        o.x = w[0];
+        o.y = w[1];
+        o.z = w[2];
+        o.w = w[3];
+        return o;
+    }
     if (TYPE == T_Q8_0) {
         uint2 q = *(const uint2*)(raw + r * 64 + c * 8);
         __half2 d2 = __half2half2(*(const __half*)(raw + 8192 + (r * 2 + (c >> 2)) * 2));
@@ -915,6 +932,7 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.ncols = nc;
     if (!gemm_on_smem_a()) {
         // k_gemm_tm: shared memory holds only the activation ring (up to 8 stages in ~222 KB).
+        if (TYPE == T_QX) throw Error(JV_ERR_UNSUPPORTED, "gemm: the TMEM-operand kernel takes Q8_0, Q5_1 and Q4_0 only");
         if (a.bn > TM_MAX_BN) throw Error(JV_ERR_ARG, "gemm: token tile above 224 for the TMEM-operand kernel");
         const size_t budget = 222 * 1024, stage = (size_t)a.bn * 128;
         p.ns = (int)std::min<size_t>(8, budget / stage);
@@ -984,6 +1002,7 @@ void launch_gemm(const GemmArgs& a, cudaStream_t s) {
         case T_Q8_0: launch_tc_epi<T_Q8_0>(a, s); break;
         case T_Q4_0: launch_tc_epi<T_Q4_0>(a, s); break;
         case T_Q5_1: launch_tc_epi<T_Q5_1>(a, s); break;
+        case T_QX: launch_tc_epi<T_QX>(a, s); break;
         default: throw Error(JV_ERR_UNSUPPORTED, "gemm: weight type not on the B200 path");
     }
 }
@@ -1020,6 +1039,7 @@ void launch_gemm_reference(const GemmArgs& a, cudaStream_t s) {
     switch (a.w->type) {
         case T_Q8_0: k_gemm_ref<T_Q8_0><<<grid, 128, 0, s>>>(a.w->data, a.w->ksteps, a.x, a.T, a.tpad, a.y, a.ldy, a.epilogue); break;
         case T_Q4_0: k_gemm_ref<T_Q4_0><<<grid, 128, 0, s>>>(a.w->data, a.w->ksteps, a.x, a.T, a.tpad, a.y, a.ldy, a.epilogue); break;
+        case T_QX: k_gemm_ref<T_QX><<<grid, 128, 0, s>>>(a.w->data, a.w->ksteps, a.x, a.T, a.tpad, a.y, a.ldy, a.epilogue); break;
         default: k_gemm_ref<T_Q5_1><<<grid, 128, 0, s>>>(a.w->data, a.w->ksteps, a.x, a.T, a.tpad, a.y, a.ldy, a.epilogue); break;
     }
     note_launch();

@@ -18,7 +18,8 @@ namespace jv {
 int Gguf::block_size(int type) {
     switch (type) {
         case T_F32: case T_F16: case T_BF16: return 1;
-        case T_Q4_0: case T_Q5_1: case T_Q8_0: return 32;
+        case T_Q4_0: case T_Q4_1: case T_Q5_0: case T_Q5_1: case T_Q8_0: case T_Q8_1: return 32;
+        case T_Q2_K: case T_Q3_K: case T_Q4_K: case T_Q5_K: case T_Q6_K: return 256;
         default: return -1;
     }
 }
@@ -27,8 +28,16 @@ int Gguf::type_size(int type) {
         case T_F32: return 4;
         case T_F16: case T_BF16: return 2;
         case T_Q4_0: return 18;
+        case T_Q4_1: return 20;
+        case T_Q5_0: return 22;
         case T_Q5_1: return 24;
         case T_Q8_0: return 34;
+        case T_Q8_1: return 36;
+        case T_Q2_K: return 84;
+        case T_Q3_K: return 110;
+        case T_Q4_K: return 144;
+        case T_Q5_K: return 176;
+        case T_Q6_K: return 210;
         default: return -1;
     }
 }

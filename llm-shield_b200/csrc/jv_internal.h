@@ -31,7 +31,13 @@ struct Error : std::runtime_error {
 // ------------------------------------------------------------- GGML types
 
 // ggml_type numbering (reference src/Jevstral/Gguf/GgmlType.cs:9-44).
-enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_1 = 7, T_Q8_0 = 8, T_BF16 = 30 };
+enum GgmlType : int {
+    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q8_1 = 9,
+    T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_BF16 = 30,
+    // Not a GGML type: the affine layout (qx.cpp) that every other block format is converted to
+    // on load: per 16 weights, v = (a * q) + c with int8 q and fp32 a, c.
+    T_QX = 64
+};
 
 // Tile geometry of a quantized matrix in HBM. The GGUF blocks of 128 consecutive rows ×
 // 64 consecutive columns are gathered into one contiguous "chunk", split into planes so
@@ -41,13 +47,20 @@ enum GgmlType : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_1 = 7, T_Q8_0 = 8, 
 //   Q8_0: qs  int8 [128][64]   | d fp16 [128][2]                                  = 8704 B
 //   Q4_0: qs  u8   [128][2][16] | d fp16 [128][2]                                 = 4608 B
 //   Q5_1: qs  u8   [128][2][16] | qh u32 [128][2] | d fp16 [128][2] | m fp16 [128][2] = 6144 B
+//   QX:   q   int8 [128][64]    | a fp32 [128][4]  | c fp32 [128][4] (per 16 columns) = 12288 B
 constexpr int TILE_ROWS = 128;
 constexpr int TILE_K = 64;
 
 __host__ __device__ constexpr int chunk_bytes(int type) {
-    return type == T_Q8_0 ? 8704 : type == T_Q4_0 ? 4608 : type == T_Q5_1 ? 6144 : 0;
+    return type == T_Q8_0 ? 8704 : type == T_Q4_0 ? 4608 : type == T_Q5_1 ? 6144 : type == T_QX ? 12288 : 0;
 }
-__host__ __device__ constexpr int qs_bytes(int type) { return type == T_Q8_0 ? 8192 : 4096; }
+__host__ __device__ constexpr int qs_bytes(int type) { return type == T_Q8_0 || type == T_QX ? 8192 : 4096; }
+
+// qx.cpp: the GGUF formats with an affine form, and their conversion to row-major T_QX rows
+// (per 64 columns: 64 int8 q, 4 fp32 a, 4 fp32 c) for the device re-tiling.
+bool qx_expressible(int type);
+int64_t qx_row_bytes(int cols);
+void qx_convert_rows(int type, const uint8_t* src, int64_t src_row_bytes, int rows, int cols, uint8_t* dst);
 
 struct QWeight {
     int type = 0;

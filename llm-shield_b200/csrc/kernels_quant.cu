@@ -26,7 +26,8 @@ int64_t launches_total() { return g_launches.load(); }
 __global__ void k_repack(const uint8_t* __restrict__ raw, int type, int rows, int cols, int64_t raw_row_bytes,
                          uint8_t* __restrict__ dst, int ksteps, int row_in_tile_base, int tile_offset,
                          int interleave) {
-    int blocks_per_row = cols / 32;
+    const int unit = type == T_QX ? 64 : 32;  // QX rows come in 96-byte units of 64 columns
+    int blocks_per_row = cols / unit;
     int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)rows * blocks_per_row) return;
     int j = (int)(idx / blocks_per_row), b = (int)(idx % blocks_per_row);
@@ -39,10 +40,15 @@ __global__ void k_repack(const uint8_t* __restrict__ raw, int type, int rows, in
         tile = tile_offset + j / 128;
         rit = j % 128;
     }
-    int ks = b >> 1, half = b & 1;
+    int ks = type == T_QX ? b : b >> 1, half = b & 1;
     uint8_t* chunk = dst + ((int64_t)tile * ksteps + ks) * chunk_bytes(type);
     const uint8_t* src = raw + (int64_t)j * raw_row_bytes;
-    if (type == T_Q8_0) {
+    if (type == T_QX) {  // 64 q, 4 a, 4 c of one 64-column unit
+        src += (int64_t)b * 96;
+        for (int i = 0; i < 64; i++) chunk[rit * 64 + i] = src[i];
+        for (int i = 0; i < 16; i++) chunk[8192 + rit * 16 + i] = src[64 + i];
+        for (int i = 0; i < 16; i++) chunk[10240 + rit * 16 + i] = src[80 + i];
+    } else if (type == T_Q8_0) {
         src += (int64_t)b * 34;
         for (int i = 0; i < 32; i++) chunk[rit * 64 + half * 32 + i] = src[2 + i];
         chunk[8192 + (rit * 2 + half) * 2] = src[0];
@@ -67,7 +73,7 @@ void launch_repack(const uint8_t* raw, int type, int rows, int cols, int64_t raw
                    int dst_tiles, int ksteps, int row_in_tile_base, int tile_offset, int interleave,
                    cudaStream_t s) {
     (void)dst_tiles;
-    int64_t n = (int64_t)rows * (cols / 32);
+    int64_t n = (int64_t)rows * (cols / (type == T_QX ? 64 : 32));
     int threads = 256;
     int64_t grid = (n + threads - 1) / threads;
     k_repack<<<(unsigned)grid, threads, 0, s>>>(raw, type, rows, cols, raw_row_bytes, dst, ksteps, row_in_tile_base,
@@ -80,6 +86,11 @@ void launch_repack(const uint8_t* raw, int type, int rows, int cols, int64_t raw
 __device__ __forceinline__ float dq_element(const uint8_t* __restrict__ data, int type, int ksteps, int r, int k) {
     int tile = r >> 7, rit = r & 127, ks = k >> 6, kk = k & 63, half = kk >> 5, e = kk & 31;
     const uint8_t* chunk = data + ((int64_t)tile * ksteps + ks) * chunk_bytes(type);
+    if (type == T_QX) {
+        const float a = *(const float*)(chunk + 8192 + (rit * 4 + (kk >> 4)) * 4);
+        const float c = *(const float*)(chunk + 10240 + (rit * 4 + (kk >> 4)) * 4);
+        return __fadd_rn(__fmul_rn(a, (float)(int8_t)chunk[rit * 64 + kk]), c);
+    }
     if (type == T_Q8_0) {
         float d = __half2float(*(const __half*)(chunk + 8192 + (rit * 2 + half) * 2));
         return __fmul_rn(d, (float)(int8_t)chunk[rit * 64 + kk]);
@@ -133,7 +144,19 @@ constexpr int GEMV_UNROLL = 4;
 template <int TYPE>
 __device__ __forceinline__ float gemv_chunk(const uint8_t* __restrict__ chunk, const float* __restrict__ xs, int rit,
                                            int half, float acc) {
-    if (TYPE == T_Q8_0) {
+    if (TYPE == T_QX) {
+        const int4* q = (const int4*)(chunk + rit * 64 + half * 32);
+        int4 qa = __ldg(q), qb = __ldg(q + 1);
+        const float2 a = __ldg((const float2*)(chunk + 8192 + (rit * 4 + half * 2) * 4));
+        const float2 c = __ldg((const float2*)(chunk + 10240 + (rit * 4 + half * 2) * 4));
+        const int8_t* p0 = (const int8_t*)&qa;
+        const int8_t* p1 = (const int8_t*)&qb;
+#pragma unroll
+        for (int i = 0; i < 16; i++) acc = fmaf(xs[i], __fadd_rn(__fmul_rn(a.x, (float)p0[i]), c.x), acc);
+#pragma unroll
+        for (int i = 0; i < 16; i++) acc = fmaf(xs[16 + i], __fadd_rn(__fmul_rn(a.y, (float)p1[i]), c.y), acc);
+        return acc;
+    } else if (TYPE == T_Q8_0) {
         const int4* q = (const int4*)(chunk + rit * 64 + half * 32);
         int4 a = __ldg(q), b = __ldg(q + 1);
         float d = __half2float(__ldg((const __half*)(chunk + 8192 + (rit * 2 + half) * 2)));
@@ -224,6 +247,10 @@ void launch_gemv(const QWeight& w, const float* x, float* partial, int splits, c
         if (smem > 48 * 1024)
             JV_CUDA(cudaFuncSetAttribute(k_gemv<T_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         k_gemv<T_Q4_0><<<grid, GEMV_THREADS, smem, s>>>(w.data, w.ksteps, w.rows, x, partial, splits);
+    } else if (w.type == T_QX) {
+        if (smem > 48 * 1024)
+            JV_CUDA(cudaFuncSetAttribute(k_gemv<T_QX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        k_gemv<T_QX><<<grid, GEMV_THREADS, smem, s>>>(w.data, w.ksteps, w.rows, x, partial, splits);
     } else {
         if (smem > 48 * 1024)
             JV_CUDA(cudaFuncSetAttribute(k_gemv<T_Q5_1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

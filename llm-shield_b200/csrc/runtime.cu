@@ -129,6 +129,7 @@ struct jv_model {
     float mscale = 1.f;
     QWeight embd, head;  // head == embd when the LM head is tied (no output.weight)
     bool tied = true;
+    bool has_qx = false;  // some matrix was converted to the affine layout (no fused decode kernels)
     float* out_norm = nullptr;
     std::vector<LayerW> layers;
     float2* rope_table = nullptr;
@@ -273,10 +274,30 @@ void set_device(const jv_model* m) { JV_CUDA(cudaSetDevice(m->device)); }
 
 // ------------------------------------------------------------ model load
 
+bool native_type(int t) { return t == T_Q8_0 || t == T_Q4_0 || t == T_Q5_1; }
+
+// The device layout of a matrix assembled from GGUF tensors of `types`: their own when they are
+// one of the three formats the kernels decode directly, else the affine layout T_QX, which takes
+// every other block format (and mixes of them, as the K-quant files do per tensor).
+int pick_type(std::initializer_list<int> types, const std::string& what) {
+    const int first = *types.begin();
+    bool same = true, affine = true;
+    for (int t : types) {
+        same &= t == first;
+        affine &= qx_expressible(t);
+    }
+    if (same && native_type(first)) return first;
+    if (affine) return T_QX;
+    throw Error(JV_ERR_UNSUPPORTED, what + ": weight type " + std::to_string(first) +
+                                        " is not on the B200 path (Q8_0, Q5_1, Q4_0, and Q4_1, Q5_0, Q8_1, Q2_K-Q6_K "
+                                        "through the affine layout, are)");
+}
+
 QWeight alloc_qweight(jv_model* m, int type, int rows, int cols) {
-    if (type != T_Q8_0 && type != T_Q4_0 && type != T_Q5_1)
+    if (!native_type(type) && type != T_QX)
         throw Error(JV_ERR_UNSUPPORTED, "weight type " + std::to_string(type) +
                                             " is not on the B200 path (Q8_0, Q5_1 and Q4_0 are)");
+    if (type == T_QX) m->has_qx = true;
     if (rows % TILE_ROWS != 0 || cols % TILE_K != 0)
         throw Error(JV_ERR_UNSUPPORTED, "matrix " + std::to_string(rows) + "x" + std::to_string(cols) +
                                             " does not tile into 128 rows x 64 columns");
@@ -309,15 +330,24 @@ struct Loader {
         rows = (int)t.shape[1];
         cols = (int)t.shape[0];
     }
-    // Upload a GGUF matrix's raw rows and re-tile them into w.
+    // Upload a GGUF matrix's raw rows and re-tile them into w. For the affine layout the rows
+    // are converted on the host first (qx.cpp), then re-tiled the same way.
     void upload(const GgufTensor& t, QWeight& w, int tile_offset, int interleave, int rit_base) {
         int rows, cols;
         matrix_shape(t, rows, cols);
-        if (t.type != w.type)
+        if (t.type != w.type && w.type != T_QX)
             throw Error(JV_ERR_UNSUPPORTED, "'" + t.name + "' is " + std::to_string(t.type) +
                                                 " but the fused matrix it belongs to is " + std::to_string(w.type));
         if (cols != w.cols) throw Error(JV_ERR_FORMAT, "'" + t.name + "' width disagrees with its fused matrix");
         int64_t rb = Gguf::row_bytes(t.type, cols);
+        const uint8_t* src = g.data(t);
+        std::vector<uint8_t> converted;
+        if (w.type == T_QX) {
+            converted.resize((size_t)qx_row_bytes(cols) * rows);
+            qx_convert_rows(t.type, src, rb, rows, cols, converted.data());
+            src = converted.data();
+            rb = qx_row_bytes(cols);
+        }
         size_t bytes = (size_t)rb * rows;
         if (bytes > staging_cap) {
             if (staging) cudaFree(staging);
@@ -325,8 +355,8 @@ struct Loader {
             staging = dalloc<uint8_t>(bytes);
             staging_cap = bytes;
         }
-        JV_CUDA(cudaMemcpyAsync(staging, g.data(t), bytes, cudaMemcpyHostToDevice, s));
-        launch_repack(staging, t.type, rows, cols, rb, w.data, w.tiles, w.ksteps, rit_base, tile_offset, interleave, s);
+        JV_CUDA(cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, s));
+        launch_repack(staging, w.type, rows, cols, rb, w.data, w.tiles, w.ksteps, rit_base, tile_offset, interleave, s);
         JV_CUDA(cudaStreamSynchronize(s));
     }
     float* vector(const std::string& name, int n) {
@@ -450,14 +480,14 @@ void load_model(jv_model* m, const std::string& path, int kv_pool_mb) {
         L.matrix_shape(t, rows, cols);
         if (cols != c.hidden)
             throw Error(JV_ERR_FORMAT, "token_embd is " + std::to_string(cols) + " wide but the model's hidden size is " + std::to_string(c.hidden) + ".");
-        m->embd = alloc_qweight(m, t.type, rows, cols);
+        m->embd = alloc_qweight(m, pick_type({t.type}, "token_embd"), rows, cols);
         L.upload(t, m->embd, 0, 0, 0);
         if (c.vocab > rows) c.vocab = rows;
     }
     if (const GgufTensor* t = g.tensor("output.weight")) {
         int rows, cols;
         L.matrix_shape(*t, rows, cols);
-        m->head = alloc_qweight(m, t->type, rows, cols);
+        m->head = alloc_qweight(m, pick_type({t->type}, "output"), rows, cols);
         L.upload(*t, m->head, 0, 0, 0);
         m->tied = false;
     } else {
@@ -488,26 +518,27 @@ void load_model(jv_model* m, const std::string& path, int kv_pool_mb) {
         L.matrix_shape(tg, r, k);
         if (r != c.ff) throw Error(JV_ERR_FORMAT, "ffn_gate has " + std::to_string(r) + " rows; expected " + std::to_string(c.ff) + ".");
         // [Wq; Wk; Wv] as one matrix: one GEMM writes q | k | v per token.
-        W.qkv = alloc_qweight(m, tq.type, qdim + 2 * kvdim, c.hidden);
+        W.qkv = alloc_qweight(m, pick_type({tq.type, tk.type, tv.type}, p + "attn_q/k/v"), qdim + 2 * kvdim, c.hidden);
         L.upload(tq, W.qkv, 0, 0, 0);
         L.upload(tk, W.qkv, qdim / TILE_ROWS, 0, 0);
         L.upload(tv, W.qkv, (qdim + kvdim) / TILE_ROWS, 0, 0);
         int orows, ocols;
         L.matrix_shape(to, orows, ocols);
-        W.o = alloc_qweight(m, to.type, orows, ocols);
+        W.o = alloc_qweight(m, pick_type({to.type}, p + "attn_output"), orows, ocols);
         L.upload(to, W.o, 0, 0, 0);
         // gate and up interleaved in alternating 16-row groups of each 128-row tile.
-        W.gu = alloc_qweight(m, tg.type, 2 * c.ff, c.hidden);
+        W.gu = alloc_qweight(m, pick_type({tg.type, tu.type}, p + "ffn_gate/up"), 2 * c.ff, c.hidden);
         L.upload(tg, W.gu, 0, 1, 0);
         L.upload(tu, W.gu, 0, 1, 16);
         int drows, dcols;
         L.matrix_shape(td, drows, dcols);
-        W.down = alloc_qweight(m, td.type, drows, dcols);
+        W.down = alloc_qweight(m, pick_type({td.type}, p + "ffn_down"), drows, dcols);
         L.upload(td, W.down, 0, 0, 0);
         if (W.o.rows != c.hidden || W.o.cols != qdim || W.down.rows != c.hidden || W.down.cols != c.ff)
             throw Error(JV_ERR_FORMAT, "blk." + std::to_string(l) + " projection shapes disagree with the config");
     }
-    c.weight_type = m->layers.empty() ? m->embd.type : m->layers[0].qkv.type;
+    // the file's own type of the first layer's query projection (the embedding's when there are none)
+    c.weight_type = g.tensor(c.layers > 0 ? "blk.0.attn_q.weight" : "token_embd.weight")->type;
 
     // RoPE table for every position the context window allows.
     m->rope_positions = std::max(c.context_length, 32768);
@@ -1051,7 +1082,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
     size_t total_words = items_off + n_items_words;
     // A single token without an activation sink runs the fused decode kernels, which read
     // the step from device memory (appended to the same upload).
-    const bool fused = decode && x->sink == nullptr;
+    const bool fused = decode && x->sink == nullptr && !m->has_qx;
     const size_t step_off = (total_words + 7) & ~(size_t)7;
     if (fused) total_words = step_off + sizeof(DecodeStep) / 4;
     int32_t* hin = x->h_in.get(total_words);
@@ -1636,7 +1667,8 @@ int jv_decode_greedy(jv_ctx* x, int32_t first_token, int32_t steps, int32_t* out
         if (steps <= 0) return;
         jv_model* m = x->m;
         set_device(m);
-        if (x->sink) {  // activation capture: the step-by-step path, every activation observed
+        if (x->sink || m->has_qx) {  // activation capture, or affine-layout weights (no fused decode
+                                     // kernels): the step-by-step path
             int32_t tok = first_token;
             for (int i = 0; i < steps; i++) {
                 forward(x, &tok, 1, nullptr, nullptr, 0, false, nullptr, true, nullptr);

@@ -116,6 +116,66 @@ void q5_1(const float* x, uint8_t* out) {
 
 int block_bytes(int type) { return type == 8 ? 34 : type == 2 ? 18 : type == 7 ? 24 : type == 0 ? 128 : -1; }
 
+// Formats written as random blocks (no quantizer: the bytes are drawn directly, with scales
+// chosen so the decoded weights spread like N(0, 0.02^2) on average). GGML ids: Q4_1 3, Q5_0 6,
+// Q2_K 10, Q3_K 11, Q4_K 12, Q5_K 13, Q6_K 14. Returns {weights per block, bytes per block}.
+bool random_block_type(int type, int& bw, int& bb) {
+    switch (type) {
+        case 3: bw = 32; bb = 20; return true;
+        case 6: bw = 32; bb = 22; return true;
+        case 10: bw = 256; bb = 84; return true;
+        case 11: bw = 256; bb = 110; return true;
+        case 12: bw = 256; bb = 144; return true;
+        case 13: bw = 256; bb = 176; return true;
+        case 14: bw = 256; bb = 210; return true;
+        default: return false;
+    }
+}
+
+void random_block(int type, uint64_t key, uint8_t* out) {
+    int bw, bb;
+    random_block_type(type, bw, bb);
+    uint64_t st = splitmix64(key);
+    for (int i = 0; i < bb; i += 8) {
+        st = splitmix64(st);
+        for (int j = 0; j < 8 && i + j < bb; j++) out[i + j] = (uint8_t)(st >> (8 * j));
+    }
+    auto put16 = [&](int off, float v) {
+        uint16_t h = f2h(v);
+        std::memcpy(out + off, &h, 2);
+    };
+    switch (type) {
+        case 3:  // Q4_1: d, m; v = d q + m, q in [0, 15]
+            put16(0, 0.0043f);
+            put16(2, -0.0043f * 7.5f);
+            break;
+        case 6:  // Q5_0: d; v = d (q - 16)
+            put16(0, 0.0022f);
+            break;
+        case 10: {  // Q2_K: scale nibbles >= 1
+            for (int i = 0; i < 16; i++) out[i] = (uint8_t)((out[i] & 0xF0) | (1 + (out[i] & 0x0F) % 15));
+            put16(80, 0.0022f);
+            put16(82, 0.0022f * 1.6f);
+            break;
+        }
+        case 11:  // Q3_K: d (signed 6-bit scales in the packed bytes)
+            put16(108, 0.0005f);
+            break;
+        case 12:  // Q4_K: d, dmin
+            put16(0, 0.00014f);
+            put16(2, 0.00014f * 7.5f);
+            break;
+        case 13:  // Q5_K
+            put16(0, 0.00007f);
+            put16(2, 0.00007f * 15.5f);
+            break;
+        case 14:  // Q6_K: scales in [1, 63], d last
+            for (int i = 192; i < 208; i++) out[i] = (uint8_t)(1 + out[i] % 63);
+            put16(208, 0.000034f);
+            break;
+    }
+}
+
 void quantize_row(int type, const float* x, int64_t cols, uint8_t* out) {
     if (type == 0) {
         std::memcpy(out, x, (size_t)cols * 4);
@@ -151,6 +211,23 @@ void jvs_normal(uint64_t seed, uint32_t tid, float stdev, int64_t n, float* out)
 // weights of tensor `tid`. Returns bytes written or -1.
 int64_t jvs_fill(uint8_t* dst, int type, int64_t rows, int64_t cols, uint64_t seed, uint32_t tid, float stdev,
                  int threads) {
+    int bw, bb;
+    if (random_block_type(type, bw, bb)) {  // random blocks, one counter-based stream per block
+        if (cols % bw != 0) return -1;
+        const int64_t nb = cols / bw, rb = nb * bb;
+        int nt = threads > 0 ? threads : (int)std::max(1u, std::thread::hardware_concurrency());
+        nt = (int)std::min<int64_t>(nt, rows);
+        std::vector<std::thread> pool;
+        for (int w = 0; w < nt; w++)
+            pool.emplace_back([=] {
+                for (int64_t r = w; r < rows; r += nt)
+                    for (int64_t b = 0; b < nb; b++)
+                        random_block(type, splitmix64(seed ^ ((uint64_t)tid << 40)) ^ (uint64_t)(r * nb + b),
+                                     dst + r * rb + b * bb);
+            });
+        for (auto& t : pool) t.join();
+        return rows * rb;
+    }
     if (block_bytes(type) < 0 || (type != 0 && cols % 32 != 0)) return -1;
     int64_t rb = type == 0 ? cols * 4 : cols / 32 * block_bytes(type);
     int nt = threads > 0 ? threads : (int)std::max(1u, std::thread::hardware_concurrency());
@@ -207,7 +284,8 @@ int main(int argc, char** argv) {
     long long off, rows, cols;
     int rc = 0;
     while (std::scanf("%u %lld %lld %lld", &tid, &off, &rows, &cols) == 4) {
-        const int64_t rb = type == 0 ? cols * 4 : cols / 32 * block_bytes(type);
+        int bw, bb;
+        const int64_t rb = type == 0 ? cols * 4 : random_block_type(type, bw, bb) ? cols / bw * bb : cols / 32 * block_bytes(type);
         if (off < 0 || rows <= 0 || off + rows * rb > (long long)st.st_size) {
             std::fprintf(stderr, "jvsynth: tensor %u does not fit the file\n", tid);
             rc = 1;

@@ -31,8 +31,13 @@ PKG = Path(__file__).resolve().parent.parent
 SYNTH_LIB = PKG / "libjvsynth.so"
 SYNTH_EXE = PKG / "jvsynth"
 
-QTYPES = {"F32": 0, "Q4_0": 2, "Q5_1": 7, "Q8_0": 8}
-BLOCK_BYTES = {0: 4, 2: 18, 7: 24, 8: 34}
+QTYPES = {"F32": 0, "Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12,
+          "Q5_K": 13, "Q6_K": 14}
+# (weights, bytes) per block
+BLOCKS = {0: (1, 4), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34), 10: (256, 84), 11: (256, 110),
+          12: (256, 144), 13: (256, 176), 14: (256, 210)}
+# Formats the fast writer fills with random blocks (no quantizer; see gguf_synth.cpp).
+RANDOM_BLOCK_TYPES = ("Q4_1", "Q5_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K")
 YES_ID, NO_ID = 13059, 2649
 
 
@@ -52,6 +57,9 @@ class SynthConfig:
     # "str", "u32" or "f32". yarn_metadata() gives the real checkpoint's RoPE scaling keys.
     extra: Tuple[Tuple[str, str, object], ...] = ()
     norm_gain: float = 1.0  # every RMSNorm gain (1.0 in the benchmark model)
+    # Per-tensor weight types, as (tensor-name suffix, qtype): e.g. (("attn_v.weight", "Q6_K"),
+    # ("ffn_down.weight", "Q6_K")) over a Q4_K file is the layout of a "Q4_K_M" checkpoint.
+    type_overrides: Tuple[Tuple[str, str], ...] = ()
 
 
 MINISTRAL_3B = SynthConfig()
@@ -149,7 +157,8 @@ def _enc_kv(key: str, kind: str, val) -> bytes:
 
 
 def _row_bytes(qtype: int, cols: int) -> int:
-    return cols * 4 if qtype == 0 else cols // 32 * BLOCK_BYTES[qtype]
+    w, b = BLOCKS[qtype]
+    return cols // w * b
 
 
 def _synth_lib():
@@ -185,6 +194,8 @@ def write_random_gguf(path, cfg: SynthConfig = MINISTRAL_3B, qtype: str = "Q8_0"
                       backend: str = "fast", std: float = 0.02) -> Path:
     path = Path(path)
     if backend == "numpy":
+        if qtype in RANDOM_BLOCK_TYPES:
+            raise ValueError(f"{qtype} has no quantizer here; write it with backend='fast' (random blocks)")
         return _write_numpy(path, cfg, qtype, seed, std)
     t = QTYPES[qtype]
     plan = tensor_plan(cfg)
@@ -192,9 +203,15 @@ def write_random_gguf(path, cfg: SynthConfig = MINISTRAL_3B, qtype: str = "Q8_0"
     header = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(plan), len(kv)))
     for k, (kind, v) in kv.items():
         header += _enc_kv(k, kind, v)
+    def type_of(name: str) -> int:
+        for suffix, q in cfg.type_overrides:
+            if name.endswith(suffix):
+                return QTYPES[q]
+        return t
+
     offsets, off = [], 0
     for name, shape, is_mat in plan:
-        tt = t if is_mat else 0
+        tt = type_of(name) if is_mat else 0
         ne = list(reversed(shape))
         header += _enc_str(name) + struct.pack("<I", len(ne)) + b"".join(struct.pack("<Q", d) for d in ne)
         header += struct.pack("<IQ", tt, off)
@@ -215,22 +232,23 @@ def write_random_gguf(path, cfg: SynthConfig = MINISTRAL_3B, qtype: str = "Q8_0"
         if not is_mat:
             mm[base:base + 4 * shape[0]] = np.full(shape[0], cfg.norm_gain, dtype=np.float32).view(np.uint8)
             continue
-        jobs.append((tid, base, shape[0], shape[1], name))
+        jobs.append((tid, base, shape[0], shape[1], name, type_of(name)))
     if backend == "exe":
         mm.flush()
         del mm
         if not SYNTH_EXE.exists():
             raise FileNotFoundError(f"{SYNTH_EXE} is not built; run `python llm-shield_b200/build.py`")
-        plan_text = "".join(f"{tid} {base} {rows} {cols}\n" for tid, base, rows, cols, _ in jobs)
-        r = subprocess.run([str(SYNTH_EXE), str(tmp), str(t), str(seed), repr(float(std)), str(threads)],
-                           input=plan_text, capture_output=True, text=True)
-        if r.returncode != 0:
-            raise RuntimeError(f"jvsynth failed ({r.returncode}): {r.stderr.strip()}")
+        for jt in sorted({j[5] for j in jobs}):  # the program fills one weight type per run
+            plan_text = "".join(f"{tid} {base} {rows} {cols}\n" for tid, base, rows, cols, _, tt in jobs if tt == jt)
+            r = subprocess.run([str(SYNTH_EXE), str(tmp), str(jt), str(seed), repr(float(std)), str(threads)],
+                               input=plan_text, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"jvsynth failed ({r.returncode}): {r.stderr.strip()}")
     else:
         lib = _synth_lib()
-        for tid, base, rows, cols, name in jobs:
-            n = lib.jvs_fill(C.c_void_p(mm.ctypes.data + base), t, rows, cols, seed, tid, std, threads)
-            if n != _row_bytes(t, cols) * rows:
+        for tid, base, rows, cols, name, tt in jobs:
+            n = lib.jvs_fill(C.c_void_p(mm.ctypes.data + base), tt, rows, cols, seed, tid, std, threads)
+            if n != _row_bytes(tt, cols) * rows:
                 raise RuntimeError(f"jvs_fill failed for {name}")
         mm.flush()
         del mm

@@ -54,9 +54,10 @@ def ctx(model, cap=512):
 # ------------------------------------------------------------------ dequant
 
 
-@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
+@pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0", "Q4_1", "Q5_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"])
 def test_embedding_gather_is_bit_exact(model_factory, qtype):
-    """GatherRows decodes rows bit-exactly (d*q, d*(n-8), d*q5+m; no FMA)."""
+    """GatherRows decodes rows bit-exactly (d*q, d*(n-8), d*q5+m; no FMA), the K-quants and the
+    other affine formats through the affine layout (a*q + c per 16 weights)."""
     path = model_factory(SMALL_CFG, qtype, seed=3)
     prompt = [1] + toks(30, 5)
     gpu, cpu = {}, {}
@@ -101,6 +102,74 @@ def test_tree_decision_matches_the_oracle(model_factory, qtype):
     z_gpu, z_cpu = margins_from_verdicts(v_gpu, 1), margins_from_verdicts(v_cpu, 1)
     assert np.abs(z_gpu - z_cpu).max() < Z_TOL
     assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
+
+
+@pytest.mark.parametrize("qtype", ["Q4_K", "Q6_K", "Q2_K", "Q5_K"])
+def test_k_quant_tree_decision_matches_the_oracle(model_factory, qtype):
+    """The K-quant formats (Dequantizer.cs:323-471) on the tensor-core path: weights converted on
+    load to the affine layout and decoded to fp16 in the GEMM; per-layer hidden states and z_i
+    against the oracle."""
+    path = model_factory(SMALL_CFG, qtype, seed=11)
+    trunk = [1] + toks(70, 21)
+    branches = [toks(n, 30 + i) for i, n in enumerate((12, 7, 20, 3, 16))]
+    gpu, cpu = {}, {}
+    with jv.Model(path, kv_pool_mb=128) as m, ctx(m) as c:
+        assert m.config.weight_type == {"Q4_K": 12, "Q6_K": 14, "Q2_K": 10, "Q5_K": 13}[qtype]
+        c.set_activation_sink(capture_into(gpu))
+        c.forward_tree(trunk, branches, VERDICT_ROWS)
+        c.set_activation_sink(None)
+        c.kv_cache.reset()
+        v_gpu = c.forward_tree(trunk, branches, VERDICT_ROWS)
+    with ob.OracleModel(path) as o:
+        v_cpu = o.forward_tree(trunk, branches, VERDICT_ROWS, sink=capture_into(cpu))
+    for l in range(SMALL_CFG.layers):
+        assert rel_l2(gpu[f"blk.{l}.output"], cpu[f"blk.{l}.output"]) < HIDDEN_TOL
+    z_gpu, z_cpu = margins_from_verdicts(v_gpu, 1), margins_from_verdicts(v_cpu, 1)
+    assert np.abs(z_gpu - z_cpu).max() < Z_TOL
+    assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
+
+
+def test_mixed_k_quant_checkpoint_at_full_width_matches_the_oracle(model_factory):
+    """A "Q4_K_M"-style file at every real matrix shape: Q4_K everywhere but attn_v and ffn_down in
+    Q6_K, so the fused QKV matrix mixes two formats. Tree decision (hidden states, z_i), then
+    single-token steps (the step-by-step decode path these files take) and the greedy loop."""
+    from jevstral_b200.synth import SynthConfig
+
+    mix = (("attn_v.weight", "Q6_K"), ("ffn_down.weight", "Q6_K"))
+    cfg = SynthConfig(layers=2, vocab=16384, type_overrides=mix)
+    path = model_factory(cfg, "Q4_K", seed=5)
+    trunk = [1] + toks(190, 7)
+    branches = [toks(n, 40 + i) for i, n in enumerate((32, 17, 48))]
+    gpu, cpu = {}, {}
+    with jv.Model(path, kv_pool_mb=512) as m, ctx(m) as c, ob.OracleModel(path) as o:
+        c.set_activation_sink(capture_into(gpu))
+        v_gpu = c.forward_tree(trunk, branches, VERDICT_ROWS)
+        v_cpu = o.forward_tree(trunk, branches, VERDICT_ROWS, sink=capture_into(cpu))
+        for key in [f"blk.{l}.{n}" for l in range(cfg.layers) for n in ("attn_out", "ffn_out", "output")]:
+            assert rel_l2(gpu[key], cpu[key]) < HIDDEN_TOL, key
+        z_gpu, z_cpu = margins_from_verdicts(v_gpu, 1), margins_from_verdicts(v_cpu, 1)
+        assert np.abs(z_gpu - z_cpu).max() < Z_TOL
+        assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
+        c.set_activation_sink(None)
+        c.kv_cache.reset()
+        o.kv_reset()
+        prompt = [1] + toks(60, 9)
+        c.prefill(prompt)
+        o.forward(prompt, logits=False)
+        nxt = 2000
+        for step in range(3):
+            lg = c.forward([nxt])
+            lo = o.forward([nxt])
+            assert rel_l2(lg, lo) < HIDDEN_TOL, step
+            nxt = int(np.argmax(lo))
+        base = c.kv_cache.length
+        got = c.decode_greedy(1500, 4)
+        c.kv_cache.truncate(base)
+        want, tok = [], 1500
+        for _ in range(4):
+            tok = int(np.argmax(c.forward([tok])))
+            want.append(tok)
+        assert got.tolist() == want
 
 
 @pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])

@@ -82,3 +82,36 @@ def test_the_standalone_writer_gives_the_same_file(tmp_path, qtype):
     a = write_random_gguf(tmp_path / "a.gguf", cfg, qtype, seed=4, backend="fast")
     b = write_random_gguf(tmp_path / "b.gguf", cfg, qtype, seed=4, backend="exe")
     assert a.read_bytes() == b.read_bytes()
+
+
+@pytest.mark.parametrize("qtype", ["Q4_1", "Q5_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"])
+def test_random_block_files_decode_like_the_gguf_package(tmp_path, qtype):
+    """The formats the writer fills with random blocks (there is no quantizer for them here): the
+    file reads back through gguf.GGUFReader, and the oracle decodes each sampled matrix exactly as
+    gguf.quants.dequantize does (the tool the reference's fixtures come from)."""
+    from oracle import binding as ob
+
+    cfg = SynthConfig(layers=1, hidden=256, heads=8, kv_heads=2, head_dim=128, ff=512, vocab=2048)
+    path = write_random_gguf(tmp_path / "k.gguf", cfg, qtype, seed=2, backend="fast")
+    reader = gguf.GGUFReader(str(path))
+    for t in reader.tensors:
+        if not t.name.endswith(("attn_q.weight", "ffn_down.weight", "token_embd.weight")):
+            continue
+        assert t.tensor_type.name == qtype
+        want = gguf.quants.dequantize(np.asarray(t.data), t.tensor_type).reshape(-1).astype(np.float32)
+        got = ob.dequantize(QTYPES[qtype], np.asarray(t.data).reshape(-1), want.size)
+        assert got.view(np.uint32).tobytes() == want.view(np.uint32).tobytes(), t.name
+        assert 0.01 < float(want.std()) < 0.05
+
+
+def test_per_tensor_types_make_a_mixed_k_quant_file(tmp_path):
+    """type_overrides: a Q4_K file whose attn_v and ffn_down are Q6_K (the "Q4_K_M" mix), the same
+    bytes from the in-process and the stand-alone writer."""
+    mix = (("attn_v.weight", "Q6_K"), ("ffn_down.weight", "Q6_K"))
+    cfg = SynthConfig(layers=1, hidden=256, heads=8, kv_heads=2, head_dim=128, ff=512, vocab=2048, type_overrides=mix)
+    a = write_random_gguf(tmp_path / "a.gguf", cfg, "Q4_K", seed=2, backend="fast")
+    b = write_random_gguf(tmp_path / "b.gguf", cfg, "Q4_K", seed=2, backend="exe")
+    assert a.read_bytes() == b.read_bytes()
+    types = {t.name: t.tensor_type.name for t in gguf.GGUFReader(str(a)).tensors}
+    assert types["blk.0.attn_v.weight"] == "Q6_K" and types["blk.0.ffn_down.weight"] == "Q6_K"
+    assert types["blk.0.attn_q.weight"] == "Q4_K" and types["token_embd.weight"] == "Q4_K"
