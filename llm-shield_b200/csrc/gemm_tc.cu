@@ -51,16 +51,45 @@ __device__ __forceinline__ uint32_t hu(__half2 h) { return *reinterpret_cast<uin
 // Decode one (row, 16-byte chunk) item: 8 consecutive weights of row r, k = 8c..8c+7, as
 // packed fp16 pairs. Q8_0 and Q4_0: the integer is exact in fp16 and d * q is one
 // correctly rounded fp16 multiply — the same value as the exact fp32 product rounded to
-// fp16. Q5_1: d * q5 + m with one fp16 rounding (an fp16 FMA).
+// fp16. Q5_1: d * q5 + m with one fp16 rounding (an fp16 FMA). QX: (a * q) + c in fp32, then
+// one rounding to fp16. The raw words an item needs are loaded first (item_load, from shared
+// memory or straight from global memory), then decoded from registers (item_decode).
+struct Item {
+    uint2 q;         // the item's 8 quantized values (bytes or nibble pairs)
+    uint32_t w0, w1, w2;  // Q8_0/Q4_0: d; Q5_1: d, m, qh; QX: a, c
+};
+
 template <int TYPE>
-__device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r, int c) {
+__device__ __forceinline__ Item item_load(const uint8_t* __restrict__ raw, int r, int c) {
+    Item it;
+    if (TYPE == T_Q8_0 || TYPE == T_QX) {
+        it.q = *(const uint2*)(raw + r * 64 + c * 8);
+        if (TYPE == T_Q8_0) {
+            it.w0 = *(const uint16_t*)(raw + 8192 + (r * 2 + (c >> 2)) * 2);
+        } else {
+            it.w0 = *(const uint32_t*)(raw + 8192 + (r * 4 + (c >> 1)) * 4);
+            it.w1 = *(const uint32_t*)(raw + 10240 + (r * 4 + (c >> 1)) * 4);
+        }
+        return it;
+    }
+    const int b = c >> 2, e0 = (c & 3) * 8;
+    it.q = *(const uint2*)(raw + r * 32 + b * 16 + (e0 & 15));
+    if (TYPE == T_Q4_0) {
+        it.w0 = *(const uint16_t*)(raw + 4096 + (r * 2 + b) * 2);
+    } else {
+        it.w0 = *(const uint16_t*)(raw + 5120 + (r * 2 + b) * 2);
+        it.w1 = *(const uint16_t*)(raw + 5632 + (r * 2 + b) * 2);
+        it.w2 = *(const uint32_t*)(raw + 4096 + (r * 2 + b) * 4);
+    }
+    return it;
+}
+
+template <int TYPE>
+__device__ __forceinline__ uint4 item_decode(const Item& it, int c) {
     uint4 o;
     if (TYPE == T_QX) {
-        // v = (a * q) + c in fp32, then one rounding to fp16 (the others' rounding too)
-        const uint2 q = *(const uint2*)(raw + r * 64 + c * 8);
-        const float a = *(const float*)(raw + 8192 + (r * 4 + (c >> 1)) * 4);
-        const float cc = *(const float*)(raw + 10240 + (r * 4 + (c >> 1)) * 4);
-        const int8_t* qb = (const int8_t*)&q;
+        const float a = __uint_as_float(it.w0), cc = __uint_as_float(it.w1);
+        const int8_t* qb = (const int8_t*)&it.q;
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; i++)
@@ -72,29 +101,26 @@ __device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r,
         o.w = w[3];
         return o;
     }
+    const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)it.w0));
     if (TYPE == T_Q8_0) {
-        uint2 q = *(const uint2*)(raw + r * 64 + c * 8);
-        __half2 d2 = __half2half2(*(const __half*)(raw + 8192 + (r * 2 + (c >> 2)) * 2));
-        uint32_t x0 = q.x ^ 0x80808080u, x1 = q.y ^ 0x80808080u;  // int8 -> biased byte b = q + 128
-        const __half2 bias = __floats2half2_rn(1152.f, 1152.f);    // 1024 + 128
+        uint32_t x0 = it.q.x ^ 0x80808080u, x1 = it.q.y ^ 0x80808080u;  // int8 -> biased byte b = q + 128
+        const __half2 bias = __floats2half2_rn(1152.f, 1152.f);        // 1024 + 128
         o.x = hu(__hmul2(__hsub2(byte_pair(x0, 0x4140u), bias), d2));
         o.y = hu(__hmul2(__hsub2(byte_pair(x0, 0x4342u), bias), d2));
         o.z = hu(__hmul2(__hsub2(byte_pair(x1, 0x4140u), bias), d2));
         o.w = hu(__hmul2(__hsub2(byte_pair(x1, 0x4342u), bias), d2));
         return o;
     }
-    int b = c >> 2, e0 = (c & 3) * 8;
-    uint2 q = *(const uint2*)(raw + r * 32 + b * 16 + (e0 & 15));
+    const int e0 = (c & 3) * 8;
     uint32_t x0, x1;
     if (e0 < 16) {
-        x0 = q.x & 0x0F0F0F0Fu;
-        x1 = q.y & 0x0F0F0F0Fu;
+        x0 = it.q.x & 0x0F0F0F0Fu;
+        x1 = it.q.y & 0x0F0F0F0Fu;
     } else {
-        x0 = (q.x >> 4) & 0x0F0F0F0Fu;
-        x1 = (q.y >> 4) & 0x0F0F0F0Fu;
+        x0 = (it.q.x >> 4) & 0x0F0F0F0Fu;
+        x1 = (it.q.y >> 4) & 0x0F0F0F0Fu;
     }
     if (TYPE == T_Q4_0) {
-        __half2 d2 = __half2half2(*(const __half*)(raw + 4096 + (r * 2 + b) * 2));
         const __half2 bias = __floats2half2_rn(1032.f, 1032.f);  // 1024 + 8
         o.x = hu(__hmul2(__hsub2(byte_pair(x0, 0x4140u), bias), d2));
         o.y = hu(__hmul2(__hsub2(byte_pair(x0, 0x4342u), bias), d2));
@@ -103,9 +129,8 @@ __device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r,
         return o;
     }
     // Q5_1: fifth bit of element e from qh bit e, spread into bit 4 of each byte.
-    uint32_t qh = *(const uint32_t*)(raw + 4096 + (r * 2 + b) * 4);
-    __half2 d2 = __half2half2(*(const __half*)(raw + 5120 + (r * 2 + b) * 2));
-    __half2 m2 = __half2half2(*(const __half*)(raw + 5632 + (r * 2 + b) * 2));
+    const uint32_t qh = it.w2;
+    const __half2 m2 = __half2half2(__ushort_as_half((unsigned short)it.w1));
     uint32_t h0 = (qh >> e0) & 0xFu, h1 = (qh >> (e0 + 4)) & 0xFu;
     x0 |= ((h0 & 1u) << 4) | ((h0 & 2u) << 11) | ((h0 & 4u) << 18) | ((h0 & 8u) << 25);
     x1 |= ((h1 & 1u) << 4) | ((h1 & 2u) << 11) | ((h1 & 4u) << 18) | ((h1 & 8u) << 25);
@@ -115,6 +140,11 @@ __device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r,
     o.z = hu(__hfma2(__hsub2(byte_pair(x1, 0x4140u), bias), d2, m2));
     o.w = hu(__hfma2(__hsub2(byte_pair(x1, 0x4342u), bias), d2, m2));
     return o;
+}
+
+template <int TYPE>
+__device__ __forceinline__ uint4 decode8(const uint8_t* __restrict__ raw, int r, int c) {
+    return item_decode<TYPE>(item_load<TYPE>(raw, r, c), c);
 }
 
 constexpr int RAW_PREFETCH = 24;  // raw chunks prefetched into L2 ahead of the shared-memory copies
@@ -908,7 +938,7 @@ static bool gemm_on_smem_a() {
 template <int TYPE, int EPI, bool CSPLIT>
 static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     const QWeight& w = *a.w;
-    TcParams p;
+    TcParams p{};
     p.w = w.data;
     p.x = a.x;
     p.y = a.y;
