@@ -40,6 +40,8 @@ def _load():
         ("orc_last_error", C.c_char_p, []),
         ("orc_set_threads", None, [C.c_int]),
         ("orc_threads", C.c_int, []),
+        ("orc_set_isa", None, [C.c_int]),
+        ("orc_isa", C.c_int, []),
         ("orc_open", C.c_int, [C.c_char_p, C.c_int, C.POINTER(C.c_void_p)]),
         ("orc_close", None, [C.c_void_p]),
         ("orc_config_get", C.c_int, [C.c_void_p, C.POINTER(OrcConfig)]),

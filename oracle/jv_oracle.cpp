@@ -446,9 +446,42 @@ static const int kKBlock = 2048;  // PanelGemm.KBlock, PanelGemm.cs:43
 // Here the 64-row panel is decoded per K block into [k][64] and tokens are streamed
 // six at a time against it with 8-lane AVX2 FMA, which keeps exactly that per-element
 // chain (each lane is its own output row).
+// The same tile with 16-lane AVX-512 vectors (the reference's Tile512x6 width), used when the
+// host has AVX-512F: six tokens against the whole 64-row panel per k, each lane still its own
+// output row's FMA chain in ascending k, so the results are the AVX2 tile's bit for bit.
+__attribute__((target("avx512f"))) static void panel_tile6_avx512(const float* packed, const float* xk, int64_t cols,
+                                                                 int kc, bool acc, float* yr, int64_t rows) {
+    __m512 c[6][4];
+    for (int i = 0; i < 6; i++)
+        for (int h = 0; h < 4; h++)
+            c[i][h] = acc ? _mm512_loadu_ps(yr + i * rows + 16 * h) : _mm512_setzero_ps();
+    const float* p = packed;
+    for (int k = 0; k < kc; k++, p += kPanel) {
+        __m512 b0 = _mm512_loadu_ps(p), b1 = _mm512_loadu_ps(p + 16), b2 = _mm512_loadu_ps(p + 32),
+               b3 = _mm512_loadu_ps(p + 48);
+        for (int i = 0; i < 6; i++) {
+            __m512 a = _mm512_set1_ps(xk[i * cols + k]);
+            c[i][0] = _mm512_fmadd_ps(a, b0, c[i][0]);
+            c[i][1] = _mm512_fmadd_ps(a, b1, c[i][1]);
+            c[i][2] = _mm512_fmadd_ps(a, b2, c[i][2]);
+            c[i][3] = _mm512_fmadd_ps(a, b3, c[i][3]);
+        }
+    }
+    for (int i = 0; i < 6; i++)
+        for (int h = 0; h < 4; h++) _mm512_storeu_ps(yr + i * rows + 16 * h, c[i][h]);
+}
+
+// 0: the widest vectors the host has; 1: the AVX2 tile only (orc_set_isa).
+static int g_isa = 0;
+static bool use_avx512() {
+    static const bool has = __builtin_cpu_supports("avx512f");
+    return has && g_isa == 0;
+}
+
 static void panel_gemm(const Matrix& w, const float* x, int tokens, float* y) {
     int cols = w.cols, rows = w.rows;
     int panels = rows / kPanel;
+    const bool wide = use_avx512();
     parallel_for(panels, [&](int panel) {
         int r0 = panel * kPanel;
         int kb = std::min(cols, kKBlock);
@@ -465,6 +498,9 @@ static void panel_gemm(const Matrix& w, const float* x, int tokens, float* y) {
             const float* xk = x + k0;
             float* yr = y + r0;
             int t = 0;
+            if (wide)
+                for (; t + 6 <= tokens; t += 6)
+                    panel_tile6_avx512(packed.data(), xk + (int64_t)t * cols, cols, kc, acc, yr + (int64_t)t * rows, rows);
             for (; t + 6 <= tokens; t += 6) {
                 for (int s = 0; s < kPanel; s += 16) {
                     __m256 c[6][2];
@@ -1220,6 +1256,8 @@ struct orc_config {
 
 const char* orc_last_error(void) { return g_error.c_str(); }
 void orc_set_threads(int n) { g_threads = n; }
+void orc_set_isa(int isa) { g_isa = isa; }
+int orc_isa(void) { return use_avx512() ? 512 : 256; }
 int orc_threads(void) { return thread_count(); }
 
 int orc_open(const char* path, int initial_capacity, void** out) {

@@ -335,3 +335,21 @@ def test_yarn_frequencies_follow_the_reference_formula(tmp_path):
     # the fast bands keep the base frequency, the slow bands are divided by the factor
     assert np.allclose(got[:8], base[:8], rtol=1e-6)
     assert np.allclose(got[-4:], base[-4:] / 16, rtol=1e-6)
+
+
+def test_the_avx512_tile_gives_the_avx2_tile_s_bits():
+    """The panel GEMM's 16-lane tile (used where the host has AVX-512F, as the reference's
+    Tile512x6 is) keeps each output's FMA chain, so it matches the 8-lane tile bit for bit."""
+    rng = np.random.default_rng(8)
+    raw = rng.integers(0, 256, 128 * 4096 // 32 * 34, dtype=np.uint8)
+    for b in range(128 * 4096 // 32):  # finite fp16 scales
+        raw[b * 34:b * 34 + 2] = np.frombuffer(np.float16(0.01 + 0.001 * (b % 7)).tobytes(), np.uint8)
+    x = rng.normal(0, 1, (13, 4096)).astype(np.float32)
+    try:
+        ob.lib.orc_set_isa(1)
+        narrow = ob.matmul(8, raw, 128, 4096, x, 13)
+        ob.lib.orc_set_isa(0)
+        wide = ob.matmul(8, raw, 128, 4096, x, 13)
+    finally:
+        ob.lib.orc_set_isa(0)
+    assert narrow.tobytes() == wide.tobytes()
