@@ -81,6 +81,13 @@ const char* jv_last_error(void);
 int jv_device_count(int32_t* count);
 /* Counts this library's kernel launches on the calling process (all contexts). */
 int64_t jv_kernel_launches(void);
+/* How this copy of the library was built (no counterpart in the reference): bit 0 set in the
+ * bounds-checked build (libjv_checked.so), whose kernels test every KV page-table lookup and
+ * GEMM work unit and fail the call with JV_ERR_RANGE, naming the site, instead of touching
+ * memory out of range. The check stands in for a memory checker; it is slower and not for
+ * serving. */
+#define JV_FEATURE_BOUNDS_CHECK 1
+int32_t jv_build_features(void);
 
 /* ---- model (weights) ----------------------------------------------------------------- */
 

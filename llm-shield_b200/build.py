@@ -2,6 +2,8 @@
 
 libjv.so     CUDA kernels for sm_100a + the host runtime behind include/jv.h
              (nvcc -gencode arch=compute_100a,code=sm_100a, static CUDA runtime).
+libjv_checked.so  the same with -DJV_BOUNDS_CHECK (index checks that fail the call instead of
+             touching memory out of range; a diagnostic build, selected with JV_LIBRARY).
 libjvsynth.so  the random-weight GGUF filler used by the tests and the benchmark.
 jvsynth        the same filler as a stand-alone program (the benchmark's reference arm).
 
@@ -19,7 +21,9 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 OUT = PKG / "_build"
+OUT_CHECKED = PKG / "_build_checked"
 LIB = PKG / "libjv.so"
+LIB_CHECKED = PKG / "libjv_checked.so"
 SYNTH = PKG / "libjvsynth.so"
 SYNTH_EXE = PKG / "jvsynth"
 
@@ -49,16 +53,23 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 
 
 def build(verbose: bool = False, ptxas: bool = False, force: bool = False) -> Path:
-    OUT.mkdir(exist_ok=True)
+    _build_lib(LIB, OUT, [], verbose, ptxas, force)
+    _build_lib(LIB_CHECKED, OUT_CHECKED, ["-DJV_BOUNDS_CHECK"], verbose, False, force)
+    _build_synth(force, verbose)
+    return LIB
+
+
+def _build_lib(lib: Path, out: Path, extra: list[str], verbose: bool, ptxas: bool, force: bool) -> None:
+    out.mkdir(exist_ok=True)
     headers = list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + [PKG.parent / "include" / "jv.h"]
     jobs = []
     objs = []
     for src in SOURCES:
         s = CSRC / src
-        o = OUT / (src + ".o")
+        o = out / (src + ".o")
         objs.append(o)
         if force or _stale(o, [s] + headers):
-            flags = list(NVCC_FLAGS)
+            flags = list(NVCC_FLAGS) + extra
             if ptxas and src.endswith(".cu"):
                 flags += ["-Xptxas", "-v"]
             jobs.append([NVCC] + flags + (["-x", "cu"] if src.endswith(".cu") else []) + ["-c", str(s), "-o", str(o)])
@@ -69,9 +80,12 @@ def build(verbose: bool = False, ptxas: bool = False, force: bool = False) -> Pa
     if ptxas:
         for log in logs:
             print(log)
-    if force or jobs or _stale(LIB, objs):
-        _run([NVCC] + ARCH + ["-shared", "-o", str(LIB)] + [str(o) for o in objs] +
+    if force or jobs or _stale(lib, objs):
+        _run([NVCC] + ARCH + ["-shared", "-o", str(lib)] + [str(o) for o in objs] +
              ["-cudart", "static", "-lpthread", "-ldl", "-lrt"], verbose)
+
+
+def _build_synth(force: bool, verbose: bool) -> None:
     synth_src = CSRC / "synth" / "gguf_synth.cpp"
     if force or _stale(SYNTH, [synth_src]):
         _run(["g++", "-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math", "-shared", "-o", str(SYNTH),
@@ -79,7 +93,6 @@ def build(verbose: bool = False, ptxas: bool = False, force: bool = False) -> Pa
     if force or _stale(SYNTH_EXE, [synth_src]):
         _run(["g++", "-O3", "-std=c++17", "-DJVS_MAIN", "-ffp-contract=off", "-fno-fast-math", "-o", str(SYNTH_EXE),
               str(synth_src), "-lpthread"], verbose)
-    return LIB
 
 
 if __name__ == "__main__":

@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     if (warp >= 8 && staged) {
         // stage the page-table entries of both key regions
         for (int i = tid - 256; i < pagesA + pagesB; i += 96)
-            pg[i] = __ldg(a.page_table + (i < pagesA ? pA0 + i : pB0 + (i - pagesA)));
+            pg[i] = kv_page(a.page_table, (i < pagesA ? pA0 + i : pB0 + (i - pagesA)) * ps, ps, a.err, BS_ATTN_PAGE);
     }
     tc_fence_before();
     __syncthreads();
@@ -226,8 +226,9 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                         const int slot = reg == 0 ? it.base + La : it.segment + (La - nA);
                         const int row = slot % ps;
                         const int n = min(Lb - La, ps - row);
-                        const int page = !staged ? __ldg(a.page_table + slot / ps)
-                                         : reg == 0 ? pg[slot / ps - pA0] : pg[pagesA + slot / ps - pB0];
+                        const int gi = reg == 0 ? slot / ps - pA0 : pagesA + slot / ps - pB0;
+                        const int page = !staged ? kv_page(a.page_table, slot, ps, err, BS_ATTN_PAGE)
+                                         : JV_CHECK(gi >= 0 && gi < AT_PAGES, err, BS_ATTN_STAGED) ? pg[gi] : 0;
                         const char* plane = pool + (int64_t)page * a.page_bytes;
                         const int key0 = La - L0;
                         if (((key0 - row) & 7) == 0) {

@@ -192,8 +192,8 @@ __device__ __forceinline__ bool dec_better(float v, int i, float bv, int bi) {
 // The (layer, head, K|V) plane of the page holding `slot` (rows inside it are swizzled: see
 // kv_chunk_offset / kv_elem_offset).
 __device__ __forceinline__ char* kv_plane(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots,
-                                          int layer, int kv_heads, int head, int kv, int slot) {
-    return (char*)pool + (int64_t)page_table[slot / page_slots] * page_bytes +
+                                          int layer, int kv_heads, int head, int kv, int slot, int* err) {
+    return (char*)pool + (int64_t)kv_page(page_table, slot, page_slots, err, BS_DECODE_PAGE) * page_bytes +
            kv_plane_offset(layer, kv_heads, head, kv, page_slots);
 }
 

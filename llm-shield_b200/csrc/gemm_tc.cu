@@ -374,6 +374,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 int tile, tt, sp;
                 unit_coords(u, splits, ttiles, tile, tt, sp);
                 const int kb = sp * nks, t0 = tt * bn;
+                if (!JV_CHECK(tile < p.tiles && kb + nks <= ksteps && t0 + bn <= tpad, g_err, BS_GEMM_UNIT)) break;
                 const uint8_t* src = weights ? g_w + ((int64_t)tile * ksteps + kb) * cb
                                              : (const uint8_t*)(g_x + ((int64_t)kb * tpad + t0) * 64);
                 const int64_t step = weights ? (int64_t)cb : (int64_t)tpad * 128;

@@ -151,6 +151,48 @@ __device__ __forceinline__ void report_numeric(int* err, int site) {
 }
 #endif
 
+// Bounds-checked builds (-DJV_BOUNDS_CHECK, libjv_checked.so): the index sites below test what
+// they are about to use and, when it is out of range, record JV_ERR_RANGE with the site in the
+// error word and use a safe stand-in instead (page 0, or the access skipped), so a bad index is
+// reported rather than read or written. Normal builds compile the checks away.
+enum BoundsSite : int {
+    BS_ROPE_PAGE = 80, BS_ATTN_PAGE = 81, BS_ATTN_STAGED = 82, BS_MMA_ATTN_PAGE = 83, BS_DECODE_PAGE = 84,
+    BS_GEMM_UNIT = 85, BS_SNAPSHOT_PAGE = 86
+};
+#ifdef __CUDACC__
+__device__ __forceinline__ void report_oob(int* err, int site) {
+    if (!err) return;
+    atomicCAS(err, 0, JV_ERR_RANGE);
+    atomicCAS(err + 1, 0, site);
+}
+// The physical KV page of `slot`. A context's page table on the device is preceded by two words:
+// its entry count and the pool's page count (ctx_upload_pages), which a checked build tests.
+__device__ __forceinline__ int kv_page(const int32_t* table, int slot, int page_slots, int* err, int site) {
+#ifdef JV_BOUNDS_CHECK
+    const int e = slot / page_slots;
+    if (slot < 0 || e >= table[-2]) {
+        report_oob(err, site);
+        return 0;
+    }
+    const int p = table[e];
+    if (p < 0 || p >= table[-1]) {
+        report_oob(err, site);
+        return 0;
+    }
+    return p;
+#else
+    (void)err;
+    (void)site;
+    return table[slot / page_slots];
+#endif
+}
+#ifdef JV_BOUNDS_CHECK
+#define JV_CHECK(cond, err, site) ((cond) ? true : (::jv::report_oob((err), (site)), false))
+#else
+#define JV_CHECK(cond, err, site) true
+#endif
+#endif
+
 void launch_rmsnorm(const float* h, const float* w, int T, int n, float eps, __half* xs, int tpad, float* out32,
                     int* err, cudaStream_t s);
 // Prefill RMSNorm into the fp16 K-slab, first folding a pending split-K residual into h
@@ -228,6 +270,7 @@ struct DecodeAttnArgs {
     float* partial;             // workspace
     int splits;
     float* ctx32;               // [heads*hd]
+    int* err = nullptr;         // error word (bounds-checked builds)
 };
 void launch_decode_attention(const DecodeAttnArgs& a, cudaStream_t s);
 
@@ -292,6 +335,7 @@ struct DecAttnArgs {
     int* counters;    // [kv_heads], zero between launches
     float* ctx32;     // [heads * 128]
     const uint8_t* pf = nullptr;  // L2 prefetch of a later kernel's weights (as in DecGemvArgs)
+    int* err = nullptr;           // error word (bounds-checked builds)
     int64_t pf_bytes = 0;
 };
 constexpr int DEC_ATTN_KEYS = 64;      // logical keys per attention split
@@ -308,7 +352,8 @@ void launch_kslab_to_f32(const __half* xs, int T, int K, int tpad, float* out, c
 // Elements [base, base + count) of the flat snapshot (count = 0: to the end), to or from a
 // buffer holding exactly those elements.
 void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, float* out, cudaStream_t s, int64_t base = 0, int64_t count = 0);
+                      int kv_heads, int len, float* out, cudaStream_t s, int64_t base = 0, int64_t count = 0,
+                      int* err = nullptr);
 void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
                       int kv_heads, int len, const float* in, int* err, cudaStream_t s, int64_t base = 0,
                       int64_t count = 0);

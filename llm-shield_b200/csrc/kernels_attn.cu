@@ -65,9 +65,9 @@ __device__ __forceinline__ int swz(int r, int c) { return r * ATT_HD + ((c ^ (r 
 // The (layer, head, K|V) plane of the page holding `slot`, and the slot's row in it.
 __device__ __forceinline__ const char* kv_plane(const __half* pool, const int32_t* page_table, int64_t page_bytes,
                                                 int page_slots, int layer, int kv_heads, int head, int kv, int slot,
-                                                int& row) {
+                                                int& row, int* err) {
     row = slot % page_slots;
-    return (const char*)pool + (int64_t)page_table[slot / page_slots] * page_bytes +
+    return (const char*)pool + (int64_t)kv_page(page_table, slot, page_slots, err, BS_MMA_ATTN_PAGE) * page_bytes +
            kv_plane_offset(layer, kv_heads, head, kv, page_slots);
 }
 
@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(AttnArgs a) {
         for (int j = 0; j < 4; j++) {
             const int L = L0 + j * ATT_THREADS;
             slot[j] = L < it.shared ? it.base + L : it.segment + (L - it.shared);
-            page[j] = L < max_limit ? a.page_table[slot[j] / a.page_slots] : 0;
+            page[j] = L < max_limit ? kv_page(a.page_table, slot[j], a.page_slots, a.err, BS_MMA_ATTN_PAGE) : 0;
         }
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -324,7 +324,7 @@ __global__ void k_decode_attention(DecodeAttnArgs a) {
         int L = k0 + i;
         int slot = L < a.shared ? L : a.segment + (L - a.shared);
         int row;
-        const char* k = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot, row);
+        const char* k = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot, row, a.err);
         float acc = 0.f;
         for (int d = 0; d < ATT_HD; d += 8) {
             int4 raw = *(const int4*)(k + kv_chunk_offset(row, d >> 3, a.page_slots));
@@ -355,7 +355,7 @@ __global__ void k_decode_attention(DecodeAttnArgs a) {
         int L = k0 + i;
         int slot = L < a.shared ? L : a.segment + (L - a.shared);
         int row;
-        const char* v = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot, row);
+        const char* v = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot, row, a.err);
         float p = ps[h * DEC_KEYS + i];
         uint2 raw = *(const uint2*)(v + kv_elem_offset(row, lane * 4, a.page_slots));
         const __half2* vh = (const __half2*)&raw;

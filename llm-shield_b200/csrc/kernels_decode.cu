@@ -253,12 +253,12 @@ __global__ void __launch_bounds__(DG_THREADS) k_dec_gemv(DecGemvArgs a) {
                     a.q32[tile * 128 + 2 * t] = r0;
                     a.q32[tile * 128 + 2 * t + 1] = r1;
                 } else {
-                    char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq, 0, st.slot);
+                    char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq, 0, st.slot, a.err);
                     if (f16_out_of_range(r0) || f16_out_of_range(r1)) report_numeric(a.err, NS_DEC_KV);
                     *(__half2*)(dst + kv_elem_offset(st.slot % a.page_slots, 2 * t, a.page_slots)) = __floats2half2_rn(r0, r1);
                 }
             } else {
-                char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq - hk, 1, st.slot);
+                char* dst = kv_plane(a.kv_pool, a.page_table, a.page_bytes, a.page_slots, a.layer, hk, tile - hq - hk, 1, st.slot, a.err);
                 if (f16_out_of_range(x0) || f16_out_of_range(x1)) report_numeric(a.err, NS_DEC_KV);
                 *(__half2*)(dst + kv_elem_offset(st.slot % a.page_slots, 2 * t, a.page_slots)) = __floats2half2_rn(x0, x1);
             }
@@ -368,8 +368,8 @@ __global__ void __launch_bounds__(256) k_dec_attn(DecAttnArgs a) {
             const int L = k0 + threadIdx.x;
             const int slot = L < st.shared ? L : st.segment + (L - st.shared);
             __half* pool = const_cast<__half*>(a.kv_pool);
-            krow[threadIdx.x] = kv_plane(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot);
-            vrow[threadIdx.x] = kv_plane(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot);
+            krow[threadIdx.x] = kv_plane(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 0, slot, a.err);
+            vrow[threadIdx.x] = kv_plane(pool, a.page_table, a.page_bytes, a.page_slots, a.layer, a.kv_heads, kvh, 1, slot, a.err);
             krowi[threadIdx.x] = slot % a.page_slots;
         }
         for (int i = threadIdx.x; i < group * 128; i += nthreads) qs[i] = a.q32[kvh * group * 128 + i];

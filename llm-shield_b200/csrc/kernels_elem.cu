@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
     }
     // K plane of (layer, kv head 0) in this token's page; heads and V are fixed plane offsets,
     // the slot's row inside a plane is swizzled (kv_elem_offset)
-    const int page = a.page_table[slot / a.page_slots], row_in_page = slot % a.page_slots;
+    const int page = kv_page(a.page_table, slot, a.page_slots, a.err, BS_ROPE_PAGE), row_in_page = slot % a.page_slots;
     char* kv0 = (char*)a.kv_pool + (int64_t)page * a.page_bytes + kv_plane_offset(a.layer, a.kv_heads, 0, 0, a.page_slots);
     const int64_t head_stride = (int64_t)2 * a.page_slots * 256, v_off = (int64_t)a.page_slots * 256;
     const int nq4 = qdim / 4, nk4 = kvdim / 4;
@@ -319,7 +319,7 @@ namespace jv {
 // [pass: K then V][layer][kv head][position < len][128] fp32.
 __global__ void k_kv_export(const __half* __restrict__ pool, const int32_t* __restrict__ page_table, int64_t page_bytes,
                             int page_slots, int layers, int kv_heads, int len, float* __restrict__ out, int64_t base,
-                            int64_t count) {
+                            int64_t count, int* err) {
     for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < count; j += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = base + j;
         int d = (int)(i % 128);
@@ -330,7 +330,7 @@ __global__ void k_kv_export(const __half* __restrict__ pool, const int32_t* __re
         r /= kv_heads;
         int l = (int)(r % layers);
         int kv = (int)(r / layers);
-        int page = page_table[p / page_slots];
+        int page = kv_page(page_table, p, page_slots, err, BS_SNAPSHOT_PAGE);
         const __half* src = (const __half*)((const char*)pool + (int64_t)page * page_bytes +
                                              kv_plane_offset(l, kv_heads, h, kv, page_slots) +
                                              kv_elem_offset(p % page_slots, d, page_slots));
@@ -351,7 +351,7 @@ __global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict
         r /= kv_heads;
         int l = (int)(r % layers);
         int kv = (int)(r / layers);
-        int page = page_table[p / page_slots];
+        int page = kv_page(page_table, p, page_slots, err, BS_SNAPSHOT_PAGE);
         __half* dst = (__half*)((char*)pool + (int64_t)page * page_bytes + kv_plane_offset(l, kv_heads, h, kv, page_slots) +
                                 kv_elem_offset(p % page_slots, d, page_slots));
         const float v = in[j];
@@ -361,10 +361,11 @@ __global__ void k_kv_import(__half* __restrict__ pool, const int32_t* __restrict
 }
 
 void launch_kv_export(const __half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,
-                      int kv_heads, int len, float* out, cudaStream_t s, int64_t base, int64_t count) {
+                      int kv_heads, int len, float* out, cudaStream_t s, int64_t base, int64_t count, int* err) {
     if (len <= 0) return;
     if (count <= 0) count = (int64_t)2 * layers * kv_heads * len * 128 - base;
-    k_kv_export<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, out, base, count);
+    k_kv_export<<<1024, 256, 0, s>>>(pool, page_table, page_bytes, page_slots, layers, kv_heads, len, out, base, count,
+                                     err);
     note_launch();
 }
 void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_bytes, int page_slots, int layers,

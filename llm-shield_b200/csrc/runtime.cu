@@ -595,15 +595,20 @@ void ctx_make_writable(jv_ctx* x, const std::vector<int>& written_pages) {
     }
 }
 
+// The device page table: two words (the entry count and the pool's page count, which the
+// bounds-checked build tests every lookup against), then logical page -> physical page.
 void ctx_upload_pages(jv_ctx* x) {
     if (!x->pages_dirty) return;
-    size_t n = std::max<size_t>(1, x->pages.size());
-    int32_t* d = x->d_pages.get(n);
-    if (!x->pages.empty())
-        JV_CUDA(cudaMemcpyAsync(d, x->pages.data(), sizeof(int32_t) * x->pages.size(), cudaMemcpyHostToDevice, x->stream));
+    std::vector<int32_t> h(2 + x->pages.size());
+    h[0] = (int32_t)x->pages.size();
+    h[1] = x->m->n_pages;
+    std::copy(x->pages.begin(), x->pages.end(), h.begin() + 2);
+    int32_t* d = x->d_pages.get(h.size());
+    JV_CUDA(cudaMemcpyAsync(d, h.data(), sizeof(int32_t) * h.size(), cudaMemcpyHostToDevice, x->stream));
     JV_CUDA(cudaStreamSynchronize(x->stream));  // the host vector may change before the copy would run
     x->pages_dirty = false;
 }
+const int32_t* ctx_table(jv_ctx* x) { return x->d_pages.p + 2; }
 
 void ctx_release_pages(jv_ctx* x) {
     for (int p : x->pages) x->m->release(p);
@@ -645,6 +650,19 @@ const char* timeout_site(int site) {
     }
 }
 
+const char* bounds_site(int site) {
+    switch (site) {
+        case BS_ROPE_PAGE: return "RoPE / K-V write: page table";
+        case BS_ATTN_PAGE: return "tensor-core attention: page table";
+        case BS_ATTN_STAGED: return "tensor-core attention: staged page entry";
+        case BS_MMA_ATTN_PAGE: return "mma.sync attention: page table";
+        case BS_DECODE_PAGE: return "single-token step: page table";
+        case BS_GEMM_UNIT: return "GEMM work unit";
+        case BS_SNAPSHOT_PAGE: return "snapshot export/import: page table";
+        default: return "a token id or vocabulary row";
+    }
+}
+
 const char* numeric_site(int site) {
     switch (site) {
         case NS_RMSNORM: return "an RMSNorm (the fp16 operand of the next projection)";
@@ -671,7 +689,7 @@ void sync_check(jv_ctx* x) {
             throw Error(JV_ERR_NUMERIC, std::string("an activation left the fp16 range the device path computes in "
                                                     "(|x| >= 65520, or not a number) at ") + numeric_site(site) +
                                             "; the reference's fp32 path has no such limit");
-        throw Error(e, "a kernel reported an out-of-range index");
+        throw Error(e, std::string("a kernel reported an out-of-range index (") + bounds_site(site) + ")");
     }
 }
 
@@ -851,7 +869,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         a.temperature_scale = c.temperature_scale;
         a.q32 = q32;
         a.kv_pool = m->pool;
-        a.page_table = x->d_pages.p;
+        a.page_table = ctx_table(x);
         a.page_bytes = m->page_bytes;
         a.page_slots = m->page_slots;
         a.pf = pf_qkv.first;
@@ -863,7 +881,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         DecAttnArgs da;
         da.q32 = q32;
         da.kv_pool = m->pool;
-        da.page_table = x->d_pages.p;
+        da.page_table = ctx_table(x);
         da.page_bytes = m->page_bytes;
         da.page_slots = m->page_slots;
         da.layer = l;
@@ -873,6 +891,7 @@ void decode_step(jv_ctx* x, DecodeStep* d_step, int attn_splits, bool head, bool
         da.step = d_step;
         da.partial = apart;
         da.counters = ctr + DEC_ATTN_CTR;
+        da.err = x->d_err;
         da.ctx32 = ctx;
         da.pf = pf_attn.first;
         da.pf_bytes = pf_attn.second;
@@ -1145,7 +1164,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         ra.temperature_scale = c.temperature_scale;
         ra.orig_ctx = c.rope_orig_ctx;
         ra.kv_pool = m->pool;
-        ra.page_table = x->d_pages.p;
+        ra.page_table = ctx_table(x);
         ra.page_bytes = m->page_bytes;
         ra.page_slots = m->page_slots;
         ra.k32 = capture ? x->k32.get((size_t)T * kvdim) : nullptr;
@@ -1164,7 +1183,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
             DecodeAttnArgs da;
             da.q32 = ra.q32;
             da.kv_pool = m->pool;
-            da.page_table = x->d_pages.p;
+            da.page_table = ctx_table(x);
             da.page_bytes = m->page_bytes;
             da.page_slots = m->page_slots;
             da.layer = l;
@@ -1177,6 +1196,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
             da.splits = (da.n_keys + 63) / 64;
             da.partial = x->tmp32.get((size_t)c.heads * da.splits * (2 + c.head_dim));
             da.ctx32 = x->ctx32.get(qdim);
+            da.err = x->d_err;
             {
                 ProfScope ps(x, JV_PROF_ATTENTION, 4.0 * c.heads * c.head_dim * da.n_keys,
                              (double)da.n_keys * c.kv_heads * c.head_dim * 2 * 2 + 8.0 * qdim);
@@ -1229,7 +1249,7 @@ void forward(jv_ctx* x, const int32_t* tokens, int T, const HostLayout* L, const
         aa.items = d_items;
         aa.n_items = (int)items.size();
         aa.kv_pool = m->pool;
-        aa.page_table = x->d_pages.p;
+        aa.page_table = ctx_table(x);
         aa.page_bytes = m->page_bytes;
         aa.page_slots = m->page_slots;
         aa.layer = l;
@@ -1405,6 +1425,13 @@ QWeight qweight_view(int type, const void* tiled, int rows, int cols) {
 
 extern "C" {
 
+int32_t jv_build_features(void) {
+#ifdef JV_BOUNDS_CHECK
+    return JV_FEATURE_BOUNDS_CHECK;
+#else
+    return 0;
+#endif
+}
 const char* jv_last_error(void) { return g_last_error.c_str(); }
 
 int jv_device_count(int32_t* count) {
@@ -1787,7 +1814,8 @@ int jv_kv_snapshot(jv_ctx* x, int32_t length, float* out, int64_t n_floats) {
         ctx_upload_pages(x);
         float* d = x->cap32.get((size_t)need);
         const jv_config& c = x->m->cfg;
-        launch_kv_export(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, length, d, x->stream);
+        launch_kv_export(x->m->pool, ctx_table(x), x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, length, d, x->stream, 0, 0,
+                         x->d_err);
         JV_CUDA(cudaMemcpyAsync(out, d, sizeof(float) * need, cudaMemcpyDeviceToHost, x->stream));
         JV_CUDA(cudaStreamSynchronize(x->stream));
     });
@@ -1808,7 +1836,7 @@ int jv_kv_restore(jv_ctx* x, const float* snap, int64_t n_floats, int32_t length
         float* d = x->cap32.get((size_t)std::max<int64_t>(1, need));
         JV_CUDA(cudaMemcpyAsync(d, snap, sizeof(float) * need, cudaMemcpyHostToDevice, x->stream));
         const jv_config& c = x->m->cfg;
-        launch_kv_import(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, length, d, x->d_err, x->stream);
+        launch_kv_import(x->m->pool, ctx_table(x), x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, length, d, x->d_err, x->stream);
         JV_CUDA(cudaStreamSynchronize(x->stream));
         x->length = length;
     });
@@ -1869,8 +1897,8 @@ int jv_kv_save_shkv(jv_ctx* x, const char* path, const char* fingerprint, const 
         float* d = x->cap32.get((size_t)std::max<int64_t>(1, slice));
         float* h = x->h_cap.get((size_t)std::max<int64_t>(1, slice));
         for (int64_t base = 0; base < total; base += slice) {
-            launch_kv_export(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, n_tokens, d,
-                             x->stream, base, slice);
+            launch_kv_export(x->m->pool, ctx_table(x), x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, n_tokens, d,
+                             x->stream, base, slice, x->d_err);
             JV_CUDA(cudaMemcpyAsync(h, d, sizeof(float) * slice, cudaMemcpyDeviceToHost, x->stream));
             JV_CUDA(cudaStreamSynchronize(x->stream));
             if (std::fwrite(h, sizeof(float), (size_t)slice, f.f) != (size_t)slice)
@@ -1942,7 +1970,7 @@ int jv_kv_load_shkv(jv_ctx* x, const char* path, const char* fingerprint, int32_
             if (std::fread(h, sizeof(float), (size_t)slice, f.f) != (size_t)slice)
                 throw Error(JV_ERR_IO, std::string("read failed: ") + path);
             JV_CUDA(cudaMemcpyAsync(d, h, sizeof(float) * slice, cudaMemcpyHostToDevice, x->stream));
-            launch_kv_import(x->m->pool, x->d_pages.p, x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, count, d,
+            launch_kv_import(x->m->pool, ctx_table(x), x->m->page_bytes, x->m->page_slots, c.layers, c.kv_heads, count, d,
                              x->d_err, x->stream, base, slice);
             JV_CUDA(cudaStreamSynchronize(x->stream));
         }

@@ -63,7 +63,9 @@ __device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity, long lo
 // A bounded wait gave up: the error word takes JV_ERR_DEVICE_TIMEOUT and the word after it
 // the first site that gave up (kernel x 16 + role), which the host names in its message.
 __device__ __forceinline__ void report_timeout(int* err, int site) {
-    atomicExch(err, JV_ERR_DEVICE_TIMEOUT);
+    // takes the place of a numeric report, not of an out-of-range index (its cause, in a checked build)
+    atomicCAS(err, 0, JV_ERR_DEVICE_TIMEOUT);
+    atomicCAS(err, JV_ERR_NUMERIC, JV_ERR_DEVICE_TIMEOUT);
     atomicCAS(err + 1, 0, site);
 }
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

@@ -6,10 +6,12 @@ module raises, so nothing can silently run without the CUDA path.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent.parent
-LIB_PATH = PKG / "libjv.so"
+# JV_LIBRARY may name the bounds-checked build (libjv_checked.so) for a diagnostic run.
+LIB_PATH = Path(os.environ["JV_LIBRARY"]) if os.environ.get("JV_LIBRARY") else PKG / "libjv.so"
 
 if not LIB_PATH.exists():
     raise ImportError(f"{LIB_PATH} is not built; run `python llm-shield_b200/build.py` (nvcc, sm_100a)")
@@ -41,6 +43,7 @@ SIGNATURES = [
     ("jv_last_error", C.c_char_p, []),
     ("jv_device_count", C.c_int, [i32p]),
     ("jv_kernel_launches", i64, []),
+    ("jv_build_features", i32, []),
     ("jv_model_open", C.c_int, [C.c_char_p, i32, i32, C.POINTER(vp)]),
     ("jv_model_close", None, [vp]),
     ("jv_model_config", C.c_int, [vp, C.POINTER(JvConfig)]),

@@ -168,3 +168,20 @@ def ctypes_i32():
     import ctypes
 
     return ctypes.byref(ctypes.c_int32(0))
+
+
+def test_the_bounds_checked_build_exports_the_same_api_and_says_so():
+    """libjv_checked.so (built with -DJV_BOUNDS_CHECK) carries every declared symbol, and
+    jv_build_features tells the two builds apart."""
+    import ctypes
+
+    from jevstral_b200._lib import LIB_PATH
+
+    checked = LIB_PATH.parent / "libjv_checked.so"
+    normal = ctypes.CDLL(str(LIB_PATH.parent / "libjv.so"))
+    chk = ctypes.CDLL(str(checked))
+    for lib in (normal, chk):
+        assert not [n for n in declared_functions() if not hasattr(lib, n)]
+        lib.jv_build_features.restype = ctypes.c_int32
+    assert normal.jv_build_features() == 0
+    assert chk.jv_build_features() == 1
