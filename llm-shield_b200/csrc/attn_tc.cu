@@ -21,10 +21,15 @@
 // pages store their rows in the operand swizzle (kv_chunk_offset), so each run of consecutive
 // slots inside one page is two bulk copies (one per 64-dim half); a run whose first row sits at
 // a different position modulo 8 in the page than in the tile (a branch segment starting off a
-// multiple of 8) goes chunk by chunk through cp.async instead. Warp 10 owns TMEM and issues the
-// MMAs from an event loop: the next P V as soon as its P and V are in place, S_X(b) as soon as
-// K(b) is and the softmax has read S_X(b - 1). Every wait is bounded (WAIT_CYCLES of the SM clock); on
-// expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
+// multiple of 8) goes chunk by chunk through cp.async instead.
+// Each tile has its own MMA issuer (lane 0 of warp 10 for A, of warp 11 for B; warp 10 also owns
+// TMEM): one thread issues a tcgen05.mma about every 150 SM cycles whatever N is, while the tensor
+// core finishes an N = 128 MMA in about half that, so a single issuer would leave it half idle. An
+// issuer runs an event loop over its own tile: the next P V as soon as its P and V are in place,
+// S_X(b) as soon as K(b) is and the softmax has read S_X(b - 1). Each tile releases a K stage
+// through its own barrier (the two tiles' S MMAs are not ordered); a V stage is released by the
+// last tile to use it, whose P V follows the other's through the P buffer. Every wait is bounded
+// (WAIT_CYCLES of the SM clock); on expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
 #include "tc_common.cuh"
 
 namespace jv {
@@ -32,7 +37,7 @@ namespace {
 
 constexpr int AT_ROWS = 128;                 // 32 tokens x 4 query heads per tile
 constexpr int AT_KEYS = 128;                 // keys per block
-constexpr int AT_THREADS = 352;              // 11 warps
+constexpr int AT_THREADS = 384;              // 12 warps
 constexpr int AT_TILE = 128 * 128 * 2;       // one [128][128] fp16 tile, two 16 KB halves
 constexpr int AT_PAGES = 448;                // page-table entries staged in shared memory
 constexpr float AT_LOG2E = 1.4426950408889634f;
@@ -129,10 +134,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     uint8_t* Ps = sm + 6 * AT_TILE;         // [128 rows][128 keys]: one tile's P at a time
     int32_t* pg = (int32_t*)(sm + 7 * AT_TILE);  // physical pages of the item's keys
     uint64_t* bars = (uint64_t*)(pg + AT_PAGES);
-    const uint32_t q_full = s_addr(bars), k_full = q_full + 8, k_empty = k_full + 16, v_full = k_empty + 16;
+    // k_empty: per tile x and stage s at k_empty + 8 (2x + s); p_full, s_full, s_free, o_done per tile
+    const uint32_t q_full = s_addr(bars), k_full = q_full + 8, k_empty = k_full + 16, v_full = k_empty + 32;
     const uint32_t v_empty = v_full + 16, s_full = v_empty + 16, s_free = s_full + 16, p_full = s_free + 16;
-    const uint32_t o_done = p_full + 8;
-    uint32_t* tslot = (uint32_t*)(bars + 16);
+    const uint32_t o_done = p_full + 16;
+    uint32_t* tslot = (uint32_t*)(bars + 20);
 
     // Items and the page table were uploaded before the pass: set-up reads them before waiting
     // for the previous kernel, which wrote Q and this pass's K/V.
@@ -161,19 +167,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
         for (int i = 0; i < 2; i++) {
             mbar_init(k_full + 8 * i, 32);
             mbar_init(k_empty + 8 * i, 1);
+            mbar_init(k_empty + 16 + 8 * i, 1);
             mbar_init(v_full + 8 * i, 32);
             mbar_init(v_empty + 8 * i, 1);
             mbar_init(s_full + 8 * i, 1);
             mbar_init(s_free + 8 * i, 4);
+            mbar_init(p_full + 8 * i, 4);
             mbar_init(o_done + 8 * i, 1);
         }
-        mbar_init(p_full, 4);
         fence_barrier_init();
     }
     if (warp == 10) tmem_alloc(s_addr(tslot), 512);
     if (warp >= 8 && staged) {
         // stage the page-table entries of both key regions
-        for (int i = tid - 256; i < pagesA + pagesB; i += 96)
+        for (int i = tid - 256; i < pagesA + pagesB; i += 128)
             pg[i] = kv_page(a.page_table, (i < pagesA ? pA0 + i : pB0 + (i - pagesA)) * ps, ps, a.err, BS_ATTN_PAGE);
     }
     tc_fence_before();
@@ -210,7 +217,16 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 const int s = b & 1;
                 if (b == 1) load_q();
                 bool ok = true;
-                if (lane == 0) ok = mbar_wait(empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u);
+                if (lane == 0) {
+                    if (kv) {
+                        ok = mbar_wait(empty + 8 * s, (uint32_t)((b >> 1) & 1) ^ 1u);
+                    } else {
+                        // K(b - 2) must be done with by every tile that took it
+                        for (int x = 0; x < 2 && ok; x++)
+                            if (b >= 2 && b - 2 < (x ? nbB : nbA))
+                                ok = mbar_wait(empty + 8 * (2 * x + s), (uint32_t)(((b - 2) >> 1) & 1));
+                    }
+                }
                 if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
                     if (lane == 0) report_timeout(err, 16 + 1 + kv);
                     break;
@@ -258,60 +274,50 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             }
             if (nb < 2) load_q();
             cp_wait_all();
-        } else if (warp == 10 && lane == 0) {
-            // ------------------------------------------------------------------- MMA
+        } else if (lane == 0) {
+            // ------------------------------------------------------- MMA, one issuer per tile
+            const int x = warp - 10;
+            const int nbt = x ? nbB : nbA;
             const uint32_t id_s = idesc_f16(AT_KEYS, AT_ROWS);
             const uint32_t id_pv = idesc_f16(128, AT_ROWS) | (1u << 16);  // B (V) MN-major
-            bool ok = mbar_wait(q_full, 0);
+            bool ok = nbt == 0 || mbar_wait(q_full, 0);
             tc_fence_after();
-            // P V follows the order the tiles take the P buffer in: A(0), B(0), A(1), B(1), ...,
-            // then B alone for the blocks past tile A's last (tile A never sees more keys than B).
-            int ns[2] = {0, 0};  // per tile: next S
-            const int nbx[2] = {nbA, nbB};
-            const int nuses = nbA + nbB;
-            int u = 0;  // next P V
+            const uint32_t q = s_addr(Qs + x * AT_TILE), o = tmem + (uint32_t)(x * 128), d = tmem + 256u + (uint32_t)(x * 128);
+            int ns = 0, u = 0;  // next S block, next P V block of this tile
             long long idle_since = clock64();
-            while (ok && u < nuses) {
+            // Each barrier tested here is at most one phase behind the one wanted: this thread
+            // consumed the phase before it (P_X(u - 1), V(u - 2), K(ns - 2), the read of S_X(ns - 2)),
+            // and the next phase needs this thread's own later MMAs.
+            while (ok && u < nbt) {
                 bool did = false;
-                {
-                    const int x = (nbB == 0 || u >= 2 * nbA) ? (nbB == 0 ? 0 : 1) : (u & 1);
-                    const int b = nbB == 0 ? u : u < 2 * nbA ? (u >> 1) : u - nbA;
-                    if ((x ? ns[1] : ns[0]) > b && mbar_test(p_full, (uint32_t)(u & 1)) &&
-                        mbar_test(v_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) {
-                        tc_fence_after();
-                        const uint32_t p = s_addr(Ps), v = s_addr(Vs + (b & 1) * AT_TILE);
-                        const uint32_t o = tmem + (uint32_t)(x * 128);
+                if (ns > u && mbar_test(p_full + 8 * x, (uint32_t)(u & 1)) &&
+                    mbar_test(v_full + 8 * (u & 1), (uint32_t)((u >> 1) & 1))) {
+                    tc_fence_after();
+                    const uint32_t v = s_addr(Vs + (u & 1) * AT_TILE), p = s_addr(Ps);
 #pragma unroll
-                        for (int kk = 0; kk < 8; kk++) {
-                            const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                            umma(o, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (b > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        // tile B's P V is the last use of V(b) wherever B takes the block
-                        if (x == 1 || nbB == 0) umma_commit(v_empty + 8 * (b & 1));
-                        umma_commit(o_done + 8 * x);  // last: its arrival implies the release before it
-                        u++;
-                        did = true;
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                        umma(o, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (u > 0 || kk > 0) ? 1u : 0u);
                     }
-                }
+                    // tile B's P V is the last use of V(u) wherever B takes the block
+                    if (x == 1 || nbB == 0) umma_commit(v_empty + 8 * (u & 1));
+                    umma_commit(o_done + 8 * x);  // last: its arrival implies the release before it
+                    u++;
+                    did = true;
+                } else if (ns < nbt && mbar_test(k_full + 8 * (ns & 1), (uint32_t)((ns >> 1) & 1)) &&
+                           (ns == 0 || mbar_test(s_free + 8 * x, (uint32_t)((ns - 1) & 1)))) {
+                    // S_X(ns) overwrites S_X(ns - 1): only once the softmax has read that
+                    tc_fence_after();
+                    const uint32_t k = s_addr(Ks + (ns & 1) * AT_TILE);
 #pragma unroll
-                for (int x = 0; x < 2; x++) {
-                    const int b = ns[x];
-                    // S_X(b) overwrites S_X(b - 1): only once the softmax has read that
-                    if (!did && b < nbx[x] && mbar_test(k_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1)) &&
-                        (b == 0 || mbar_test(s_free + 8 * x, (uint32_t)((b - 1) & 1)))) {
-                        tc_fence_after();
-                        const uint32_t q = s_addr(Qs + x * AT_TILE), k = s_addr(Ks + (b & 1) * AT_TILE);
-                        const uint32_t d = tmem + 256u + (uint32_t)(x * 128);
-#pragma unroll
-                        for (int kk = 0; kk < 8; kk++) {
-                            const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                            umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
-                        }
-                        if (b >= nbx[x ^ 1] || ns[x ^ 1] > b) umma_commit(k_empty + 8 * (b & 1));
-                        umma_commit(s_full + 8 * x);
-                        ns[x] = b + 1;
-                        did = true;
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                        umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
                     }
+                    umma_commit(k_empty + 8 * (2 * x + (ns & 1)));
+                    umma_commit(s_full + 8 * x);
+                    ns++;
+                    did = true;
                 }
                 if (did) {
                     idle_since = clock64();
@@ -320,7 +326,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                     if (clock64() - idle_since > WAIT_CYCLES) ok = false;
                 }
             }
-            if (!ok) report_timeout(err, 16 + 3);
+            if (!ok) report_timeout(err, x ? 16 + 6 : 16 + 3);
         }
     } else {
         // --------------------------------------------------- softmax and the output
@@ -429,7 +435,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             fence_proxy_async();  // P stores -> visible to the tensor core
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(p_full + 8 * x);
         }
         if (nbt > 0) {
             if (ok && !warp_wait(o_done + 8 * x, (uint32_t)((nbt - 1) & 1))) ok = false;
@@ -493,7 +499,7 @@ __global__ void k_wait_check(int* err, long long bound) {
 
 }  // namespace
 
-constexpr size_t AT_SMEM = (size_t)7 * AT_TILE + AT_PAGES * 4 + 160 + 1024;
+constexpr size_t AT_SMEM = (size_t)7 * AT_TILE + AT_PAGES * 4 + 192 + 1024;
 
 void launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
     if (a.n_items <= 0) return;
