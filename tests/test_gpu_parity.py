@@ -497,12 +497,13 @@ def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
 
 
 @pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
-def test_tmem_operand_gemm_is_bit_identical_to_the_shared_memory_gemm(model_factory, qtype):
-    """k_gemm_tm (decoded weights in TMEM, read straight from L2) against k_gemm_tc (decoded weights
-    staged in shared memory): the same fp16 operands and the same K order, so every captured
-    activation (the capture path's counter-combined K split) and the product path's verdict
-    logits (split-K halves folded by the next RMSNorm) are the same bits, for a causal prefill of
-    300 tokens and a tree after it."""
+def test_gemm_kernels_are_bit_identical(model_factory, qtype):
+    """The three prefill GEMM kernels on the same model: k_gemm_tc (the default: one CTA per
+    128-row tile), k_gemm_2sm (CTA pairs, 2-SM MMA with M = 256, half an activation tile per CTA,
+    JV_GEMM_KERNEL=2sm) and k_gemm_tm (decoded weights in TMEM, JV_GEMM_KERNEL=tmem). The same
+    fp16 operands and the same K order, so every captured activation (the capture path's
+    counter-combined K split) and the product path's verdict logits (split-K halves folded by
+    the next RMSNorm) are the same bits, for a causal prefill of 300 tokens and a tree after it."""
     path = model_factory(WIDE_CFG, qtype, seed=12)
     code = (
         "import sys, numpy as np; sys.path[:0] = sys.argv[2:];"
@@ -520,19 +521,22 @@ def test_tmem_operand_gemm_is_bit_identical_to_the_shared_memory_gemm(model_fact
     from conftest import REPO
 
     paths = [str(REPO / "llm-shield_b200"), str(REPO)]
-    outs = []
-    for kernel in ("tmem", "smem"):
+    outs = {}
+    for kernel in ("1sm", "2sm", "tmem"):
         env = dict(os.environ)
         env.pop("JV_GEMM_KERNEL", None)
-        if kernel == "tmem":
-            env["JV_GEMM_KERNEL"] = "tmem"
+        if kernel != "1sm":
+            env["JV_GEMM_KERNEL"] = kernel
         r = subprocess.run([sys.executable, "-c", code, str(path)] + paths, env=env, capture_output=True, timeout=900)
         assert r.returncode == 0, r.stderr.decode()[-2000:]
-        outs.append(np.load(io.BytesIO(r.stdout)))
-    tm, sm = outs
-    assert set(tm.files) == set(sm.files) and len(tm.files) > 20
-    diff = [k for k in sm.files if tm[k].tobytes() != sm[k].tobytes()]
-    assert not diff, {k: rel_l2(tm[k], sm[k]) for k in diff}
+        outs[kernel] = np.load(io.BytesIO(r.stdout))
+    ref = outs["1sm"]
+    assert len(ref.files) > 20
+    for kernel in ("2sm", "tmem"):
+        other = outs[kernel]
+        assert set(other.files) == set(ref.files)
+        diff = [k for k in ref.files if other[k].tobytes() != ref[k].tobytes()]
+        assert not diff, (kernel, {k: rel_l2(other[k], ref[k]) for k in diff})
 
 
 def test_tensor_core_attention_matches_the_mma_sync_attention(model_factory):
