@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     const bool staged = pagesA + pagesB <= AT_PAGES;  // else the loaders read the page table
 
     if (tid == 0) {
-        mbar_init(q_full, 96);
+        mbar_init(q_full, 64);
         for (int i = 0; i < 2; i++) {
             mbar_init(k_full + 8 * i, 32);
             mbar_init(k_empty + 8 * i, 1);
@@ -191,23 +191,31 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     pdl_wait();
 
     if (warp >= 8) {
-        // ------------------------------------------------- K / V rings, and Q alongside
-        const int lt = tid - 256;
-        // Q row r of tile X = token 32 X + r / 4, head r % 4 of this KV head; warps 8 and 9 join
-        // in once their first K / V block is on its way
-        auto load_q = [&]() {
-            for (int id = lt; id < 2 * AT_ROWS * 16; id += 96) {
-                const int x = id >> 11, r = (id >> 4) & 127, c = id & 15;
-                const int tl = 32 * x + r / group, j = r % group;
-                const bool ok = tl < it.ntok;
-                const __half* src = ok ? a.q16 + (int64_t)(it.t0 + tl) * qdim + (it.kv_head * group + j) * 128 + c * 8 : a.q16;
-                cp16(s_addr(Qs + x * AT_TILE) + tile_off(r, c), src, ok ? 16 : 0);
-            }
+        // ------------------------------------------------- K / V rings, and Q first
+        if (warp >= 10) {
+            // Q row r of tile X = token 32 X + r / 4, head r % 4 of this KV head (4 query heads per
+            // KV head, checked on the host). The two issuer warps load it before they issue: thread
+            // t takes 16-byte chunk c = t % 16 of rows r = t / 16 + 4 h + 8 k, so its swizzle
+            // (c ^ (r & 7)) is fixed per h and each step of k is one row group further.
+            const int t = tid - 320, c = t & 15, rg = t >> 4;  // rg 0..3
+            const __half* qsrc = a.q16 + (int64_t)it.t0 * qdim + (it.kv_head * 4 + (rg & 3)) * 128 + c * 8;
+#pragma unroll
+            for (int x = 0; x < 2; x++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int rr = rg + 4 * h;
+                    const uint32_t dst0 = s_addr(Qs + x * AT_TILE) + (uint32_t)((c >> 3) * 16384 + rr * 128 + (((c & 7) ^ rr) << 4));
+#pragma unroll
+                    for (int k = 0; k < 16; k++) {
+                        const int tl = 32 * x + (rr >> 2) + 2 * k;  // token of row rr + 8 k
+                        const bool ok = tl < it.ntok;
+                        cp16(dst0 + (uint32_t)(k * 1024), ok ? qsrc + (int64_t)tl * qdim : a.q16, ok ? 16 : 0);
+                    }
+                }
             cp_wait_all();
             fence_proxy_async();
             mbar_arrive(q_full);
-        };
-        if (warp == 10) load_q();
+        }
         if (warp == 8 || warp == 9) {
             const int kv = warp - 8;  // 0: K ring, 1: V ring
             const char* pool = (const char*)a.kv_pool + kv_plane_offset(a.layer, a.kv_heads, it.kv_head, kv, ps);
@@ -215,7 +223,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             const uint32_t ring = s_addr(kv ? Vs : Ks);
             for (int b = 0; b < nb; b++) {
                 const int s = b & 1;
-                if (b == 1) load_q();
                 bool ok = true;
                 if (lane == 0) {
                     if (kv) {
@@ -272,7 +279,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
                 fence_proxy_async();
                 mbar_arrive(full + 8 * s);
             }
-            if (nb < 2) load_q();
             cp_wait_all();
         } else if (lane == 0) {
             // ------------------------------------------------------- MMA, one issuer per tile
