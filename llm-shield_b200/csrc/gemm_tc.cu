@@ -570,14 +570,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
 //     forwards each completed stage to the even CTA's b_full;
 //   * the MMA lane commits with .multicast::cluster, so st_empty and acc_full arrive in both CTAs;
 //   * the odd CTA's epilogue warps arrive on the even CTA's acc_empty.
-// The MMA lane waits with acquire at cluster scope. No TMA, no multicast load: the copies are
+// Remote arrives and the waits use the default mbarrier semantics; arrivals with release and
+// acquire at cluster scope measured ~0.8 us from arrive to the MMA lane seeing it. No TMA, no multicast load: the copies are
 // plain cp.async.bulk into the issuing CTA's own shared memory. Every wait is bounded; a CTA
 // leaves only after a cluster barrier, once no MMA can read its shared memory.
-// Measured on C5 trees (two layers of the 3B model, one B200 at 1965 MHz): 705 TFLOP/s against
-// 1026 for k_gemm_tc. A k step takes ~1280 cycles against the 514 of its four MMAs; the MMA lane
-// spends ~600 of them waiting for activation stages and ~300 for decoded weights although five
-// stages are in flight, and polling instead of sleeping in those waits made it slower still. So
-// it is not the default (JV_GEMM_KERNEL=2sm selects it).
+// Measured on C5 (26 layers, one B200 under its power cap): 956 TFLOP/s against 919 for k_gemm_tc,
+// 121.8K against 115.4K tokens/s for the whole step.
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
@@ -602,35 +600,14 @@ __device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) 
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
     return r;
 }
+// Arrive on an mbarrier of the other CTA (default semantics, as for a local arrive).
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(caddr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(caddr) : "memory");
 }
-// Bounded polls with acquire at cluster scope (arrivals come from the other CTA too).
-__device__ __forceinline__ bool mbar_poll_cl(uint32_t bar, uint32_t parity, long long bound = WAIT_CYCLES) {
-    uint32_t ok;
-    const long long t0 = clock64();
-    for (;;) {
-        asm volatile(
-            "{\n.reg .pred p;\nmbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if (clock64() - t0 > bound) return false;
-    }
-}
-__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, long long bound = WAIT_CYCLES) {
-    uint32_t ok;
-    const long long t0 = clock64();
-    for (;;) {
-        asm volatile(
-            "{\n.reg .pred p;\nmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity), "r"(1000000u)
-            : "memory");
-        if (ok) return true;
-        if (clock64() - t0 > bound) return false;
-    }
+// This CTA's barrier at `local` (a plain arrive), or the even CTA's barrier at the same offset.
+__device__ __forceinline__ void mbar_arrive_even(uint32_t local, uint32_t even_caddr, uint32_t rank) {
+    if (rank == 0) mbar_arrive(local);
+    else mbar_arrive_remote(even_caddr);
 }
 __device__ __forceinline__ void umma2(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
     asm volatile(
@@ -754,7 +731,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
             // needs the relay, so it waits for the transaction count through b_full as well.
             for (int i = 0; i < issued && i < depth; i++) {
                 r.prev();
-                if (!mbar_wait_cl(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
+                if (!mbar_wait(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
             }
         }
     } else if (warp == 2) {
@@ -778,11 +755,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
             int i = 0;
             for (int u = cid; u < units && ok; u += ncl, i++) {
                 const int ab = i & 1;
-                if (!mbar_wait_cl(acc_empty + 8 * ab, (uint32_t)((i >> 1) & 1) ^ 1u)) { ok = false; break; }
+                if (!mbar_wait(acc_empty + 8 * ab, (uint32_t)((i >> 1) & 1) ^ 1u)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t acc = tmem + (uint32_t)(ab * ncols);
                 for (int ks = 0; ks < nks; ks++) {
-                    if (!mbar_poll_cl(a_full + 8 * rs.idx, rs.phase) || !mbar_poll_cl(b_full + 8 * rs.idx, rs.phase)) {
+                    if (!mbar_poll(a_full + 8 * rs.idx, rs.phase) || !mbar_poll(b_full + 8 * rs.idx, rs.phase)) {
                         ok = false;
                         break;
                     }
@@ -828,7 +805,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
                 for (int it = 0; it < 8; it++) *(uint4*)(A + it * 16 * 128) = v[it];
                 fence_proxy_async();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_remote(a_full_even + 8 * rs.idx);
+                if (lane == 0) mbar_arrive_even(a_full + 8 * rs.idx, a_full_even + 8 * rs.idx, rank);
                 rs.next();
                 rs.next();
             }
@@ -883,7 +860,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_remote(acc_empty_even + 8 * ab);
+            if (lane == 0) mbar_arrive_even(acc_empty + 8 * ab, acc_empty_even + 8 * ab, rank);
         }
     }
     // The decoder warps drain two thirds of the last unit's columns, as in k_gemm_tc.
@@ -1292,16 +1269,16 @@ int gemm_bn_for(int T, int units_per_tile, int sm_count) {
 
 static int g_sm_count = 0;
 
-// The prefill GEMM kernel: k_gemm_tc by default; JV_GEMM_KERNEL=2sm for k_gemm_2sm (CTA pairs,
-// M = 256; a matrix with an odd number of 128-row tiles still runs on k_gemm_tc), and
-// JV_GEMM_KERNEL=tmem for k_gemm_tm (decoded weights in TMEM, token tiles of at most 224). All
-// give the same bits (test_gemm_kernels_are_bit_identical); k_gemm_tc is the fastest measured.
+// The prefill GEMM kernel: k_gemm_2sm by default (CTA pairs, M = 256; a matrix with an odd number
+// of 128-row tiles runs on k_gemm_tc), JV_GEMM_KERNEL=1sm for k_gemm_tc everywhere, and
+// JV_GEMM_KERNEL=tmem for k_gemm_tm (decoded weights in TMEM, token tiles of at most 224). All give
+// the same bits (test_gemm_kernels_are_bit_identical); k_gemm_2sm is the fastest measured.
 static GemmKernel gemm_kernel_choice() {
     static const GemmKernel v = [] {
         const char* e = getenv("JV_GEMM_KERNEL");
         if (e != nullptr && strcmp(e, "tmem") == 0) return GK_TMEM;
-        if (e != nullptr && strcmp(e, "2sm") == 0) return GK_2SM;
-        return GK_1SM;
+        if (e != nullptr && strcmp(e, "1sm") == 0) return GK_1SM;
+        return GK_2SM;
     }();
     return v;
 }
