@@ -440,7 +440,7 @@ def run_prefill(args, rank, world, local_rank, dist, ctx, stream):
         "tokens_per_s_per_gpu": job_tokens / dev_s / world,
         "linear_tflops": job_tokens * LINEAR_FLOPS_PER_TOKEN * args.layers / 26 / dev_s / 1e12,
         "attention_pairs_per_item": pairs // max(1, n_items),
-        "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (all four projections)",
+        "roofline": {"bound": "tensor", "kernel": f"{gemm_kernel_name()} (all four projections)",
                      "achieved": gemm_tflops, "peak": burst, "unit": "TFLOP/s",
                      "frac": gemm_tflops / burst if burst else None,
                      "peak_source": f"{src} bf16 dense burst (each launch is event-timed alone; fp16 runs at the "
@@ -523,9 +523,15 @@ def run_decode(args, rank, world, dist, ctx, stream):
     }
 
 
+def gemm_kernel_name() -> str:
+    """The prefill GEMM kernel the library runs (JV_GEMM_KERNEL selects another; see gemm_tc.cu)."""
+    return {"1sm": "k_gemm_tc", "tmem": "k_gemm_tm"}.get(os.environ.get("JV_GEMM_KERNEL", ""), "k_gemm_2sm")
+
+
 def gemm_traffic_per_launch(config: str):
-    """DRAM bytes per k_gemm_tc launch from the committed ncu summary of this configuration."""
-    for name in (f"gemm_tc_{config}.md", "gemm_tc_c2.md"):
+    """DRAM bytes per GEMM launch from the committed ncu summary of this configuration and kernel."""
+    stem = "gemm_2sm" if gemm_kernel_name() == "k_gemm_2sm" else "gemm_tc"
+    for name in (f"{stem}_{config}.md", f"gemm_tc_{config}.md", "gemm_tc_c2.md"):
         f = REPO / "profiles" / name
         if not f.exists():
             continue
