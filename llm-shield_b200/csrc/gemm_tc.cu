@@ -326,12 +326,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     uint8_t* Rs = sm + raw_off;   // NR x chunk raw quant blocks
     uint64_t* bars = (uint64_t*)(sm + bar_off);
     // raw ring: raw_full (copy landed), raw_empty (8 decoder warps read it)
-    // stage ring: b_full (activation tile landed), a_full (8 decoder warps wrote the fp16
-    //             weights), st_empty (the MMA that read both completed)
+    // stage ring: st_full (the activation tile landed and four decoder warps wrote the fp16
+    //             weights: one barrier, so the MMA lane tests one per k step), st_empty (the MMA
+    //             that read both completed)
     const uint32_t raw_full = s_addr(bars), raw_empty = raw_full + 8 * NR;
-    const uint32_t b_full = raw_empty + 8 * NR, a_full = b_full + 8 * NS, st_empty = a_full + 8 * NS;
+    const uint32_t st_full = raw_empty + 8 * NR, st_empty = st_full + 8 * NS;
     const uint32_t acc_full = st_empty + 8 * NS, acc_empty = acc_full + 16, drained = acc_empty + 16;
-    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 3 * NS + 5);
+    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 2 * NS + 5);
     volatile int* last_flag = (volatile int*)(tslot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -341,8 +342,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_WARPS_PER_GROUP); }
         for (int i = 0; i < NS; i++) {
-            mbar_init(b_full + 8 * i, 1);
-            mbar_init(a_full + 8 * i, DEC_WARPS_PER_GROUP);
+            mbar_init(st_full + 8 * i, DEC_WARPS_PER_GROUP + 1);  // decoder warps + the copy's expect_tx
             mbar_init(st_empty + 8 * i, 1);
         }
         for (int i = 0; i < 2; i++) { mbar_init(acc_full + 8 * i, 1); mbar_init(acc_empty + 8 * i, 4); }
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             // activation tiles (stage ring, freed by the MMA): neither waits on the other.
             const bool weights = warp == 0;
             const int depth = weights ? NR : NS;
-            const uint32_t full = weights ? raw_full : b_full, empty = weights ? raw_empty : st_empty;
+            const uint32_t full = weights ? raw_full : st_full, empty = weights ? raw_empty : st_empty;
             const uint32_t bytes = weights ? (uint32_t)cb : bbytes;
             uint8_t* ring = weights ? Rs : Bs;
             Ring r(depth);
@@ -394,7 +394,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             }
             if (!ok) report_timeout(g_err, weights ? 1 : 2);
             // Never leave with copies in flight into this CTA's shared memory: wait for the
-            // last min(issued, ring) copies.
+            // last min(issued, ring) copies (an activation stage's phase also needs its decoder
+            // warps; on an error path the bounded wait outlasts any copy).
             for (int i = 0; i < issued && i < depth; i++) {
                 r.prev();
                 if (!mbar_wait(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
@@ -412,7 +413,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 tc_fence_after();
                 const uint32_t acc = tmem + (uint32_t)(ab * ncols);
                 for (int ks = 0; ks < nks; ks++) {
-                    if (!mbar_poll(a_full + 8 * rs.idx, rs.phase) || !mbar_poll(b_full + 8 * rs.idx, rs.phase)) {
+                    if (!mbar_poll(st_full + 8 * rs.idx, rs.phase)) {
                         ok = false;
                         break;
                     }
@@ -462,7 +463,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 for (int it = 0; it < 8; it++) *(uint4*)(A + it * 16 * 128) = v[it];
                 fence_proxy_async();  // each writer's generic-proxy stores -> visible to the tensor core
                 __syncwarp();
-                if (lane == 0) mbar_arrive(a_full + 8 * rs.idx);
+                if (lane == 0) mbar_arrive(st_full + 8 * rs.idx);
                 rs.next();
                 rs.next();
             }
@@ -564,14 +565,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
 // One lane of the even CTA issues every MMA: M = 256 (each CTA's 128 rows), N = bn (each CTA's
 // half of the tokens), accumulating in both CTAs' TMEM; each CTA drains its own 128 rows x bn.
 // Hand-offs across the pair:
-//   * the odd CTA's decoder warps arrive on the even CTA's a_full (remote mbarrier arrive,
-//     release at cluster scope, after fence.proxy.async of their stores);
+//   * the odd CTA's decoder warps arrive on the even CTA's st_full (remote mbarrier arrive,
+//     after fence.proxy.async of their stores);
 //   * the odd CTA's activation copies complete on its own barrier; one relay lane (warp 2)
-//     forwards each completed stage to the even CTA's b_full;
+//     forwards each completed stage to the even CTA's st_full, which also takes the even CTA's
+//     own copy and decoder warps, so the MMA lane tests one barrier per k step;
 //   * the MMA lane commits with .multicast::cluster, so st_empty and acc_full arrive in both CTAs;
 //   * the odd CTA's epilogue warps arrive on the even CTA's acc_empty.
 // Remote arrives and the waits use the default mbarrier semantics; arrivals with release and
-// acquire at cluster scope measured ~0.8 us from arrive to the MMA lane seeing it. No TMA, no multicast load: the copies are
+// acquire at cluster scope measured ~0.8 us from arrive to the MMA lane seeing it. No TMA, no
+// multicast load: the copies are
 // plain cp.async.bulk into the issuing CTA's own shared memory. Every wait is bounded; a CTA
 // leaves only after a cluster barrier, once no MMA can read its shared memory.
 // Measured on C5 (26 layers, one B200 under its power cap): 956 TFLOP/s against 919 for k_gemm_tc,
@@ -659,14 +662,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
     uint8_t* Bs = sm + b_off;     // NS x hb*128 activations
     uint8_t* Rs = sm + raw_off;   // NR x chunk raw quant blocks
     uint64_t* bars = (uint64_t*)(sm + bar_off);
-    // The same offsets in both CTAs. Used in the even CTA only: b_full (its copy + the odd
-    // CTA's relay), a_full (four decoder warps of each CTA), acc_empty (four epilogue warps of
-    // each), drained. In the odd CTA only: b_local (its own copy landed).
+    // The same offsets in both CTAs. Used in the even CTA only: st_full (its activation copy,
+    // the odd CTA's relay of its copy, and four decoder warps of each CTA: one barrier per stage,
+    // so the MMA lane tests one per k step), acc_empty (four epilogue warps of each), drained.
+    // In the odd CTA only: b_local (its own copy landed).
     const uint32_t raw_full = s_addr(bars), raw_empty = raw_full + 8 * NR;
-    const uint32_t b_full = raw_empty + 8 * NR, a_full = b_full + 8 * NS, st_empty = a_full + 8 * NS;
+    const uint32_t st_full = raw_empty + 8 * NR, st_empty = st_full + 8 * NS;
     const uint32_t b_local = st_empty + 8 * NS;
     const uint32_t acc_full = b_local + 8 * NS, acc_empty = acc_full + 16, drained = acc_empty + 16;
-    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 4 * NS + 5);
+    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 3 * NS + 5);
     volatile int* last_flag = (volatile int*)(tslot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -676,8 +680,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_WARPS_PER_GROUP); }
         for (int i = 0; i < NS; i++) {
-            mbar_init(b_full + 8 * i, 2);
-            mbar_init(a_full + 8 * i, 2 * DEC_WARPS_PER_GROUP);
+            mbar_init(st_full + 8 * i, 2 * DEC_WARPS_PER_GROUP + 2);  // decoder warps, copy, relay
             mbar_init(st_empty + 8 * i, 1);
             mbar_init(b_local + 8 * i, 1);
         }
@@ -697,7 +700,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
         if (lane == 0) {  // ----------------------------------------------- producers
             const bool weights = warp == 0;
             const int depth = weights ? NR : NS;
-            const uint32_t full = weights ? raw_full : (rank == 0 ? b_full : b_local);
+            const uint32_t full = weights ? raw_full : (rank == 0 ? st_full : b_local);
             const uint32_t empty = weights ? raw_empty : st_empty;
             const uint32_t bytes = weights ? (uint32_t)cb : hbytes;
             uint8_t* ring = weights ? Rs : Bs;
@@ -727,8 +730,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
             }
             if (!ok) report_timeout(g_err, weights ? 1 : 2);
             // Never leave with copies in flight into this CTA's shared memory. The odd CTA's
-            // activation copies land on b_local; the even CTA's on b_full, whose phase also
-            // needs the relay, so it waits for the transaction count through b_full as well.
+            // activation copies land on b_local; the even CTA's on st_full, whose phase also needs
+            // the relay and the decoder warps (on an error path the bounded wait outlasts any copy).
             for (int i = 0; i < issued && i < depth; i++) {
                 r.prev();
                 if (!mbar_wait(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
@@ -738,7 +741,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
         if (lane == 0 && rank == 1) {  // -------------------- relay of the odd CTA's activation tiles
             Ring rs(NS);
             bool ok = true;
-            const uint32_t remote = cluster_addr(b_full, 0);
+            const uint32_t remote = cluster_addr(st_full, 0);
             for (int u = cid; u < units && ok; u += ncl)
                 for (int ks = 0; ks < nks; ks++) {
                     if (!mbar_wait(b_local + 8 * rs.idx, rs.phase)) { ok = false; break; }
@@ -759,7 +762,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
                 tc_fence_after();
                 const uint32_t acc = tmem + (uint32_t)(ab * ncols);
                 for (int ks = 0; ks < nks; ks++) {
-                    if (!mbar_poll(a_full + 8 * rs.idx, rs.phase) || !mbar_poll(b_full + 8 * rs.idx, rs.phase)) {
+                    if (!mbar_poll(st_full + 8 * rs.idx, rs.phase)) {
                         ok = false;
                         break;
                     }
@@ -782,7 +785,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
         const int dt = threadIdx.x - (DEC_WARP0 + grp * DEC_WARPS_PER_GROUP) * 32;
         const int c = dt & 7, r0 = dt >> 3;
         const int a_off = r0 * 128 + ((c ^ (r0 & 7)) << 4);
-        const uint32_t a_full_even = cluster_addr(a_full, 0);
+        const uint32_t st_full_even = cluster_addr(st_full, 0);
         Ring rr(NR), rs(NS);
         if (grp) { rr.next(); rs.next(); }
         bool ok = true;
@@ -805,7 +808,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
                 for (int it = 0; it < 8; it++) *(uint4*)(A + it * 16 * 128) = v[it];
                 fence_proxy_async();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_even(a_full + 8 * rs.idx, a_full_even + 8 * rs.idx, rank);
+                if (lane == 0) mbar_arrive_even(st_full + 8 * rs.idx, st_full_even + 8 * rs.idx, rank);
                 rs.next();
                 rs.next();
             }
@@ -1344,7 +1347,7 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
         p.b_off = 16384 * p.ns;
         p.raw_off = p.b_off + a.bn * 64 * p.ns;
         p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
-        const size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 4 * p.ns + 5) + 16 + 1024;
+        const size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
         auto kern = k_gemm_2sm<TYPE, EPI, CSPLIT>;
         static int max_clusters = 0;  // per instantiation: its shared memory decides residency
         if (max_clusters == 0) {
@@ -1381,7 +1384,7 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.b_off = 16384 * p.ns;
     p.raw_off = p.b_off + a.bn * 128 * p.ns;
     p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
-    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
+    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 2 * p.ns + 5) + 16 + 1024;
     JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE, EPI, CSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (g_sm_count == 0) {
         int dev = 0;
