@@ -227,6 +227,18 @@ struct RopeArgs {
     int* err = nullptr;     // error word (JV_ERR_NUMERIC when a value leaves the fp16 range)
 };
 void launch_rope_kv(const RopeArgs& a, cudaStream_t s);
+#ifdef __CUDACC__
+// The llama-4 query temperature at a position (Rope.cs / MinistralModel.cs:676-682): 1 below the
+// original context, 1 + scale * ln(1 + floor(pos / orig)) past it.
+__device__ __forceinline__ float rope_temperature(int pos, int orig_ctx, float temperature_scale) {
+    float temp = 1.0f;
+    if (orig_ctx > 0 && temperature_scale != 0.f) {
+        float interval = floorf(__fdiv_rn((float)pos, (float)orig_ctx));
+        if (interval != 0.f) temp = __fadd_rn(1.0f, __fmul_rn(temperature_scale, logf(__fadd_rn(1.0f, interval))));
+    }
+    return temp;
+}
+#endif
 void launch_rope_table(float2* table, const float* freqs, int half, int pos0, int npos, float mscale, cudaStream_t s);
 
 constexpr int ATT_ITEM_TOKENS = 32;  // tokens per prefill attention item (x 4 query heads = 128 rows)

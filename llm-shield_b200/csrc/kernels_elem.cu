@@ -201,11 +201,7 @@ __global__ void __launch_bounds__(256) k_rope_kv(RopeArgs a) {
     const int pos = a.pos[t], slot = a.slot[t];
     const float* row = a.qkv + (int64_t)t * (qdim + 2 * kvdim);
     const float4* tab4 = (const float4*)(a.table + (int64_t)pos * half);  // two (cos, sin) pairs each
-    float temp = 1.0f;
-    if (a.orig_ctx > 0 && a.temperature_scale != 0.f) {
-        float interval = floorf(__fdiv_rn((float)pos, (float)a.orig_ctx));
-        if (interval != 0.f) temp = __fadd_rn(1.0f, __fmul_rn(a.temperature_scale, logf(__fadd_rn(1.0f, interval))));
-    }
+    const float temp = rope_temperature(pos, a.orig_ctx, a.temperature_scale);
     // K plane of (layer, kv head 0) in this token's page; heads and V are fixed plane offsets,
     // the slot's row inside a plane is swizzled (kv_elem_offset)
     const int page = kv_page(a.page_table, slot, a.page_slots, a.err, BS_ROPE_PAGE), row_in_page = slot % a.page_slots;
