@@ -104,6 +104,33 @@ def test_tree_decision_matches_the_oracle(model_factory, qtype):
     assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
 
 
+def test_odd_row_tile_counts_match_the_oracle(model_factory):
+    """A width of 384 leaves the O and down projections three 128-row tiles each: the CTA-pair GEMM
+    (k_gemm_2sm, the default) runs the matrices with an even tile count and hands those to the
+    one-CTA kernel. Per-layer hidden states (activation capture) and the product path's verdicts
+    against the oracle."""
+    from jevstral_b200.synth import SynthConfig
+
+    cfg = SynthConfig(layers=2, hidden=384, heads=4, kv_heads=1, head_dim=128, ff=512, vocab=16384)
+    path = model_factory(cfg, "Q8_0", seed=23)
+    trunk = [1] + toks(90, 41)
+    branches = [toks(n, 50 + i) for i, n in enumerate((14, 5, 23))]
+    gpu, cpu = {}, {}
+    with jv.Model(path, kv_pool_mb=128) as m, ctx(m) as c:
+        c.set_activation_sink(capture_into(gpu))
+        c.forward_tree(trunk, branches, VERDICT_ROWS)
+        c.set_activation_sink(None)
+        c.kv_cache.reset()
+        v_gpu = c.forward_tree(trunk, branches, VERDICT_ROWS)
+    with ob.OracleModel(path) as o:
+        v_cpu = o.forward_tree(trunk, branches, VERDICT_ROWS, sink=capture_into(cpu))
+    for l in range(cfg.layers):
+        assert rel_l2(gpu[f"blk.{l}.output"], cpu[f"blk.{l}.output"]) < HIDDEN_TOL, l
+    z_gpu, z_cpu = margins_from_verdicts(v_gpu, 1), margins_from_verdicts(v_cpu, 1)
+    assert np.abs(z_gpu - z_cpu).max() < Z_TOL
+    assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
+
+
 @pytest.mark.parametrize("qtype", ["Q4_K", "Q6_K", "Q2_K", "Q5_K"])
 def test_k_quant_tree_decision_matches_the_oracle(model_factory, qtype):
     """The K-quant formats (Dequantizer.cs:323-471) on the tensor-core path: weights converted on
