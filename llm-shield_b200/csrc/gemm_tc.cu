@@ -736,6 +736,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
                 r.prev();
                 if (!mbar_wait(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
             }
+            if (!weights && ok) {
+                // The stage-empty barriers receive the MMA lane's commits asynchronously (the odd
+                // CTA's through the cluster, multicast): wait until the last use of every stage
+                // has been released, so that no arrival is still in flight into this CTA's shared
+                // memory when it leaves.
+                for (int i = 0; i < issued && i < depth; i++) r.next();
+                for (int i = 0; i < depth; i++) {
+                    if (!mbar_wait(empty + 8 * r.idx, r.phase ^ 1u)) report_timeout(g_err, 3);
+                    r.next();
+                }
+            }
         }
     } else if (warp == 2) {
         if (lane == 0 && rank == 1) {  // -------------------- relay of the odd CTA's activation tiles

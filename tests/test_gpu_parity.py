@@ -104,6 +104,22 @@ def test_tree_decision_matches_the_oracle(model_factory, qtype):
     assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
 
 
+def test_two_sm_gemm_short_prefills_are_repeatable(model_factory):
+    """Many short full-width prefills (91 tokens: one token tile of 96, so each CTA pair of the
+    2-SM GEMM takes one unit and leaves soon after its last MMA, with up to six stage releases in
+    flight) must give the same logits every time. This is the shape an earlier 2-SM kernel faulted
+    on when a CTA could leave before the multicast stage releases addressed to it had landed."""
+    path = model_factory(WIDE_CFG, "Q8_0", seed=31)
+    prompt = [1] + toks(90, 71)
+    with jv.Model(path, kv_pool_mb=256) as m, ctx(m) as c:
+        first = c.forward(prompt)
+        for i in range(40):
+            c.kv_cache.reset()
+            again = c.forward(prompt)
+            assert again.tobytes() == first.tobytes(), i
+        assert np.isfinite(first).all()
+
+
 def test_odd_row_tile_counts_match_the_oracle(model_factory):
     """A width of 384 leaves the O and down projections three 128-row tiles each: the CTA-pair GEMM
     (k_gemm_2sm, the default) runs the matrices with an even tile count and hands those to the
