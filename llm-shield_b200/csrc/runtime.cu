@@ -80,7 +80,11 @@ struct DevVec {
             p = nullptr;
             cap = 0;
             p = dalloc<T>(n);
-            JV_CUDA(cudaMemset(p, 0, n * sizeof(T)));
+            // Zeroed and finished before the buffer is handed out: the contexts' streams are
+            // non-blocking, so a memset left pending on the legacy stream could land after (and
+            // wipe) what the first call's kernels write into the new buffer.
+            JV_CUDA(cudaMemsetAsync(p, 0, n * sizeof(T), cudaStreamLegacy));
+            JV_CUDA(cudaStreamSynchronize(cudaStreamLegacy));
             cap = n;
         }
         return p;
@@ -1500,7 +1504,8 @@ int jv_ctx_create(jv_model* m, int32_t initial_capacity, jv_ctx** out) {
         set_device(m);
         JV_CUDA(cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking));
         x->d_err = dalloc<int>(2);  // error code, then the site of a timeout
-        JV_CUDA(cudaMemset(x->d_err, 0, 2 * sizeof(int)));
+        JV_CUDA(cudaMemsetAsync(x->d_err, 0, 2 * sizeof(int), x->stream));
+        JV_CUDA(cudaStreamSynchronize(x->stream));
         x->capacity = std::max(1, initial_capacity > 0 ? initial_capacity : 512);
         ctx_ensure_capacity(x, 1);
     });

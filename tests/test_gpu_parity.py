@@ -104,11 +104,13 @@ def test_tree_decision_matches_the_oracle(model_factory, qtype):
     assert int(np.argmax(z_gpu)) == int(np.argmax(z_cpu))
 
 
-def test_two_sm_gemm_short_prefills_are_repeatable(model_factory):
-    """Many short full-width prefills (91 tokens: one token tile of 96, so each CTA pair of the
-    2-SM GEMM takes one unit and leaves soon after its last MMA, with up to six stage releases in
-    flight) must give the same logits every time. This is the shape an earlier 2-SM kernel faulted
-    on when a CTA could leave before the multicast stage releases addressed to it had landed."""
+def test_repeated_short_prefills_are_bit_identical_from_the_first_call(model_factory):
+    """The first forward on a freshly loaded model and forty more after it give the same logits.
+    The first call allocates the context's buffers (a zeroing memset left pending on the legacy
+    stream once wiped what the first call's kernels had written), and 91 full-width tokens are one
+    token tile of 96, so each CTA pair of the 2-SM GEMM takes one unit and leaves soon after its
+    last MMA with up to six stage releases in flight: the shape an earlier 2-SM kernel faulted on
+    when a CTA could leave before the multicast releases addressed to it had landed."""
     path = model_factory(WIDE_CFG, "Q8_0", seed=31)
     prompt = [1] + toks(90, 71)
     with jv.Model(path, kv_pool_mb=256) as m, ctx(m) as c:
