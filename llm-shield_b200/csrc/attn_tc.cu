@@ -23,10 +23,9 @@
 // a different position modulo 8 in the page than in the tile (a branch segment starting off a
 // multiple of 8) goes chunk by chunk through cp.async instead.
 // Each tile has its own MMA issuer (lane 0 of warp 10 for A, of warp 11 for B; warp 10 also owns
-// TMEM): one thread issues a tcgen05.mma about every 150 SM cycles whatever N is, while the tensor
-// core finishes an N = 128 MMA in about half that, so a single issuer would leave it half idle. An
-// issuer runs an event loop over its own tile: the next P V as soon as its P and V are in place,
-// S_X(b) as soon as K(b) is and the softmax has read S_X(b - 1). Each tile releases a K stage
+// TMEM): a single thread issuing this loop's MMAs left the tensor core half idle. An issuer works
+// through its own tile in order: S_X(b + 1) as soon as K(b + 1) is in place and the softmax has read
+// S_X(b), then P V(b) once P_X(b) and V(b) are. Each tile releases a K stage
 // through its own barrier (the two tiles' S MMAs are not ordered); a V stage is released by the
 // last tile to use it, whose P V follows the other's through the P buffer. Every wait is bounded
 // (WAIT_CYCLES of the SM clock); on expiry the role records JV_ERR_DEVICE_TIMEOUT and stops.
@@ -289,48 +288,43 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
             bool ok = nbt == 0 || mbar_wait(q_full, 0);
             tc_fence_after();
             const uint32_t q = s_addr(Qs + x * AT_TILE), o = tmem + (uint32_t)(x * 128), d = tmem + 256u + (uint32_t)(x * 128);
-            int ns = 0, u = 0;  // next S block, next P V block of this tile
-            long long idle_since = clock64();
-            // Each barrier tested here is at most one phase behind the one wanted: this thread
-            // consumed the phase before it (P_X(u - 1), V(u - 2), K(ns - 2), the read of S_X(ns - 2)),
-            // and the next phase needs this thread's own later MMAs.
-            while (ok && u < nbt) {
-                bool did = false;
-                if (ns > u && mbar_test(p_full + 8 * x, (uint32_t)(u & 1)) &&
-                    mbar_test(v_full + 8 * (u & 1), (uint32_t)((u >> 1) & 1))) {
-                    tc_fence_after();
-                    const uint32_t v = s_addr(Vs + (u & 1) * AT_TILE), p = s_addr(Ps);
+            // In order: S(0), then per block b: S(b + 1), P V(b). S(b + 1) needs only K(b + 1) and
+            // the softmax's read of S(b), which comes before it waits for the P buffer, so the
+            // order cannot stall; each wait tests one barrier, at most one phase behind the one
+            // wanted (this thread consumed the phase before). Measured faster than an event loop
+            // over all four barriers (704 vs 678 TFLOP/s on C5 trees).
+            auto issue_s = [&](int b) -> bool {
+                if (!mbar_poll(k_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) return false;
+                if (b > 0 && !mbar_poll(s_free + 8 * x, (uint32_t)((b - 1) & 1))) return false;
+                tc_fence_after();
+                const uint32_t k = s_addr(Ks + (b & 1) * AT_TILE);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                        umma(o, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (u > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    // tile B's P V is the last use of V(u) wherever B takes the block
-                    if (x == 1 || nbB == 0) umma_commit(v_empty + 8 * (u & 1));
-                    umma_commit(o_done + 8 * x);  // last: its arrival implies the release before it
-                    u++;
-                    did = true;
-                } else if (ns < nbt && mbar_test(k_full + 8 * (ns & 1), (uint32_t)((ns >> 1) & 1)) &&
-                           (ns == 0 || mbar_test(s_free + 8 * x, (uint32_t)((ns - 1) & 1)))) {
-                    // S_X(ns) overwrites S_X(ns - 1): only once the softmax has read that
-                    tc_fence_after();
-                    const uint32_t k = s_addr(Ks + (ns & 1) * AT_TILE);
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                    umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(k_empty + 8 * (2 * x + (b & 1)));
+                umma_commit(s_full + 8 * x);
+                return true;
+            };
+            auto issue_pv = [&](int b) -> bool {
+                if (!mbar_poll(p_full + 8 * x, (uint32_t)(b & 1))) return false;
+                if (!mbar_poll(v_full + 8 * (b & 1), (uint32_t)((b >> 1) & 1))) return false;
+                tc_fence_after();
+                const uint32_t v = s_addr(Vs + (b & 1) * AT_TILE), p = s_addr(Ps);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
-                        umma(d, sdesc(q + off), sdesc(k + off), id_s, kk > 0 ? 1u : 0u);
-                    }
-                    umma_commit(k_empty + 8 * (2 * x + (ns & 1)));
-                    umma_commit(s_full + 8 * x);
-                    ns++;
-                    did = true;
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t off = (uint32_t)((kk >> 2) * 16384 + (kk & 3) * 32);
+                    umma(o, sdesc(p + off), sdesc_mn(v + kk * 2048), id_pv, (b > 0 || kk > 0) ? 1u : 0u);
                 }
-                if (did) {
-                    idle_since = clock64();
-                } else {
-                    __nanosleep(20);
-                    if (clock64() - idle_since > WAIT_CYCLES) ok = false;
-                }
+                if (x == 1 || nbB == 0) umma_commit(v_empty + 8 * (b & 1));
+                umma_commit(o_done + 8 * x);
+                return true;
+            };
+            if (ok && nbt > 0) ok = issue_s(0);
+            for (int b = 0; ok && b < nbt; b++) {
+                if (b + 1 < nbt) ok = issue_s(b + 1);
+                if (ok) ok = issue_pv(b);
             }
             if (!ok) report_timeout(err, x ? 16 + 6 : 16 + 3);
         }
