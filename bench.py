@@ -544,7 +544,18 @@ def gemm_traffic_per_launch(config: str):
     return None
 
 
+def json_stdout():
+    """The result line's own handle on the process's standard output. File descriptor 1 then points
+    at standard error, so whatever a library writes there on its own (NCCL prints its version banner
+    from C when a communicator starts) cannot land beside the one JSON line the driver reads."""
+    out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    return out
+
+
 def main():
+    result_out = json_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -568,7 +579,7 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args, world)), flush=True)
+            print(json.dumps(run_reference(args, world)), file=result_out, flush=True)
         return
 
     dist = None
@@ -595,7 +606,7 @@ def main():
                              10**6 if args.config == "c4" else max(1, args.steps))
             res["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0 and res is not None:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=result_out, flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
