@@ -122,6 +122,29 @@ def test_repeated_short_prefills_are_bit_identical_from_the_first_call(model_fac
         assert np.isfinite(first).all()
 
 
+@pytest.mark.parametrize("entry", ["forward_tree", "forward_selected", "decode_greedy"])
+def test_the_first_call_on_a_fresh_model_matches_the_second(model_factory, entry):
+    """Every public entry point's first call on a freshly loaded model (which allocates the
+    context's buffers) gives the same bits as the same call repeated on the reset cache."""
+    path = model_factory(WIDE_CFG, "Q8_0", seed=32)
+    trunk = [1] + toks(150, 81)
+    branches = [toks(n, 90 + i) for i, n in enumerate((20, 7, 33))]
+
+    def call(c):
+        if entry == "forward_tree":
+            return np.asarray(c.forward_tree(trunk, branches, VERDICT_ROWS))
+        if entry == "forward_selected":
+            return np.asarray(c.forward_selected(trunk, VERDICT_ROWS))
+        c.prefill(trunk)
+        return np.asarray(c.decode_greedy(1500, 8))
+
+    with jv.Model(path, kv_pool_mb=256) as m, ctx(m) as c:
+        first = call(c)
+        c.kv_cache.reset()
+        second = call(c)
+    assert first.tobytes() == second.tobytes(), (first, second)
+
+
 def test_odd_row_tile_counts_match_the_oracle(model_factory):
     """A width of 384 leaves the O and down projections three 128-row tiles each: the CTA-pair GEMM
     (k_gemm_2sm, the default) runs the matrices with an even tile count and hands those to the
