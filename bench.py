@@ -525,13 +525,12 @@ def run_decode(args, rank, world, dist, ctx, stream):
 
 def gemm_kernel_name() -> str:
     """The prefill GEMM kernel the library runs (JV_GEMM_KERNEL selects another; see gemm_tc.cu)."""
-    return {"1sm": "k_gemm_tc", "tmem": "k_gemm_tm"}.get(os.environ.get("JV_GEMM_KERNEL", ""), "k_gemm_2sm")
+    return {"tmem": "k_gemm_tm"}.get(os.environ.get("JV_GEMM_KERNEL", ""), "k_gemm_tc")
 
 
 def gemm_traffic_per_launch(config: str):
     """DRAM bytes per GEMM launch from the committed ncu summary of this configuration and kernel."""
-    stem = "gemm_2sm" if gemm_kernel_name() == "k_gemm_2sm" else "gemm_tc"
-    for name in (f"{stem}_{config}.md", f"gemm_tc_{config}.md", "gemm_tc_c2.md"):
+    for name in (f"gemm_tc_{config}.md", "gemm_tc_c2.md"):
         f = REPO / "profiles" / name
         if not f.exists():
             continue

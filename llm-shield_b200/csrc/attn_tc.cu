@@ -112,15 +112,6 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) { retur
 __device__ __forceinline__ void mbar_add_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
 
 __global__ void __launch_bounds__(AT_THREADS, 1) k_attn_tc(AttnArgs a) {
     extern __shared__ uint8_t at_raw[];

@@ -30,15 +30,13 @@
 // Every mbarrier wait is bounded (WAIT_CYCLES of the SM clock, about 2 s), with one verdict per
 // warp. On expiry the warp sets the error word and its role stops; the others then time out in turn; the producer
 // waits (bounded) for its copies in flight, the MMA lane drains its own MMAs, and the CTA
-// frees its TMEM and returns. k_gemm_tc and k_gemm_tm launch no clusters; k_gemm_2sm launches
-// CTA pairs and multicasts only its tcgen05.commit arrivals. No load here is a multicast load, and
-// nothing here reads another GPU's memory.
+// frees its TMEM and returns. No cluster launch and no multicast: nothing here reads another
+// GPU's memory.
 #include "tc_common.cuh"
 
 namespace jv {
 
 constexpr int GEMM_THREADS = 512;
-constexpr int DEC_THREADS = 256;
 constexpr int DEC_WARP0 = 8;
 constexpr int DEC_WARPS_PER_GROUP = 4;  // two decoder groups, alternate k steps
 // Bytes b0, b1 of x (picked by the byte_perm selector) as the fp16 pair (1024 + b0, 1024 + b1):
@@ -556,361 +554,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// k_gemm_2sm: the same product on CTA pairs with the 2-SM MMA (tcgen05.mma.cta_group::2, M = 256).
-//
-// A cluster of two CTAs takes a pair of 128-row weight tiles (2p, 2p + 1): CTA rank r streams and
-// decodes tile 2p + r into its own shared memory, as k_gemm_tc does, and loads HALF of each
-// activation tile (tokens t0 + r * bn/2 ..), so a pipeline stage is 16 KB of decoded weights plus
-// bn * 64 B of activations and five stages fit beside the raw ring where k_gemm_tc holds three.
-// One lane of the even CTA issues every MMA: M = 256 (each CTA's 128 rows), N = bn (each CTA's
-// half of the tokens), accumulating in both CTAs' TMEM; each CTA drains its own 128 rows x bn.
-// Hand-offs across the pair:
-//   * the odd CTA's decoder warps arrive on the even CTA's st_full (remote mbarrier arrive,
-//     after fence.proxy.async of their stores);
-//   * the odd CTA's activation copies complete on its own barrier; one relay lane (warp 2)
-//     forwards each completed stage to the even CTA's st_full, which also takes the even CTA's
-//     own copy and decoder warps, so the MMA lane tests one barrier per k step;
-//   * the MMA lane commits with .multicast::cluster, so st_empty and acc_full arrive in both CTAs;
-//   * the odd CTA's epilogue warps arrive on the even CTA's acc_empty.
-// Remote arrives and the waits use the default mbarrier semantics; arrivals with release and
-// acquire at cluster scope measured ~0.8 us from arrive to the MMA lane seeing it. No TMA, no
-// multicast load: the copies are
-// plain cp.async.bulk into the issuing CTA's own shared memory. Every wait is bounded; a CTA
-// leaves only after a cluster barrier, once no MMA can read its shared memory.
-// Measured on C5 (26 layers, one B200 under its power cap): 956 TFLOP/s against 919 for k_gemm_tc,
-// 121.8K against 115.4K tokens/s for the whole step.
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ int cluster_index() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;\n" : "=r"(r));
-    return (int)r;
-}
-__device__ __forceinline__ int cluster_count() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%nclusterid.x;\n" : "=r"(r));
-    return (int)r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-// The shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-// Arrive on an mbarrier of the other CTA (default semantics, as for a local arrive).
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(caddr) : "memory");
-}
-// This CTA's barrier at `local` (a plain arrive), or the even CTA's barrier at the same offset.
-__device__ __forceinline__ void mbar_arrive_even(uint32_t local, uint32_t even_caddr, uint32_t rank) {
-    if (rank == 0) mbar_arrive(local);
-    else mbar_arrive_remote(even_caddr);
-}
-__device__ __forceinline__ void umma2(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-            tmem_d),
-        "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-        : "memory");
-}
-// Arrives on the mbarrier at this shared-memory offset in both CTAs once the MMAs issued so far
-// have completed.
-__device__ __forceinline__ void umma2_commit_both(uint32_t bar) {
-    asm volatile(
-        "{\n.reg .b16 m;\nmov.b16 m, 3;\n"
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n}\n" ::"r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void umma2_commit_local(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tmem_alloc2(uint32_t slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot), "r"(ncols) : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-template <int TYPE, int EPI, bool CSPLIT>
-__global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_2sm(TcParams p) {
-    const uint8_t* __restrict__ g_w = p.w;
-    const __half* __restrict__ g_x = p.x;
-    float* __restrict__ g_y = p.y;
-    int* __restrict__ g_err = p.err;
-    __half* __restrict__ g_xs_out = p.xs_out;
-    float* g_ws = p.ws;
-    int* __restrict__ g_ctr = p.counters;
-    constexpr int epi = EPI;
-    const int ksteps = p.ksteps, T = p.T, tpad = p.tpad, bn = p.bn, ldy = p.ldy, ncols = p.ncols;
-    const int splits = p.splits, ttiles = p.ttiles, units = p.units, nr_ = p.nr, ns_ = p.ns;
-    const int raw_off = p.raw_off, b_off = p.b_off, bar_off = p.bar_off;
-    extern __shared__ uint8_t gsm_raw[];
-    uint8_t* sm = gsm_raw + ((1024u - (s_addr(gsm_raw) & 1023u)) & 1023u);
-    const int cb = chunk_bytes(TYPE);
-    const int NR = nr_, NS = ns_;
-    const uint32_t rank = cluster_rank();
-    const int cid = cluster_index(), ncl = cluster_count();
-    const int hb = bn >> 1;  // this CTA's tokens of a tile
-    uint8_t* As = sm;             // NS x 16 KB decoded weights
-    uint8_t* Bs = sm + b_off;     // NS x hb*128 activations
-    uint8_t* Rs = sm + raw_off;   // NR x chunk raw quant blocks
-    uint64_t* bars = (uint64_t*)(sm + bar_off);
-    // The same offsets in both CTAs. Used in the even CTA only: st_full (its activation copy,
-    // the odd CTA's relay of its copy, and four decoder warps of each CTA: one barrier per stage,
-    // so the MMA lane tests one per k step), acc_empty (four epilogue warps of each), drained.
-    // In the odd CTA only: b_local (its own copy landed).
-    const uint32_t raw_full = s_addr(bars), raw_empty = raw_full + 8 * NR;
-    const uint32_t st_full = raw_empty + 8 * NR, st_empty = st_full + 8 * NS;
-    const uint32_t b_local = st_empty + 8 * NS;
-    const uint32_t acc_full = b_local + 8 * NS, acc_empty = acc_full + 16, drained = acc_empty + 16;
-    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 3 * NS + 5);
-    volatile int* last_flag = (volatile int*)(tslot + 1);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nks = ksteps / splits;
-    const uint32_t hbytes = (uint32_t)hb * 128u;
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_WARPS_PER_GROUP); }
-        for (int i = 0; i < NS; i++) {
-            mbar_init(st_full + 8 * i, 2 * DEC_WARPS_PER_GROUP + 2);  // decoder warps, copy, relay
-            mbar_init(st_empty + 8 * i, 1);
-            mbar_init(b_local + 8 * i, 1);
-        }
-        for (int i = 0; i < 2; i++) { mbar_init(acc_full + 8 * i, 1); mbar_init(acc_empty + 8 * i, 8); }
-        mbar_init(drained, 1);
-        fence_barrier_init();
-    }
-    if (warp == 2) tmem_alloc2(s_addr(tslot), 2 * ncols);
-    tc_fence_before();
-    // both CTAs' barriers exist before either CTA arrives on the other's
-    cluster_sync_all();
-    tc_fence_after();
-    const uint32_t tmem = *tslot;
-    pdl_launch_dependents();
-
-    if (warp == 0 || warp == 3) {
-        if (lane == 0) {  // ----------------------------------------------- producers
-            const bool weights = warp == 0;
-            const int depth = weights ? NR : NS;
-            const uint32_t full = weights ? raw_full : (rank == 0 ? st_full : b_local);
-            const uint32_t empty = weights ? raw_empty : st_empty;
-            const uint32_t bytes = weights ? (uint32_t)cb : hbytes;
-            uint8_t* ring = weights ? Rs : Bs;
-            Ring r(depth);
-            bool ok = true;
-            int issued = 0;
-            if (!weights) pdl_wait();
-            for (int u = cid; u < units && ok; u += ncl) {
-                int tp, tt, sp;
-                unit_coords(u, splits, ttiles, tp, tt, sp);
-                const int tile = 2 * tp + (int)rank;
-                const int kb = sp * nks, t0 = tt * bn + (int)rank * hb;
-                if (!JV_CHECK(tile < p.tiles && kb + nks <= ksteps && t0 + hb <= tpad, g_err, BS_GEMM_UNIT)) break;
-                const uint8_t* src = weights ? g_w + ((int64_t)tile * ksteps + kb) * cb
-                                             : (const uint8_t*)(g_x + ((int64_t)kb * tpad + t0) * 64);
-                const int64_t step = weights ? (int64_t)cb : (int64_t)tpad * 128;
-                if (weights)
-                    for (int ks = 0; ks < RAW_PREFETCH && ks < nks; ks++) bulk_prefetch_l2(src + ks * step, bytes);
-                for (int ks = 0; ks < nks; ks++) {
-                    if (weights && ks + RAW_PREFETCH < nks) bulk_prefetch_l2(src + (ks + RAW_PREFETCH) * step, bytes);
-                    if (!mbar_wait(empty + 8 * r.idx, r.phase ^ 1u)) { ok = false; break; }
-                    mbar_expect_tx(full + 8 * r.idx, bytes);
-                    bulk_g2s(s_addr(ring + (size_t)r.idx * bytes), src + ks * step, bytes, full + 8 * r.idx);
-                    r.next();
-                    issued++;
-                }
-            }
-            if (!ok) report_timeout(g_err, weights ? 1 : 2);
-            // Never leave with copies in flight into this CTA's shared memory. The odd CTA's
-            // activation copies land on b_local; the even CTA's on st_full, whose phase also needs
-            // the relay and the decoder warps (on an error path the bounded wait outlasts any copy).
-            for (int i = 0; i < issued && i < depth; i++) {
-                r.prev();
-                if (!mbar_wait(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
-            }
-            if (!weights && ok) {
-                // The stage-empty barriers receive the MMA lane's commits asynchronously (the odd
-                // CTA's through the cluster, multicast): wait until the last use of every stage
-                // has been released, so that no arrival is still in flight into this CTA's shared
-                // memory when it leaves.
-                for (int i = 0; i < issued && i < depth; i++) r.next();
-                for (int i = 0; i < depth; i++) {
-                    if (!mbar_wait(empty + 8 * r.idx, r.phase ^ 1u)) report_timeout(g_err, 3);
-                    r.next();
-                }
-            }
-        }
-    } else if (warp == 2) {
-        if (lane == 0 && rank == 1) {  // -------------------- relay of the odd CTA's activation tiles
-            Ring rs(NS);
-            bool ok = true;
-            const uint32_t remote = cluster_addr(st_full, 0);
-            for (int u = cid; u < units && ok; u += ncl)
-                for (int ks = 0; ks < nks; ks++) {
-                    if (!mbar_wait(b_local + 8 * rs.idx, rs.phase)) { ok = false; break; }
-                    mbar_arrive_remote(remote + 8 * rs.idx);
-                    rs.next();
-                }
-            if (!ok) report_timeout(g_err, 9);
-        }
-    } else if (warp == 1) {
-        if (lane == 0 && rank == 0) {  // ----------------------------------------- MMA issue
-            const uint32_t idesc = idesc_f16(bn, 256);
-            Ring rs(NS);
-            bool ok = true;
-            int i = 0;
-            for (int u = cid; u < units && ok; u += ncl, i++) {
-                const int ab = i & 1;
-                if (!mbar_wait(acc_empty + 8 * ab, (uint32_t)((i >> 1) & 1) ^ 1u)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t acc = tmem + (uint32_t)(ab * ncols);
-                for (int ks = 0; ks < nks; ks++) {
-                    if (!mbar_poll(st_full + 8 * rs.idx, rs.phase)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_base = s_addr(As + rs.idx * 16384), b_base = s_addr(Bs + (size_t)rs.idx * hbytes);
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        umma2(acc, sdesc(a_base + 32 * j), sdesc(b_base + 32 * j), idesc, (ks > 0 || j > 0) ? 1u : 0u);
-                    umma2_commit_both(st_empty + 8 * rs.idx);
-                    rs.next();
-                }
-                if (ok) umma2_commit_both(acc_full + 8 * ab);
-            }
-            if (!ok) report_timeout(g_err, 4);
-            umma2_commit_local(drained);
-            if (!mbar_wait(drained, 0)) report_timeout(g_err, 5);
-        }
-    } else if (warp >= DEC_WARP0) {  // --------------------------------------- decode
-        const int grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
-        const int dt = threadIdx.x - (DEC_WARP0 + grp * DEC_WARPS_PER_GROUP) * 32;
-        const int c = dt & 7, r0 = dt >> 3;
-        const int a_off = r0 * 128 + ((c ^ (r0 & 7)) << 4);
-        const uint32_t st_full_even = cluster_addr(st_full, 0);
-        Ring rr(NR), rs(NS);
-        if (grp) { rr.next(); rs.next(); }
-        bool ok = true;
-        int k = 0;
-        for (int u = cid; u < units && ok; u += ncl) {
-            for (int ks = 0; ks < nks; ks++, k++) {
-                if ((k & 1) != grp) continue;
-                if (!warp_wait_all(raw_full + 8 * rr.idx, rr.phase)) { ok = false; break; }
-                const uint8_t* raw = Rs + rr.idx * cb;
-                uint4 v[8];
-#pragma unroll
-                for (int it = 0; it < 8; it++) v[it] = decode8<TYPE>(raw, r0 + 16 * it, c);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(raw_empty + 8 * rr.idx);
-                rr.next();
-                rr.next();
-                if (!warp_wait_all(st_empty + 8 * rs.idx, rs.phase ^ 1u)) { ok = false; break; }
-                uint8_t* A = As + rs.idx * 16384 + a_off;
-#pragma unroll
-                for (int it = 0; it < 8; it++) *(uint4*)(A + it * 16 * 128) = v[it];
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_even(st_full + 8 * rs.idx, st_full_even + 8 * rs.idx, rank);
-                rs.next();
-                rs.next();
-            }
-        }
-        if (!ok) report_timeout(g_err, 6);
-    } else if (warp >= 4) {  // ------------------------------------------------- epilogue
-        const int q = warp & 3;
-        constexpr bool counter_split = CSPLIT;
-        const uint32_t acc_empty_even = cluster_addr(acc_empty, 0);
-        pdl_wait();
-        int i = 0;
-        for (int u = cid; u < units; u += ncl, i++) {
-            int tp, tt, sp;
-            unit_coords(u, splits, ttiles, tp, tt, sp);
-            const int tile = 2 * tp + (int)rank;
-            const int t0 = tt * bn, ab = i & 1;
-            const bool w = warp_wait_all(acc_full + 8 * ab, (uint32_t)((i >> 1) & 1));
-            const bool ready = counter_split ? epi_all(w) : w;
-            tc_fence_after();
-            if (!ready) {
-                if (lane == 0) report_timeout(g_err, 7);
-                break;
-            }
-            const uint32_t tacc = tmem + (uint32_t)(ab * ncols) + ((uint32_t)(q * 32) << 16);
-            const int n = tile * 128 + q * 32 + lane;
-            const int tn = min(bn, T - t0);
-            float* mine = splits > 1 ? g_ws + (int64_t)sp * T * ldy : nullptr;
-            if (counter_split) {
-                drain_cols(tacc, 0, bn, DR_RAW, lane, q, n, tile, t0, tn, tpad, ldy, mine, nullptr, g_xs_out, g_err);
-                __threadfence();
-                epi_bar();
-                if (warp == 4 && lane == 0) {
-                    int* ctr = g_ctr + tile * ttiles + tt;
-                    int old = atomicAdd(ctr, 1);
-                    int is_last = old == splits - 1;
-                    if (is_last) atomicExch(ctr, 0);
-                    *last_flag = is_last;
-                }
-                epi_bar();
-                const bool last = *last_flag != 0;
-                epi_bar();
-                if (last) {
-                    __threadfence();
-                    drain_cols(tacc, 0, bn, epi == EPI_ADD ? DR_ADD : DR_STORE, lane, q, n, tile, t0, tn, tpad, ldy, g_y,
-                               g_ws + (int64_t)(1 - sp) * T * ldy, g_xs_out, g_err);
-                }
-            } else {
-                const int cend = u + ncl >= units ? drain_share(bn, 1) : bn;  // last unit: share 0
-                const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
-                drain_cols(tacc, 0, cend, kind, lane, q, n, tile, t0, tn, tpad, ldy, epi == EPI_PARTIAL ? mine : g_y, nullptr,
-                           g_xs_out, g_err);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_even(acc_empty + 8 * ab, acc_empty_even + 8 * ab, rank);
-        }
-    }
-    // The decoder warps drain two thirds of the last unit's columns, as in k_gemm_tc.
-    if (warp >= DEC_WARP0 && !CSPLIT && cid < units) {
-        const int my_units = (units - cid + ncl - 1) / ncl;
-        const int il = my_units - 1, ul = cid + il * ncl;
-        int tp, tt, sp;
-        unit_coords(ul, splits, ttiles, tp, tt, sp);
-        const int tile = 2 * tp + (int)rank;
-        const int ab = il & 1, q = warp & 3, grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
-        pdl_wait();
-        const bool ready = warp_wait_all(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
-        tc_fence_after();
-        if (ready) {
-            const int t0 = tt * bn;
-            const uint32_t tacc = tmem + (uint32_t)(ab * ncols) + ((uint32_t)(q * 32) << 16);
-            const int kind = epi == EPI_PARTIAL ? DR_RAW : epi == EPI_SWIGLU ? DR_SWIGLU : epi == EPI_ADD ? DR_ADD : DR_STORE;
-            drain_cols(tacc, drain_share(bn, grp + 1), drain_share(bn, grp + 2), kind, lane, q, tile * 128 + q * 32 + lane, tile,
-                       t0, min(bn, T - t0), tpad, ldy, epi == EPI_PARTIAL ? g_ws + (int64_t)sp * T * ldy : g_y, nullptr,
-                       g_xs_out, g_err);
-        } else {
-            report_timeout(g_err, 8);
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    // No MMA reads either CTA's shared memory or TMEM any more (the even CTA's MMA lane waited
-    // for all of them); nothing arrives on the other CTA's barriers after this.
-    cluster_sync_all();
-    if (warp == 2) {
-        tc_fence_after();
-        tmem_dealloc2(tmem, 2 * ncols);
-    }
-}
-
-// ------------------------------------------------------------------------------------------------
 // k_gemm_tm: the same product with the decoded weights (the MMA's A operand) in tensor memory.
 //
 // In k_gemm_tc every k step moves ~113 KB through shared memory at N = 256 (raw chunk in and
@@ -990,7 +633,7 @@ template <int TYPE>
 __device__ __forceinline__ void row_decode(const RowRaw<TYPE>& r, uint32_t (&v)[32]) {
     const __half2 d0 = __half2half2(__ushort_as_half((unsigned short)(r.d & 0xFFFFu)));
     const __half2 d1 = __half2half2(__ushort_as_half((unsigned short)(r.d >> 16)));
-    if (TYPE == T_Q8_0) {
+    if constexpr (TYPE == T_Q8_0) {
         const __half2 bias = __floats2half2_rn(1152.f, 1152.f);  // 1024 + 128
 #pragma unroll
         for (int i = 0; i < 16; i++) {  // word i = weights 4i .. 4i + 3
@@ -999,36 +642,36 @@ __device__ __forceinline__ void row_decode(const RowRaw<TYPE>& r, uint32_t (&v)[
             v[2 * i] = hu(__hmul2(__hsub2(byte_pair(x, 0x4140u), bias), d));
             v[2 * i + 1] = hu(__hmul2(__hsub2(byte_pair(x, 0x4342u), bias), d));
         }
-        return;
-    }
-    // Q4_0 / Q5_1: block b's byte j holds weight j (low nibble) and j + 16 (high nibble).
+    } else {
+        // Q4_0 / Q5_1: block b's byte j holds weight j (low nibble) and j + 16 (high nibble).
 #pragma unroll
-    for (int b = 0; b < 2; b++) {
-        const __half2 d = b ? d1 : d0;
-        __half2 m2 = __float2half2_rn(0.f);
-        uint32_t qh = 0;
-        if (TYPE == T_Q5_1) {
-            m2 = __half2half2(__ushort_as_half((unsigned short)(b ? (r.m >> 16) : (r.m & 0xFFFFu))));
-            qh = b ? r.qh.y : r.qh.x;
-        }
+        for (int b = 0; b < 2; b++) {
+            const __half2 d = b ? d1 : d0;
+            __half2 m2 = __float2half2_rn(0.f);
+            uint32_t qh = 0;
+            if (TYPE == T_Q5_1) {
+                m2 = __half2half2(__ushort_as_half((unsigned short)(b ? (r.m >> 16) : (r.m & 0xFFFFu))));
+                qh = b ? r.qh.y : r.qh.x;
+            }
 #pragma unroll
-        for (int half = 0; half < 2; half++) {  // weights 16 * half .. 16 * half + 15 of the block
+            for (int half = 0; half < 2; half++) {  // weights 16 * half .. 16 * half + 15 of the block
 #pragma unroll
-            for (int i = 0; i < 4; i++) {       // word i of the block: bytes 4i .. 4i + 3
-                uint32_t x = w_at(r.q[b], i);
-                x = half ? (x >> 4) & 0x0F0F0F0Fu : x & 0x0F0F0F0Fu;
-                const int e = 16 * half + 4 * i;  // first weight of these four within the block
-                const int col = 16 * b + e / 2;
-                if (TYPE == T_Q4_0) {
-                    const __half2 bias = __floats2half2_rn(1032.f, 1032.f);  // 1024 + 8
-                    v[col] = hu(__hmul2(__hsub2(byte_pair(x, 0x4140u), bias), d));
-                    v[col + 1] = hu(__hmul2(__hsub2(byte_pair(x, 0x4342u), bias), d));
-                } else {
-                    const uint32_t h4 = (qh >> e) & 0xFu;
-                    x |= ((h4 & 1u) << 4) | ((h4 & 2u) << 11) | ((h4 & 4u) << 18) | ((h4 & 8u) << 25);
-                    const __half2 bias = __floats2half2_rn(1024.f, 1024.f);
-                    v[col] = hu(__hfma2(__hsub2(byte_pair(x, 0x4140u), bias), d, m2));
-                    v[col + 1] = hu(__hfma2(__hsub2(byte_pair(x, 0x4342u), bias), d, m2));
+                for (int i = 0; i < 4; i++) {       // word i of the block: bytes 4i .. 4i + 3
+                    uint32_t x = w_at(r.q[b], i);
+                    x = half ? (x >> 4) & 0x0F0F0F0Fu : x & 0x0F0F0F0Fu;
+                    const int e = 16 * half + 4 * i;  // first weight of these four within the block
+                    const int col = 16 * b + e / 2;
+                    if (TYPE == T_Q4_0) {
+                        const __half2 bias = __floats2half2_rn(1032.f, 1032.f);  // 1024 + 8
+                        v[col] = hu(__hmul2(__hsub2(byte_pair(x, 0x4140u), bias), d));
+                        v[col + 1] = hu(__hmul2(__hsub2(byte_pair(x, 0x4342u), bias), d));
+                    } else {
+                        const uint32_t h4 = (qh >> e) & 0xFu;
+                        x |= ((h4 & 1u) << 4) | ((h4 & 2u) << 11) | ((h4 & 4u) << 18) | ((h4 & 8u) << 25);
+                        const __half2 bias = __floats2half2_rn(1024.f, 1024.f);
+                        v[col] = hu(__hfma2(__hsub2(byte_pair(x, 0x4140u), bias), d, m2));
+                        v[col + 1] = hu(__hfma2(__hsub2(byte_pair(x, 0x4342u), bias), d, m2));
+                    }
                 }
             }
         }
@@ -1262,7 +905,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tm(TcParams p) {
 // product with few row tiles (the 48-tile QKV, the split 24-tile projections) takes two tiles of
 // T / 2 so that it still covers most SMs; one with many row tiles (gate/up, the head) keeps one
 // tile of T, which halves its MMA instructions and still fills the SMs. tpad is a multiple of both.
-enum GemmKernel : int { GK_2SM = 0, GK_1SM = 1, GK_TMEM = 2 };
+enum GemmKernel : int { GK_1SM = 1, GK_TMEM = 2 };
 static bool gemm_on_smem_a();
 static int gemm_max_bn() { return gemm_on_smem_a() ? 256 : TM_MAX_BN; }
 int gemm_tpad_for(int T) {
@@ -1283,16 +926,13 @@ int gemm_bn_for(int T, int units_per_tile, int sm_count) {
 
 static int g_sm_count = 0;
 
-// The prefill GEMM kernel: k_gemm_2sm by default (CTA pairs, M = 256; a matrix with an odd number
-// of 128-row tiles runs on k_gemm_tc), JV_GEMM_KERNEL=1sm for k_gemm_tc everywhere, and
-// JV_GEMM_KERNEL=tmem for k_gemm_tm (decoded weights in TMEM, token tiles of at most 224). All give
-// the same bits (test_gemm_kernels_are_bit_identical); k_gemm_2sm is the fastest measured.
+// The prefill GEMM kernel: k_gemm_tc, or with JV_GEMM_KERNEL=tmem k_gemm_tm (decoded weights in
+// TMEM, token tiles of at most 224). Both give the same bits (test_gemm_kernels_are_bit_identical).
 static GemmKernel gemm_kernel_choice() {
     static const GemmKernel v = [] {
         const char* e = getenv("JV_GEMM_KERNEL");
         if (e != nullptr && strcmp(e, "tmem") == 0) return GK_TMEM;
-        if (e != nullptr && strcmp(e, "1sm") == 0) return GK_1SM;
-        return GK_2SM;
+        return GK_1SM;
     }();
     return v;
 }
@@ -1342,47 +982,6 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
             JV_CUDA(cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev));
         }
         launch_pdl(k_gemm_tm<TYPE, EPI, CSPLIT>, dim3(std::min(p.units, g_sm_count)), dim3(GEMM_THREADS), smem, s, p);
-        note_launch();
-        return;
-    }
-    if (gemm_kernel_choice() == GK_2SM && w.tiles % 2 == 0) {
-        // k_gemm_2sm: work units are pairs of row tiles; a stage holds half an activation tile.
-        // As many stages (up to 6) as leave room for 4 raw chunks; the raw ring takes the rest.
-        p.units = (p.tiles / 2) * p.ttiles * p.splits;
-        const size_t budget = 222 * 1024, stage = 16384 + (size_t)a.bn * 64;
-        int ns = 6;
-        while (ns > 2 && stage * ns + 4 * (size_t)cb > budget) ns--;
-        p.ns = ns;
-        p.nr = (int)std::min<size_t>(12, (budget - stage * p.ns) / cb);
-        if (p.nr < 2) throw Error(JV_ERR_ARG, "gemm: shared memory budget exceeded");
-        p.b_off = 16384 * p.ns;
-        p.raw_off = p.b_off + a.bn * 64 * p.ns;
-        p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
-        const size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
-        auto kern = k_gemm_2sm<TYPE, EPI, CSPLIT>;
-        static int max_clusters = 0;  // per instantiation: its shared memory decides residency
-        if (max_clusters == 0) {
-            JV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(2);
-            cfg.blockDim = dim3(GEMM_THREADS);
-            cfg.dynamicSmemBytes = smem;
-            cudaLaunchAttribute at[1];
-            at[0].id = cudaLaunchAttributeClusterDimension;
-            at[0].val.clusterDim.x = 2;
-            at[0].val.clusterDim.y = 1;
-            at[0].val.clusterDim.z = 1;
-            cfg.attrs = at;
-            cfg.numAttrs = 1;
-            int n = 0;
-            JV_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
-            if (n < 1) throw Error(JV_ERR_UNSUPPORTED, "gemm: no resident CTA pair for the 2-SM kernel");
-            max_clusters = n;
-        } else {
-            JV_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        }
-        const int clusters = std::min(p.units, max_clusters);
-        launch_pdl_cluster(kern, dim3(2 * clusters), dim3(GEMM_THREADS), smem, s, 2, p);
         note_launch();
         return;
     }

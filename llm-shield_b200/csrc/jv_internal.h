@@ -395,26 +395,6 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
     cfg.numAttrs = 1;
     JV_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...));
 }
-// The same with thread-block clusters of `cluster_x` CTAs along x (grid.x a multiple of it).
-template <class... KArgs, class... Args>
-void launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster_x,
-                        Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    at[1].id = cudaLaunchAttributeClusterDimension;
-    at[1].val.clusterDim.x = (unsigned)cluster_x;
-    at[1].val.clusterDim.y = 1;
-    at[1].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 2;
-    JV_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...));
-}
 #endif
 
 // The calling thread's jv_last_error() message; returns code.

@@ -643,7 +643,6 @@ const char* timeout_site(int site) {
         case 6: return "tensor-core GEMM, decoders";
         case 7: return "tensor-core GEMM, epilogue";
         case 8: return "tensor-core GEMM, decoders draining the last tile";
-        case 9: return "tensor-core GEMM (CTA pairs), relay of the second CTA's activation tiles";
         case 17: return "tensor-core attention, K loader";
         case 18: return "tensor-core attention, V loader";
         case 19: return "tensor-core attention, MMA issuer";

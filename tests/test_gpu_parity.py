@@ -107,10 +107,8 @@ def test_tree_decision_matches_the_oracle(model_factory, qtype):
 def test_repeated_short_prefills_are_bit_identical_from_the_first_call(model_factory):
     """The first forward on a freshly loaded model and forty more after it give the same logits.
     The first call allocates the context's buffers (a zeroing memset left pending on the legacy
-    stream once wiped what the first call's kernels had written), and 91 full-width tokens are one
-    token tile of 96, so each CTA pair of the 2-SM GEMM takes one unit and leaves soon after its
-    last MMA with up to six stage releases in flight: the shape an earlier 2-SM kernel faulted on
-    when a CTA could leave before the multicast releases addressed to it had landed."""
+    stream once wiped what the first call's kernels had written); 91 full-width tokens are one
+    token tile of 96, so every GEMM launch is short, one work unit per CTA."""
     path = model_factory(WIDE_CFG, "Q8_0", seed=31)
     prompt = [1] + toks(90, 71)
     with jv.Model(path, kv_pool_mb=256) as m, ctx(m) as c:
@@ -146,10 +144,9 @@ def test_the_first_call_on_a_fresh_model_matches_the_second(model_factory, entry
 
 
 def test_odd_row_tile_counts_match_the_oracle(model_factory):
-    """A width of 384 leaves the O and down projections three 128-row tiles each: the CTA-pair GEMM
-    (k_gemm_2sm, the default) runs the matrices with an even tile count and hands those to the
-    one-CTA kernel. Per-layer hidden states (activation capture) and the product path's verdicts
-    against the oracle."""
+    """A width of 384 leaves the O and down projections three 128-row tiles each (and one head per
+    KV head group of four): per-layer hidden states (activation capture) and the product path's
+    verdicts against the oracle."""
     from jevstral_b200.synth import SynthConfig
 
     cfg = SynthConfig(layers=2, hidden=384, heads=4, kv_heads=1, head_dim=128, ff=512, vocab=16384)
@@ -566,9 +563,8 @@ def test_tensor_core_gemm_matches_the_reference_gemm(model_factory):
 
 @pytest.mark.parametrize("qtype", ["Q8_0", "Q5_1", "Q4_0"])
 def test_gemm_kernels_are_bit_identical(model_factory, qtype):
-    """The three prefill GEMM kernels on the same model: k_gemm_2sm (the default: CTA pairs, 2-SM
-    MMA with M = 256, half an activation tile per CTA), k_gemm_tc (one CTA per 128-row tile,
-    JV_GEMM_KERNEL=1sm) and k_gemm_tm (decoded weights in TMEM, JV_GEMM_KERNEL=tmem). The same
+    """The two prefill GEMM kernels on the same model: k_gemm_tc (the default: decoded weights
+    staged in shared memory) and k_gemm_tm (decoded weights in TMEM, JV_GEMM_KERNEL=tmem). The same
     fp16 operands and the same K order, so every captured activation (the capture path's
     counter-combined K split) and the product path's verdict logits (split-K halves folded by
     the next RMSNorm) are the same bits, for a causal prefill of 300 tokens and a tree after it."""
@@ -590,17 +586,17 @@ def test_gemm_kernels_are_bit_identical(model_factory, qtype):
 
     paths = [str(REPO / "llm-shield_b200"), str(REPO)]
     outs = {}
-    for kernel in ("2sm", "1sm", "tmem"):
+    for kernel in ("tc", "tmem"):
         env = dict(os.environ)
         env.pop("JV_GEMM_KERNEL", None)
-        if kernel != "2sm":
+        if kernel != "tc":
             env["JV_GEMM_KERNEL"] = kernel
         r = subprocess.run([sys.executable, "-c", code, str(path)] + paths, env=env, capture_output=True, timeout=900)
         assert r.returncode == 0, r.stderr.decode()[-2000:]
         outs[kernel] = np.load(io.BytesIO(r.stdout))
-    ref = outs["2sm"]
+    ref = outs["tc"]
     assert len(ref.files) > 20
-    for kernel in ("1sm", "tmem"):
+    for kernel in ("tmem",):
         other = outs[kernel]
         assert set(other.files) == set(ref.files)
         diff = [k for k in ref.files if other[k].tobytes() != ref[k].tobytes()]
