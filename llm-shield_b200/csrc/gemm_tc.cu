@@ -323,14 +323,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     uint8_t* Bs = sm + b_off;     // NS x bn*128 activations
     uint8_t* Rs = sm + raw_off;   // NR x chunk raw quant blocks
     uint64_t* bars = (uint64_t*)(sm + bar_off);
-    // raw ring: raw_full (copy landed), raw_empty (8 decoder warps read it)
-    // stage ring: st_full (the activation tile landed and four decoder warps wrote the fp16
-    //             weights: one barrier, so the MMA lane tests one per k step), st_empty (the MMA
-    //             that read both completed)
+    // raw ring: raw_full (copy landed), raw_empty (4 decoder warps read it)
+    // stage ring: b_full (activation tile landed: the copy's transaction bytes alone), a_full
+    //             (4 decoder warps wrote the fp16 weights), st_empty (the MMA that read both
+    //             completed)
     const uint32_t raw_full = s_addr(bars), raw_empty = raw_full + 8 * NR;
-    const uint32_t st_full = raw_empty + 8 * NR, st_empty = st_full + 8 * NS;
+    const uint32_t b_full = raw_empty + 8 * NR, a_full = b_full + 8 * NS, st_empty = a_full + 8 * NS;
     const uint32_t acc_full = st_empty + 8 * NS, acc_empty = acc_full + 16, drained = acc_empty + 16;
-    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 2 * NS + 5);
+    uint32_t* tslot = (uint32_t*)(bars + 2 * NR + 3 * NS + 5);
     volatile int* last_flag = (volatile int*)(tslot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -340,7 +340,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < NR; i++) { mbar_init(raw_full + 8 * i, 1); mbar_init(raw_empty + 8 * i, DEC_WARPS_PER_GROUP); }
         for (int i = 0; i < NS; i++) {
-            mbar_init(st_full + 8 * i, DEC_WARPS_PER_GROUP + 1);  // decoder warps + the copy's expect_tx
+            mbar_init(b_full + 8 * i, 1);
+            mbar_init(a_full + 8 * i, DEC_WARPS_PER_GROUP);
             mbar_init(st_empty + 8 * i, 1);
         }
         for (int i = 0; i < 2; i++) { mbar_init(acc_full + 8 * i, 1); mbar_init(acc_empty + 8 * i, 4); }
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             // activation tiles (stage ring, freed by the MMA): neither waits on the other.
             const bool weights = warp == 0;
             const int depth = weights ? NR : NS;
-            const uint32_t full = weights ? raw_full : st_full, empty = weights ? raw_empty : st_empty;
+            const uint32_t full = weights ? raw_full : b_full, empty = weights ? raw_empty : st_empty;
             const uint32_t bytes = weights ? (uint32_t)cb : bbytes;
             uint8_t* ring = weights ? Rs : Bs;
             Ring r(depth);
@@ -392,8 +393,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
             }
             if (!ok) report_timeout(g_err, weights ? 1 : 2);
             // Never leave with copies in flight into this CTA's shared memory: wait for the
-            // last min(issued, ring) copies (an activation stage's phase also needs its decoder
-            // warps; on an error path the bounded wait outlasts any copy).
+            // last min(issued, ring) copies.
             for (int i = 0; i < issued && i < depth; i++) {
                 r.prev();
                 if (!mbar_wait(full + 8 * r.idx, r.phase)) report_timeout(g_err, 3);
@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 tc_fence_after();
                 const uint32_t acc = tmem + (uint32_t)(ab * ncols);
                 for (int ks = 0; ks < nks; ks++) {
-                    if (!mbar_poll(st_full + 8 * rs.idx, rs.phase)) {
+                    if (!mbar_poll(a_full + 8 * rs.idx, rs.phase) || !mbar_poll(b_full + 8 * rs.idx, rs.phase)) {
                         ok = false;
                         break;
                     }
@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
                 for (int it = 0; it < 8; it++) *(uint4*)(A + it * 16 * 128) = v[it];
                 fence_proxy_async();  // each writer's generic-proxy stores -> visible to the tensor core
                 __syncwarp();
-                if (lane == 0) mbar_arrive(st_full + 8 * rs.idx);
+                if (lane == 0) mbar_arrive(a_full + 8 * rs.idx);
                 rs.next();
                 rs.next();
             }
@@ -994,7 +994,7 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
     p.b_off = 16384 * p.ns;
     p.raw_off = p.b_off + a.bn * 128 * p.ns;
     p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
-    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 2 * p.ns + 5) + 16 + 1024;
+    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
     JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE, EPI, CSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (g_sm_count == 0) {
         int dev = 0;

@@ -124,8 +124,8 @@ def test_struct_layouts_match_the_binding(tmp_path):
 
 
 def test_status_codes_match_the_header():
-    """Every JV_* status in include/jv.h has the same value in the Python binding (and so in the
-    C# enum that INTEGRATION.md lists)."""
+    """Every JV_* status in include/jv.h has the same value in the Python binding (and so in a
+    C# enum generated from the same header)."""
     import re as _re
 
     from jevstral_b200 import _lib
