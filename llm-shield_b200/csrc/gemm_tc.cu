@@ -986,10 +986,16 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
         return;
     }
     // Ring depths within ~222 KB: 4 stages (activation tile + decoded weights) if at least 4
-    // raw chunks still fit, else 3; the raw ring takes the rest (up to 12 chunks).
+    // raw chunks still fit, else 3; the raw ring takes the rest (up to 12 chunks), in an EVEN
+    // number of slots. The two decoder groups take alternate k steps and wait on a raw slot by
+    // phase parity, which is exact only while the slot's barrier is at most one phase behind.
+    // With an even ring the slot's previous chunk belongs to the same group, which consumed it
+    // before; with an odd one it belongs to the other group, whose copy may still be in flight
+    // (a group runs up to NS + 2 chunks ahead of the MMA), and the parity test then passes on
+    // the wrong phase: a torn chunk is decoded and the ring's arrival counts go wrong.
     const size_t budget = 222 * 1024, stage = 16384 + (size_t)a.bn * 128;
     p.ns = (stage * 4 + 4 * (size_t)cb <= budget) ? 4 : 3;
-    p.nr = (int)std::min<size_t>(12, (budget - stage * p.ns) / cb);
+    p.nr = (int)std::min<size_t>(12, (budget - stage * p.ns) / cb) & ~1;
     if (p.nr < 2) throw Error(JV_ERR_ARG, "gemm: shared memory budget exceeded");
     p.b_off = 16384 * p.ns;
     p.raw_off = p.b_off + a.bn * 128 * p.ns;

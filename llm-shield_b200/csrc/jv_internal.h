@@ -372,6 +372,11 @@ void launch_kv_import(__half* pool, const int32_t* page_table, int64_t page_byte
 int64_t launches_total();
 
 void note_launch(int n = 1);
+// JV_DEBUG_SYNC (diagnostics): every programmatic-dependent launch is followed by a
+// synchronisation of its stream (outside stream capture), and a failure names that kernel and
+// the one launched before it. Launches then no longer overlap.
+bool debug_sync_enabled();
+void debug_after_launch(cudaStream_t s, const void* kernel);
 
 #ifdef __CUDACC__
 // Programmatic dependent launch. A kernel launched with launch_pdl may start while the
@@ -394,6 +399,7 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
     cfg.attrs = at;
     cfg.numAttrs = 1;
     JV_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...));
+    if (debug_sync_enabled()) debug_after_launch(s, (const void*)kernel);
 }
 #endif
 

@@ -8,12 +8,35 @@
 #include "jv_internal.h"
 
 #include <atomic>
+#include <cstdlib>
+#include <string>
 
 namespace jv {
 
 static std::atomic<int64_t> g_launches{0};
 void note_launch(int n) { g_launches += n; }
 int64_t launches_total() { return g_launches.load(); }
+
+bool debug_sync_enabled() {
+    static const bool on = getenv("JV_DEBUG_SYNC") != nullptr;
+    return on;
+}
+void debug_after_launch(cudaStream_t s, const void* kernel) {
+    static thread_local std::string prev = "(none)";
+    const char* name = nullptr;
+    if (cudaFuncGetName(&name, kernel) != cudaSuccess || name == nullptr) {
+        cudaGetLastError();
+        name = "(unnamed kernel)";
+    }
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &st) == cudaSuccess && st == cudaStreamCaptureStatusNone) {
+        const cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess)
+            throw Error(JV_ERR_DEVICE, std::string("after ") + name + " (the programmatic-dependent launch before it: " + prev +
+                                           "): " + cudaGetErrorString(e));
+    }
+    prev = name;
+}
 
 // ------------------------------------------------------------- re-tiling
 
