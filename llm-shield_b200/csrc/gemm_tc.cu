@@ -532,7 +532,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tc(TcParams p) {
         unit_coords(ul, splits, ttiles, tile, tt, sp);
         const int ab = il & 1, q = warp & 3, grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
         pdl_wait();
-        const bool ready = warp_wait_all(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
+        // `drained` (one phase, committed after the CTA's last MMA) rather than the last unit's
+        // acc_full: these warps never waited on the earlier units' phases, so with few k steps a
+        // unit two back could still be open and a parity test of acc_full would pass early.
+        const bool ready = warp_wait_all(drained, 0u);
         tc_fence_after();
         if (ready) {
             const int t0 = tt * bn;
@@ -878,7 +881,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_gemm_tm(TcParams p) {
         unit_coords(ul, splits, ttiles, tile, tt, sp);
         const int ab = il & 1, q = warp & 3, grp = (warp - DEC_WARP0) / DEC_WARPS_PER_GROUP;
         pdl_wait();
-        const bool ready = warp_wait_all(acc_full + 8 * ab, (uint32_t)((il >> 1) & 1));
+        // `drained` (one phase, committed after the CTA's last MMA) rather than the last unit's
+        // acc_full: these warps never waited on the earlier units' phases, so with few k steps a
+        // unit two back could still be open and a parity test of acc_full would pass early.
+        const bool ready = warp_wait_all(drained, 0u);
         tc_fence_after();
         if (ready) {
             const int t0 = tt * bn;
@@ -986,16 +992,19 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
         return;
     }
     // Ring depths within ~222 KB: 4 stages (activation tile + decoded weights) if at least 4
-    // raw chunks still fit, else 3; the raw ring takes the rest (up to 12 chunks), in an EVEN
-    // number of slots. The two decoder groups take alternate k steps and wait on a raw slot by
-    // phase parity, which is exact only while the slot's barrier is at most one phase behind.
-    // With an even ring the slot's previous chunk belongs to the same group, which consumed it
-    // before; with an odd one it belongs to the other group, whose copy may still be in flight
-    // (a group runs up to NS + 2 chunks ahead of the MMA), and the parity test then passes on
-    // the wrong phase: a torn chunk is decoded and the ring's arrival counts go wrong.
+    // raw chunks still fit, else 3; the raw ring takes the rest (up to 12 chunks). The two
+    // decoder groups take alternate k steps and wait on a raw slot by phase parity, which is
+    // exact only while the slot's barrier is at most one phase behind, i.e. while the slot's
+    // previous chunk has landed. With an even ring that chunk is the waiting group's own, which
+    // it consumed before. With an odd ring it is the other group's; a group waiting for chunk k
+    // has finished chunk k - 2, whose stage wait means the MMA consumed chunk k - 2 - NS, so
+    // every chunk up to there has landed: an odd ring is exact only from NS + 2 slots on.
+    // Below that the parity test can pass on the wrong phase (a torn chunk decoded, the ring's
+    // arrival counts off by a group), so such a ring gives up one slot.
     const size_t budget = 222 * 1024, stage = 16384 + (size_t)a.bn * 128;
     p.ns = (stage * 4 + 4 * (size_t)cb <= budget) ? 4 : 3;
-    p.nr = (int)std::min<size_t>(12, (budget - stage * p.ns) / cb) & ~1;
+    p.nr = (int)std::min<size_t>(12, (budget - stage * p.ns) / cb);
+    if (p.nr % 2 == 1 && p.nr < p.ns + 2) p.nr -= 1;
     if (p.nr < 2) throw Error(JV_ERR_ARG, "gemm: shared memory budget exceeded");
     p.b_off = 16384 * p.ns;
     p.raw_off = p.b_off + a.bn * 128 * p.ns;

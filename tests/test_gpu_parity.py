@@ -692,6 +692,22 @@ def test_tree_logits_match_the_oracle(small):
                 assert int(np.argmax(got[b][i])) == int(np.argmax(want)), (b, i)
 
 
+def test_long_tree_logits_are_bit_identical_to_each_branch_alone(small):
+    """Full-vocabulary logits at 600 branch tokens: the head GEMM runs three token tiles over the
+    128 row tiles of the 16384-row head, so many CTAs take three work units of four k steps each
+    (the decoder warps then drain the last of several short units). Every branch's logits equal
+    the same branch run alone after the trunk, bit for bit."""
+    trunk = [1] + toks(39, 61)
+    branches = [toks(n, 70 + i) for i, n in enumerate((200, 150, 250))]
+    with ctx(small, cap=2048) as c:
+        got = c.forward_tree_logits(trunk, branches)
+        for b, br in enumerate(branches):
+            c.kv_cache.reset()
+            alone = c.forward_tree_logits(trunk, [br])[0]
+            assert np.asarray(got[b]).tobytes() == np.asarray(alone).tobytes(), b
+            assert np.isfinite(np.asarray(alone)).all()
+
+
 def test_decision_batch_is_bit_identical_to_single_decisions(small):
     """jv_decide_batch: each decision of a batch (trunks of different lengths, branches of odd
     lengths so segments start off multiples of 8, one decision without a trunk) gives exactly the
