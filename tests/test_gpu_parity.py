@@ -603,6 +603,34 @@ def test_gemm_kernels_are_bit_identical(model_factory, qtype):
         assert not diff, (kernel, {k: rel_l2(other[k], ref[k]) for k in diff})
 
 
+def test_debug_sync_gives_the_same_bits(model_factory):
+    """JV_DEBUG_SYNC=1 (a synchronisation after every programmatic-dependent launch, for naming a
+    failing kernel) runs the same kernels without overlap: a full-width tree decision gives the same
+    verdict logits, bit for bit, as the default path in this process."""
+    path = model_factory(WIDE_CFG, "Q8_0", seed=33)
+    trunk = [1] + list(range(3000, 3140))
+    branches = [[5, 6, 7] * 9, [8] * 41, [9, 10, 11]]
+    code = (
+        "import sys, numpy as np; sys.path[:0] = sys.argv[2:];"
+        "import jevstral_b200 as jv;"
+        "m = jv.Model(sys.argv[1], kv_pool_mb=256); c = jv.MinistralModel(m);"
+        f"v = c.forward_tree({trunk!r}, {branches!r}, {VERDICT_ROWS!r});"
+        "np.save(sys.stdout.buffer, np.asarray(v, dtype=np.float32))"
+    )
+    import io
+
+    from conftest import REPO
+
+    env = dict(os.environ, JV_DEBUG_SYNC="1")
+    r = subprocess.run([sys.executable, "-c", code, str(path), str(REPO / "llm-shield_b200"), str(REPO)], env=env,
+                       capture_output=True, timeout=600)
+    assert r.returncode == 0, r.stderr.decode()[-2000:]
+    synced = np.load(io.BytesIO(r.stdout))
+    with jv.Model(path, kv_pool_mb=256) as m, ctx(m) as c:
+        want = np.asarray(c.forward_tree(trunk, branches, VERDICT_ROWS), dtype=np.float32)
+    assert synced.tobytes() == want.tobytes()
+
+
 def test_tensor_core_attention_matches_the_mma_sync_attention(model_factory):
     """The tcgen05 prefill attention against the mma.sync one on the same cache: a 1100-token
     causal trunk (nine 128-key blocks, ragged last block) and then a tree over it, per layer."""
