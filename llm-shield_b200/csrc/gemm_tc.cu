@@ -32,6 +32,7 @@
 // waits (bounded) for its copies in flight, the MMA lane drains its own MMAs, and the CTA
 // frees its TMEM and returns. No cluster launch and no multicast: nothing here reads another
 // GPU's memory.
+#include "gemm_plan.h"
 #include "tc_common.cuh"
 
 namespace jv {
@@ -991,25 +992,16 @@ static void launch_tc_typed(const GemmArgs& a, cudaStream_t s) {
         note_launch();
         return;
     }
-    // Ring depths within ~222 KB: 4 stages (activation tile + decoded weights) if at least 4
-    // raw chunks still fit, else 3; the raw ring takes the rest (up to 12 chunks). The two
-    // decoder groups take alternate k steps and wait on a raw slot by phase parity, which is
-    // exact only while the slot's barrier is at most one phase behind, i.e. while the slot's
-    // previous chunk has landed. With an even ring that chunk is the waiting group's own, which
-    // it consumed before. With an odd ring it is the other group's; a group waiting for chunk k
-    // has finished chunk k - 2, whose stage wait means the MMA consumed chunk k - 2 - NS, so
-    // every chunk up to there has landed: an odd ring is exact only from NS + 2 slots on.
-    // Below that the parity test can pass on the wrong phase (a torn chunk decoded, the ring's
-    // arrival counts off by a group), so such a ring gives up one slot.
-    const size_t budget = 222 * 1024, stage = 16384 + (size_t)a.bn * 128;
-    p.ns = (stage * 4 + 4 * (size_t)cb <= budget) ? 4 : 3;
-    p.nr = (int)std::min<size_t>(12, (budget - stage * p.ns) / cb);
-    if (p.nr % 2 == 1 && p.nr < p.ns + 2) p.nr -= 1;
-    if (p.nr < 2) throw Error(JV_ERR_ARG, "gemm: shared memory budget exceeded");
-    p.b_off = 16384 * p.ns;
-    p.raw_off = p.b_off + a.bn * 128 * p.ns;
-    p.bar_off = (p.raw_off + cb * p.nr + 15) & ~15;
-    size_t smem = (size_t)p.bar_off + 8 * (2 * p.nr + 3 * p.ns + 5) + 16 + 1024;
+    // Ring depths and offsets (gemm_plan.h: the raw ring is even, or at least NS + 2 slots, so
+    // the decoder groups' parity waits are exact).
+    GemmRingPlan plan;
+    if (!gemm_ring_plan(a.bn, cb, &plan)) throw Error(JV_ERR_ARG, "gemm: shared memory budget exceeded");
+    p.ns = plan.ns;
+    p.nr = plan.nr;
+    p.b_off = plan.b_off;
+    p.raw_off = plan.raw_off;
+    p.bar_off = plan.bar_off;
+    const size_t smem = plan.smem;
     JV_CUDA(cudaFuncSetAttribute(k_gemm_tc<TYPE, EPI, CSPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (g_sm_count == 0) {
         int dev = 0;
